@@ -1,0 +1,131 @@
+/*
+ * leankv_tq.h — C ABI of the B200 (sm_100a) TurboQuant KV-cache library
+ * (libleankv_tq.so).  Plain pointers and sizes only.
+ *
+ * Three layers:
+ *
+ *  1. Drop-in replacements for LeanKV's src/ggml-tq.h:145-190 (TQ3_0 / TQ4_0 /
+ *     Hadamard entry points) with the same names, signatures, block layouts
+ *     and results (bit-exact).  Host pointers, synchronous.  Like the
+ *     reference, a k that is not a multiple of 32 (or n of head_dim) is a
+ *     contract violation: the reference asserts, this library prints the
+ *     reason and aborts.  A missing GPU or a CUDA failure aborts the same way.
+ *
+ *  2. Device-pointer API (*_cuda): asynchronous on the given stream
+ *     (a cudaStream_t passed as void*; NULL = legacy default stream), returning
+ *     a tq_status instead of asserting.
+ *
+ *  3. Host-pointer API (*_host): the device-pointer operations wrapped with
+ *     host<->device copies on a library-owned stream; synchronous; thread-safe.
+ *
+ * Thread safety: every entry point may be called concurrently from several
+ * host threads (the reference's row functions are pure and row-parallel
+ * callers rely on that).
+ */
+#ifndef LEANKV_TQ_H
+#define LEANKV_TQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+#define TQ_RESTRICT __restrict__
+extern "C" {
+#else
+#define TQ_RESTRICT restrict
+#endif
+
+#define LEANKV_TQ_ABI_VERSION 1
+
+/* ── block formats: byte-identical to src/ggml-tq.h:125-141 ────────────── */
+
+#ifndef GGML_TQ_H  /* the reference header defines the same layouts */
+#define QK_TQ3 32
+#define QK_TQ4 32
+typedef struct {
+    uint16_t d;          /* fp16 scale (truncating fp32->fp16, src/ggml-tq.h:39-48) */
+    uint8_t  qs[12];     /* 4 groups x 8 codes x 3 bits, src/ggml-tq.c:26-55 */
+} block_tq3_0;           /* 14 bytes */
+typedef struct {
+    uint16_t d;
+    uint8_t  qs[16];     /* byte j = code of elem j | code of elem j+16 << 4 */
+} block_tq4_0;           /* 18 bytes */
+#endif
+
+/* ── 1. drop-in entry points (src/ggml-tq.h) ─────────────────────────────── */
+
+/* replaces quantize_row_tq3_0_ref, src/ggml-tq.c:215-247 */
+void quantize_row_tq3_0_ref(const float * TQ_RESTRICT x, block_tq3_0 * TQ_RESTRICT y, int64_t k);
+/* replaces dequantize_row_tq3_0, src/ggml-tq.c:249-265 */
+void dequantize_row_tq3_0(const block_tq3_0 * TQ_RESTRICT x, float * TQ_RESTRICT y, int64_t k);
+/* replaces quantize_row_tq4_0_ref, src/ggml-tq.c:273-304 */
+void quantize_row_tq4_0_ref(const float * TQ_RESTRICT x, block_tq4_0 * TQ_RESTRICT y, int64_t k);
+/* replaces dequantize_row_tq4_0, src/ggml-tq.c:306-321 */
+void dequantize_row_tq4_0(const block_tq4_0 * TQ_RESTRICT x, float * TQ_RESTRICT y, int64_t k);
+/* replace the ggml from_float wrappers, src/ggml-tq.c:267-269 and :323-325 */
+void quantize_row_tq3_0(const float * TQ_RESTRICT x, void * TQ_RESTRICT y, int64_t k);
+void quantize_row_tq4_0(const float * TQ_RESTRICT x, void * TQ_RESTRICT y, int64_t k);
+/* TQ3_0 with optimal rounding (2 coordinate-descent passes + least-squares
+ * scale); restates scripts/tq3_rounding.py:74-125 (quantize_coord_descent with
+ * n_passes=2), the encoder the LeanKV README.md:17,25 describes for TQ3.  Same
+ * block format, so dequantize_row_tq3_0 reads it unchanged. */
+void quantize_row_tq3_0_opt(const float * TQ_RESTRICT x, block_tq3_0 * TQ_RESTRICT y, int64_t k);
+/* replaces hadamard_transform, src/ggml-tq.c:361-381 (d a power of two) */
+void hadamard_transform(float * x, int d);
+/* replaces hadamard_transform_row, src/ggml-tq.c:398-404 */
+void hadamard_transform_row(float * x, int n, int head_dim);
+
+/* ── status, types ───────────────────────────────────────────────────────── */
+
+typedef enum {
+    TQ_SUCCESS = 0,
+    TQ_ERROR_INVALID_VALUE = 1,   /* bad size, null pointer, bad enum */
+    TQ_ERROR_UNSUPPORTED = 2,     /* e.g. head_dim not a supported power of two */
+    TQ_ERROR_MISALIGNED = 3,      /* pointer alignment below what the kernel needs */
+    TQ_ERROR_CUDA = 4,            /* a CUDA call failed; see tq_last_error_string() */
+    TQ_ERROR_OUT_OF_MEMORY = 5,
+    TQ_ERROR_NO_DEVICE = 6,
+    TQ_ERROR_TIMEOUT = 7          /* a bounded device-side wait ran out */
+} tq_status;
+
+typedef enum { TQ_DTYPE_F32 = 0, TQ_DTYPE_F16 = 1, TQ_DTYPE_BF16 = 2 } tq_dtype;
+typedef enum { TQ_TYPE_TQ3_0 = 3, TQ_TYPE_TQ4_0 = 4 } tq_type;
+
+const char *tq_status_string(tq_status s);
+/* message of the last failure on the calling thread ("" if none) */
+const char *tq_last_error_string(void);
+int tq_abi_version(void);
+
+/* ── 2. device-pointer API ───────────────────────────────────────────────── */
+
+/*
+ * Quantize k elements (k % 32 == 0) of x (dtype x_dtype) into k/32 blocks of
+ * `type` at y.  When fwht_head_dim > 0 every consecutive run of fwht_head_dim
+ * elements is first rotated with the normalized Walsh-Hadamard transform
+ * exactly as hadamard_transform_row does (fused, no intermediate buffer);
+ * fwht_head_dim must be a power of two <= 1024 dividing k.  opt_passes > 0
+ * (TQ3_0 only) applies that many passes of optimal rounding (2 = LeanKV).
+ * Results are bit-identical to running the reference functions on the
+ * float32 conversion of x.  Replaces the fork's f32->TQ copy kernel
+ * (docs/CUDA-RESULTS.md:75).
+ */
+tq_status tq_quantize_cuda(tq_type type, const void *x, tq_dtype x_dtype, void *y, int64_t k,
+                           int fwht_head_dim, int opt_passes, void *stream);
+/* Dequantize k elements (k/32 blocks) into y of dtype y_dtype (f32 is bit-exact
+ * with dequantize_row_tq*_0; f16/bf16 round that value to nearest-even). */
+tq_status tq_dequantize_cuda(tq_type type, const void *x, void *y, tq_dtype y_dtype, int64_t k, void *stream);
+/* In-place hadamard_transform_row on n float32 values (head_dim a power of two <= 32768). */
+tq_status tq_hadamard_cuda(float *x, int64_t n, int head_dim, void *stream);
+
+/* ── 3. host-pointer API (synchronous) ───────────────────────────────────── */
+
+tq_status tq_quantize_host(tq_type type, const void *x, tq_dtype x_dtype, void *y, int64_t k,
+                           int fwht_head_dim, int opt_passes);
+tq_status tq_dequantize_host(tq_type type, const void *x, void *y, tq_dtype y_dtype, int64_t k);
+tq_status tq_hadamard_host(float *x, int64_t n, int head_dim);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LEANKV_TQ_H */

@@ -1,0 +1,352 @@
+// tq_capi.cu — extern "C" entry points of libleankv_tq.so (include/leankv_tq.h).
+//
+// Argument checking turns every contract violation into a tq_status (device
+// and host APIs) or, for the ggml drop-in names, into the abort the
+// reference's assert() would produce.  Nothing here computes on the CPU: a
+// missing device is an error, never a fallback.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "leankv_tq.h"
+#include "tq_capi_internal.h"
+#include "tq_common.cuh"
+#include "tq_kernels.h"
+
+namespace tq {
+
+static thread_local char g_err[512] = "";
+
+tq_status set_error(tq_status s, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return s;
+}
+
+tq_status cuda_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return TQ_SUCCESS;
+    cudaGetLastError();   // clear a sticky launch-configuration error
+    const tq_status s = (e == cudaErrorMemoryAllocation) ? TQ_ERROR_OUT_OF_MEMORY
+                      : (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) ? TQ_ERROR_NO_DEVICE
+                      : TQ_ERROR_CUDA;
+    return set_error(s, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int log2_pow2(int64_t v) {
+    if (v <= 0 || (v & (v - 1)) != 0) return -1;
+    int l = 0;
+    while ((int64_t(1) << l) < v) ++l;
+    return l;
+}
+
+// 1/sqrt(d) with the reference's float expression (src/ggml-tq.c:377)
+float fwht_norm(int d) { return 1.0f / sqrtf((float)d); }
+
+size_t block_bytes(int type) { return type == TQ_TYPE_TQ4_0 ? TQ4_BYTES : TQ3_BYTES; }
+size_t dtype_bytes(int dt) { return dt == TQ_DTYPE_F32 ? 4 : 2; }
+bool dtype_ok(int dt) { return dt == TQ_DTYPE_F32 || dt == TQ_DTYPE_F16 || dt == TQ_DTYPE_BF16; }
+bool type_ok(int t) { return t == TQ_TYPE_TQ3_0 || t == TQ_TYPE_TQ4_0; }
+
+// ── host-API contexts: one stream + grow-only device buffer each ───────────
+struct HostCtx {
+    int dev = -1;
+    cudaStream_t st = nullptr;
+    void* buf = nullptr;
+    size_t cap = 0;
+};
+
+static std::mutex g_pool_mu;
+static std::vector<HostCtx*> g_pool;
+
+static tq_status ctx_acquire(HostCtx** out) {
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return set_error(TQ_ERROR_NO_DEVICE, "no CUDA device available");
+    }
+    int dev = 0;
+    tq_status s = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+    if (s) return s;
+    {
+        std::lock_guard<std::mutex> lk(g_pool_mu);
+        for (size_t i = 0; i < g_pool.size(); ++i) {
+            if (g_pool[i]->dev == dev) {
+                *out = g_pool[i];
+                g_pool.erase(g_pool.begin() + i);
+                return TQ_SUCCESS;
+            }
+        }
+    }
+    HostCtx* c = new HostCtx;
+    c->dev = dev;
+    s = cuda_status(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking), "cudaStreamCreate");
+    if (s) { delete c; return s; }
+    *out = c;
+    return TQ_SUCCESS;
+}
+
+static void ctx_release(HostCtx* c) {
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    g_pool.push_back(c);
+}
+
+static tq_status ctx_reserve(HostCtx* c, size_t bytes) {
+    if (bytes <= c->cap) return TQ_SUCCESS;
+    if (c->buf) {
+        cudaStreamSynchronize(c->st);
+        cudaFree(c->buf);
+        c->buf = nullptr;
+        c->cap = 0;
+    }
+    size_t cap = (bytes + ((1u << 20) - 1)) & ~size_t((1u << 20) - 1);
+    tq_status s = cuda_status(cudaMalloc(&c->buf, cap), "cudaMalloc (host API staging)");
+    if (s) return s;
+    c->cap = cap;
+    return TQ_SUCCESS;
+}
+
+// RAII holder for a host context
+struct CtxGuard {
+    HostCtx* c = nullptr;
+    ~CtxGuard() { if (c) ctx_release(c); }
+};
+
+// chunk size (elements) for host calls: bounded device staging
+static int64_t host_chunk_elems(int64_t k, int64_t unit, size_t bytes_per_elem) {
+    const size_t budget = size_t(512) << 20;   // 512 MiB of staging per call
+    int64_t ch = (int64_t)(budget / (bytes_per_elem ? bytes_per_elem : 1));
+    ch = ch / unit * unit;
+    if (ch < unit) ch = unit;
+    return ch < k ? ch : k;
+}
+
+}  // namespace tq
+
+using namespace tq;
+
+// ── status helpers ───────────────────────────────────────────────────────────
+
+extern "C" const char* tq_status_string(tq_status s) {
+    switch (s) {
+        case TQ_SUCCESS: return "success";
+        case TQ_ERROR_INVALID_VALUE: return "invalid value";
+        case TQ_ERROR_UNSUPPORTED: return "unsupported";
+        case TQ_ERROR_MISALIGNED: return "misaligned pointer";
+        case TQ_ERROR_CUDA: return "CUDA error";
+        case TQ_ERROR_OUT_OF_MEMORY: return "out of device memory";
+        case TQ_ERROR_NO_DEVICE: return "no CUDA device";
+        case TQ_ERROR_TIMEOUT: return "device-side wait timed out";
+    }
+    return "unknown status";
+}
+
+extern "C" const char* tq_last_error_string(void) { return g_err; }
+extern "C" int tq_abi_version(void) { return LEANKV_TQ_ABI_VERSION; }
+
+// ── device-pointer API ────────────────────────────────────────────────────────
+
+extern "C" tq_status tq_quantize_cuda(tq_type type, const void* x, tq_dtype x_dtype, void* y, int64_t k,
+                                      int fwht_head_dim, int opt_passes, void* stream) {
+    g_err[0] = 0;
+    if (!type_ok(type)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown block type %d", (int)type);
+    if (!dtype_ok(x_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown input dtype %d", (int)x_dtype);
+    if (k < 0 || k % QK != 0) return set_error(TQ_ERROR_INVALID_VALUE, "k=%lld is not a multiple of 32", (long long)k);
+    if (k == 0) return TQ_SUCCESS;
+    if (!x || !y) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    if (((uintptr_t)x) % dtype_bytes(x_dtype)) return set_error(TQ_ERROR_MISALIGNED, "x not aligned to its element size");
+    if (opt_passes < 0 || opt_passes > 64) return set_error(TQ_ERROR_INVALID_VALUE, "opt_passes=%d out of [0, 64]", opt_passes);
+    if (opt_passes > 0 && type != TQ_TYPE_TQ3_0) return set_error(TQ_ERROR_UNSUPPORTED, "optimal rounding is defined for TQ3_0 only");
+    int log2_hd = -1;
+    float norm = 1.0f;
+    if (fwht_head_dim != 0) {
+        log2_hd = log2_pow2(fwht_head_dim);
+        if (log2_hd < 0) return set_error(TQ_ERROR_INVALID_VALUE, "fwht_head_dim=%d is not a power of two", fwht_head_dim);
+        if (log2_hd > 10) return set_error(TQ_ERROR_UNSUPPORTED, "fused FWHT supports head_dim <= 1024 (got %d)", fwht_head_dim);
+        if (k % fwht_head_dim) return set_error(TQ_ERROR_INVALID_VALUE, "k is not a multiple of fwht_head_dim");
+        norm = fwht_norm(fwht_head_dim);
+    }
+    return cuda_status(launch_quantize((int)type, (int)x_dtype, x, y, k / QK, log2_hd, norm, opt_passes,
+                                       (cudaStream_t)stream),
+                       "quantize kernel launch");
+}
+
+extern "C" tq_status tq_dequantize_cuda(tq_type type, const void* x, void* y, tq_dtype y_dtype, int64_t k,
+                                        void* stream) {
+    g_err[0] = 0;
+    if (!type_ok(type)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown block type %d", (int)type);
+    if (!dtype_ok(y_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown output dtype %d", (int)y_dtype);
+    if (k < 0 || k % QK != 0) return set_error(TQ_ERROR_INVALID_VALUE, "k=%lld is not a multiple of 32", (long long)k);
+    if (k == 0) return TQ_SUCCESS;
+    if (!x || !y) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    if (((uintptr_t)y) % dtype_bytes(y_dtype)) return set_error(TQ_ERROR_MISALIGNED, "y not aligned to its element size");
+    if (((uintptr_t)x) & 1) return set_error(TQ_ERROR_MISALIGNED, "blocks must be 2-byte aligned (fp16 scale)");
+    return cuda_status(launch_dequantize((int)type, (int)y_dtype, x, y, k / QK, (cudaStream_t)stream),
+                       "dequantize kernel launch");
+}
+
+extern "C" tq_status tq_hadamard_cuda(float* x, int64_t n, int head_dim, void* stream) {
+    g_err[0] = 0;
+    const int l2 = log2_pow2(head_dim);
+    if (l2 < 0) return set_error(TQ_ERROR_INVALID_VALUE, "head_dim=%d is not a power of two", head_dim);
+    if (l2 > 15) return set_error(TQ_ERROR_UNSUPPORTED, "head_dim=%d exceeds 32768", head_dim);
+    if (n < 0 || n % head_dim) return set_error(TQ_ERROR_INVALID_VALUE, "n is not a multiple of head_dim");
+    if (n == 0) return TQ_SUCCESS;
+    if (!x) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    if (((uintptr_t)x) & 3) return set_error(TQ_ERROR_MISALIGNED, "x not 4-byte aligned");
+    const float norm = fwht_norm(head_dim);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (l2 > 10) return cuda_status(launch_fwht_large(x, n / head_dim, l2, norm, st), "fwht kernel launch");
+    const int64_t bulk = n - n % QK;
+    tq_status s = cuda_status(launch_fwht(x, bulk / QK, l2, norm, st), "fwht kernel launch");
+    if (s) return s;
+    return cuda_status(launch_fwht_tail(x + bulk, (int)(n - bulk), l2, norm, st), "fwht tail launch");
+}
+
+// ── host-pointer API ──────────────────────────────────────────────────────────
+
+extern "C" tq_status tq_quantize_host(tq_type type, const void* x, tq_dtype x_dtype, void* y, int64_t k,
+                                      int fwht_head_dim, int opt_passes) {
+    g_err[0] = 0;
+    if (!type_ok(type) || !dtype_ok(x_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "bad type or dtype");
+    if (k < 0 || k % QK) return set_error(TQ_ERROR_INVALID_VALUE, "k=%lld is not a multiple of 32", (long long)k);
+    if (k == 0) return TQ_SUCCESS;
+    if (!x || !y) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    const int64_t unit = fwht_head_dim > QK ? fwht_head_dim : QK;
+    if (fwht_head_dim > 0 && k % fwht_head_dim) return set_error(TQ_ERROR_INVALID_VALUE, "k is not a multiple of fwht_head_dim");
+    CtxGuard g;
+    tq_status s = ctx_acquire(&g.c);
+    if (s) return s;
+    const size_t eb = dtype_bytes(x_dtype), bb = block_bytes(type);
+    const int64_t chunk = host_chunk_elems(k, unit, eb + bb / QK + 1);
+    const size_t in_bytes = (size_t)chunk * eb, out_off = (in_bytes + 255) & ~size_t(255);
+    if ((s = ctx_reserve(g.c, out_off + (size_t)(chunk / QK) * bb))) return s;
+    uint8_t* dbuf = (uint8_t*)g.c->buf;
+    for (int64_t e0 = 0; e0 < k; e0 += chunk) {
+        const int64_t n = k - e0 < chunk ? k - e0 : chunk;
+        if ((s = cuda_status(cudaMemcpyAsync(dbuf, (const uint8_t*)x + e0 * eb, n * eb, cudaMemcpyHostToDevice, g.c->st),
+                             "cudaMemcpyAsync H2D")))
+            return s;
+        if ((s = tq_quantize_cuda(type, dbuf, x_dtype, dbuf + out_off, n, fwht_head_dim, opt_passes, g.c->st))) return s;
+        if ((s = cuda_status(cudaMemcpyAsync((uint8_t*)y + (e0 / QK) * bb, dbuf + out_off, (n / QK) * bb,
+                                             cudaMemcpyDeviceToHost, g.c->st),
+                             "cudaMemcpyAsync D2H")))
+            return s;
+    }
+    return cuda_status(cudaStreamSynchronize(g.c->st), "cudaStreamSynchronize");
+}
+
+extern "C" tq_status tq_dequantize_host(tq_type type, const void* x, void* y, tq_dtype y_dtype, int64_t k) {
+    g_err[0] = 0;
+    if (!type_ok(type) || !dtype_ok(y_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "bad type or dtype");
+    if (k < 0 || k % QK) return set_error(TQ_ERROR_INVALID_VALUE, "k=%lld is not a multiple of 32", (long long)k);
+    if (k == 0) return TQ_SUCCESS;
+    if (!x || !y) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    CtxGuard g;
+    tq_status s = ctx_acquire(&g.c);
+    if (s) return s;
+    const size_t eb = dtype_bytes(y_dtype), bb = block_bytes(type);
+    const int64_t chunk = host_chunk_elems(k, QK * 8, eb + bb / QK + 1);
+    const size_t in_bytes = (size_t)(chunk / QK) * bb, out_off = (in_bytes + 255) & ~size_t(255);
+    if ((s = ctx_reserve(g.c, out_off + (size_t)chunk * eb))) return s;
+    uint8_t* dbuf = (uint8_t*)g.c->buf;
+    for (int64_t e0 = 0; e0 < k; e0 += chunk) {
+        const int64_t n = k - e0 < chunk ? k - e0 : chunk;
+        if ((s = cuda_status(cudaMemcpyAsync(dbuf, (const uint8_t*)x + (e0 / QK) * bb, (n / QK) * bb,
+                                             cudaMemcpyHostToDevice, g.c->st),
+                             "cudaMemcpyAsync H2D")))
+            return s;
+        if ((s = tq_dequantize_cuda(type, dbuf, dbuf + out_off, y_dtype, n, g.c->st))) return s;
+        if ((s = cuda_status(cudaMemcpyAsync((uint8_t*)y + e0 * eb, dbuf + out_off, n * eb, cudaMemcpyDeviceToHost,
+                                             g.c->st),
+                             "cudaMemcpyAsync D2H")))
+            return s;
+    }
+    return cuda_status(cudaStreamSynchronize(g.c->st), "cudaStreamSynchronize");
+}
+
+extern "C" tq_status tq_hadamard_host(float* x, int64_t n, int head_dim) {
+    g_err[0] = 0;
+    if (log2_pow2(head_dim) < 0) return set_error(TQ_ERROR_INVALID_VALUE, "head_dim=%d is not a power of two", head_dim);
+    if (n < 0 || n % head_dim) return set_error(TQ_ERROR_INVALID_VALUE, "n is not a multiple of head_dim");
+    if (n == 0) return TQ_SUCCESS;
+    if (!x) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    CtxGuard g;
+    tq_status s = ctx_acquire(&g.c);
+    if (s) return s;
+    const int64_t unit = head_dim > QK ? head_dim : QK;
+    int64_t chunk = host_chunk_elems(n, unit, 4);
+    if (chunk < n && chunk % head_dim) chunk -= chunk % head_dim;
+    if ((s = ctx_reserve(g.c, (size_t)chunk * 4))) return s;
+    float* d = (float*)g.c->buf;
+    for (int64_t e0 = 0; e0 < n; e0 += chunk) {
+        const int64_t m = n - e0 < chunk ? n - e0 : chunk;
+        if ((s = cuda_status(cudaMemcpyAsync(d, x + e0, m * 4, cudaMemcpyHostToDevice, g.c->st), "cudaMemcpyAsync H2D")))
+            return s;
+        if ((s = tq_hadamard_cuda(d, m, head_dim, g.c->st))) return s;
+        if ((s = cuda_status(cudaMemcpyAsync(x + e0, d, m * 4, cudaMemcpyDeviceToHost, g.c->st), "cudaMemcpyAsync D2H")))
+            return s;
+    }
+    return cuda_status(cudaStreamSynchronize(g.c->st), "cudaStreamSynchronize");
+}
+
+// ── ggml drop-in names (src/ggml-tq.h:145-190) ───────────────────────────────
+
+[[noreturn]] static void die(const char* fn, const char* why) {
+    fprintf(stderr, "leankv_tq: %s: %s\n", fn, why);
+    fflush(stderr);
+    abort();
+}
+
+static void check_k(const char* fn, int64_t k) {
+    if (k % QK != 0) die(fn, "k % 32 != 0 (the reference asserts k % QK == 0)");
+}
+
+extern "C" void quantize_row_tq3_0_ref(const float* TQ_RESTRICT x, block_tq3_0* TQ_RESTRICT y, int64_t k) {
+    check_k(__func__, k);
+    if (tq_quantize_host(TQ_TYPE_TQ3_0, x, TQ_DTYPE_F32, y, k, 0, 0) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void quantize_row_tq4_0_ref(const float* TQ_RESTRICT x, block_tq4_0* TQ_RESTRICT y, int64_t k) {
+    check_k(__func__, k);
+    if (tq_quantize_host(TQ_TYPE_TQ4_0, x, TQ_DTYPE_F32, y, k, 0, 0) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void quantize_row_tq3_0(const float* TQ_RESTRICT x, void* TQ_RESTRICT y, int64_t k) {
+    quantize_row_tq3_0_ref(x, (block_tq3_0*)y, k);
+}
+
+extern "C" void quantize_row_tq4_0(const float* TQ_RESTRICT x, void* TQ_RESTRICT y, int64_t k) {
+    quantize_row_tq4_0_ref(x, (block_tq4_0*)y, k);
+}
+
+extern "C" void quantize_row_tq3_0_opt(const float* TQ_RESTRICT x, block_tq3_0* TQ_RESTRICT y, int64_t k) {
+    check_k(__func__, k);
+    if (tq_quantize_host(TQ_TYPE_TQ3_0, x, TQ_DTYPE_F32, y, k, 0, 2) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void dequantize_row_tq3_0(const block_tq3_0* TQ_RESTRICT x, float* TQ_RESTRICT y, int64_t k) {
+    check_k(__func__, k);
+    if (tq_dequantize_host(TQ_TYPE_TQ3_0, x, y, TQ_DTYPE_F32, k) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void dequantize_row_tq4_0(const block_tq4_0* TQ_RESTRICT x, float* TQ_RESTRICT y, int64_t k) {
+    check_k(__func__, k);
+    if (tq_dequantize_host(TQ_TYPE_TQ4_0, x, y, TQ_DTYPE_F32, k) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void hadamard_transform(float* x, int d) {
+    if (d <= 0 || (d & (d - 1)) != 0) die(__func__, "d must be a power of two (the reference asserts this)");
+    if (tq_hadamard_host(x, d, d) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void hadamard_transform_row(float* x, int n, int head_dim) {
+    if (head_dim <= 0 || n % head_dim != 0) die(__func__, "n % head_dim != 0 (the reference asserts this)");
+    if ((head_dim & (head_dim - 1)) != 0) die(__func__, "head_dim must be a power of two (the reference asserts this)");
+    if (tq_hadamard_host(x, n, head_dim) != TQ_SUCCESS) die(__func__, g_err);
+}

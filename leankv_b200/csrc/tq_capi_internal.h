@@ -1,0 +1,21 @@
+// tq_capi_internal.h — helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "leankv_tq.h"
+
+namespace tq {
+
+tq_status set_error(tq_status s, const char* fmt, ...);
+tq_status cuda_status(cudaError_t e, const char* what);
+int log2_pow2(int64_t v);
+float fwht_norm(int d);
+size_t block_bytes(int type);
+size_t dtype_bytes(int dt);
+bool dtype_ok(int dt);
+bool type_ok(int t);
+
+}  // namespace tq

@@ -1,0 +1,572 @@
+// tq_codec.cu — fused Walsh-Hadamard + TurboQuant block codecs for sm_100a.
+//
+// Kernels
+//   quantize_kernel<QT, IN, MODE>  [FWHT per head] + TQ3_0 / TQ4_0 quantize
+//                                  (src/ggml-tq.c:215-247, :273-304 after
+//                                  hadamard_transform_row, :361-404), with the
+//                                  TQ3 optimal-rounding refinement
+//                                  (scripts/tq3_rounding.py:74-125) as MODE
+//   fwht_kernel                    hadamard_transform_row in place on fp32
+//   dequantize_kernel<QT, OUT>     dequantize_row_tq{3,4}_0 (:249-265, :306-321)
+//
+// Layout of work (quantize / FWHT): one thread owns one 32-element block, so
+// a head of D elements is D/32 consecutive lanes.  A CTA of 128 threads moves
+// a tile of 128 blocks: coalesced 16-byte global loads into an XOR-swizzled
+// shared tile (conflict-free both for the row-major fill and for the
+// per-thread row reads), FWHT stages h = 1..16 in registers, stages h >= 32 by
+// warp shuffles between the lanes of a head, then amax / scale / nearest
+// level / packing in registers, and a byte-exact staging of the 18- or 14-byte
+// blocks in shared memory so the global stores are again 16-byte coalesced.
+//
+// Bit-exactness with the reference: the butterfly stages run in the
+// reference's order (h ascending) with the same (a + b, a - b) operations; the
+// 1/sqrt(D) factor is computed on the host with the reference's expression;
+// the reciprocal is the IEEE division 1.0f / amax; the build uses no fast-math
+// so every fp32 operation is correctly rounded and denormals are kept.
+#include <type_traits>
+
+#include "tq_common.cuh"
+#include "tq_kernels.h"
+
+namespace tq {
+
+constexpr int CODEC_THREADS = 128;   // blocks per tile
+
+// ── shared-memory tile addressing ───────────────────────────────────────────
+// A tile row is one 32-element block: 128 B (fp32) or 64 B (16-bit input).
+// Chunk q (16 B) of row r is stored at chunk position q ^ swz(r) so that the
+// 8 lanes of a 128-bit shared-memory phase hit 8 distinct bank groups both
+// when a warp fills consecutive chunks and when each lane reads its own row.
+template <int ROW_BYTES>
+__device__ __forceinline__ int tile_chunk_addr(int r, int q) {
+    constexpr int CPR = ROW_BYTES / 16;               // chunks per row: 8 or 4
+    const int swz = CPR == 8 ? (r & 7) : ((r >> 1) & 3);
+    return r * ROW_BYTES + ((q ^ swz) << 4);
+}
+
+// cooperative tile load: rows [0, nrows) of 32 elements each
+template <typename IN>
+__device__ __forceinline__ void load_tile(uint8_t* __restrict__ smem, const IN* __restrict__ src,
+                                          int nrows, bool vec_ok) {
+    constexpr int EB = ElemBits<IN>::bytes;
+    constexpr int ROW_BYTES = QK * EB;
+    constexpr int CPR = ROW_BYTES / 16;
+    if (vec_ok) {
+        const int4* s4 = reinterpret_cast<const int4*>(src);
+        for (int c = threadIdx.x; c < nrows * CPR; c += CODEC_THREADS) {
+            const int4 v = __ldg(s4 + c);
+            *reinterpret_cast<int4*>(smem + tile_chunk_addr<ROW_BYTES>(c / CPR, c % CPR)) = v;
+        }
+    } else {
+        // element-wise fallback for inputs that are not 16-byte aligned
+        const uint8_t* sb = reinterpret_cast<const uint8_t*>(src);
+        for (int e = threadIdx.x; e < nrows * QK; e += CODEC_THREADS) {
+            const int r = e / QK, c = e % QK;
+            const int byte = c * EB;
+            uint8_t* dst = smem + tile_chunk_addr<ROW_BYTES>(r, byte >> 4) + (byte & 15);
+            if (EB == 4) {
+                uint32_t w;
+                memcpy(&w, sb + (size_t)e * 4, 4);
+                *reinterpret_cast<uint32_t*>(dst) = w;
+            } else {
+                uint16_t w;
+                memcpy(&w, sb + (size_t)e * 2, 2);
+                *reinterpret_cast<uint16_t*>(dst) = w;
+            }
+        }
+    }
+}
+
+// thread-private read of row r as 32 floats (exact conversion from 16-bit)
+template <typename IN>
+__device__ __forceinline__ void read_row(const uint8_t* __restrict__ smem, int r, float (&v)[QK]) {
+    constexpr int EB = ElemBits<IN>::bytes;
+    constexpr int ROW_BYTES = QK * EB;
+    constexpr int CPR = ROW_BYTES / 16;
+#pragma unroll
+    for (int q = 0; q < CPR; ++q) {
+        const uint4 w = *reinterpret_cast<const uint4*>(smem + tile_chunk_addr<ROW_BYTES>(r, q));
+        if constexpr (EB == 4) {
+            v[4 * q + 0] = __uint_as_float(w.x);
+            v[4 * q + 1] = __uint_as_float(w.y);
+            v[4 * q + 2] = __uint_as_float(w.z);
+            v[4 * q + 3] = __uint_as_float(w.w);
+        } else {
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t lo = ws[i] & 0xFFFFu, hi = ws[i] >> 16;
+                if constexpr (std::is_same<IN, __nv_bfloat16>::value) {
+                    v[8 * q + 2 * i] = bf16_bits_to_float(lo);
+                    v[8 * q + 2 * i + 1] = bf16_bits_to_float(hi);
+                } else {
+                    v[8 * q + 2 * i] = f16_bits_to_float(lo);
+                    v[8 * q + 2 * i + 1] = f16_bits_to_float(hi);
+                }
+            }
+        }
+    }
+}
+
+// ── Walsh-Hadamard transform of one head spread over D/32 lanes ─────────────
+// Stage h combines elements j and j+h as (x[j] + x[j+h], x[j] - x[j+h]),
+// h = 1, 2, 4, ... (src/ggml-tq.c:365-374), then scales by norm.
+__device__ __forceinline__ void fwht_block(float (&v)[QK], int log2_hd, float norm) {
+#pragma unroll
+    for (int s = 0; s < 5; ++s) {
+        if (s < log2_hd) {
+            const int h = 1 << s;
+#pragma unroll
+            for (int j = 0; j < QK; ++j) {
+                if (j & h) continue;
+                const float a = v[j], b = v[j + h];
+                v[j] = a + b;
+                v[j + h] = a - b;
+            }
+        }
+    }
+    for (int s = 5; s < log2_hd; ++s) {
+        const int lane_bit = 1 << (s - 5);
+        const bool upper = (threadIdx.x & lane_bit) != 0;
+#pragma unroll
+        for (int j = 0; j < QK; ++j) {
+            const float p = __shfl_xor_sync(0xffffffffu, v[j], lane_bit);
+            // lower element: self + partner; upper element: partner - self
+            v[j] = upper ? (p - v[j]) : (v[j] + p);
+        }
+    }
+    if (log2_hd >= 0) {
+#pragma unroll
+        for (int j = 0; j < QK; ++j) v[j] = __fmul_rn(v[j], norm);
+    }
+}
+
+// ── block staging (byte-exact reference layout) ──────────────────────────────
+// Write `nbytes` (18 or 14) bytes made of the fp16 scale and the packed codes
+// words[] (little endian) at smem + off, where off is even.
+template <int NB>
+__device__ __forceinline__ void stage_block(uint8_t* __restrict__ smem, int off, uint16_t d,
+                                            const uint32_t (&w)[NB]) {
+    // byte stream: d_lo d_hi q0 q1 ... ; off % 4 is 0 or 2
+    if ((off & 2) == 0) {
+        // [d | q0 q1] [q2..q5] ...
+        *reinterpret_cast<uint32_t*>(smem + off) = (uint32_t)d | (w[0] << 16);
+#pragma unroll
+        for (int i = 1; i < NB; ++i)
+            *reinterpret_cast<uint32_t*>(smem + off + 4 * i) = (w[i - 1] >> 16) | (w[i] << 16);
+        *reinterpret_cast<uint16_t*>(smem + off + 4 * NB) = (uint16_t)(w[NB - 1] >> 16);
+    } else {
+        *reinterpret_cast<uint16_t*>(smem + off) = d;
+#pragma unroll
+        for (int i = 0; i < NB; ++i) *reinterpret_cast<uint32_t*>(smem + off + 2 + 4 * i) = w[i];
+    }
+}
+
+// cooperative copy of nbytes from shared staging to global
+__device__ __forceinline__ void store_staged(uint8_t* __restrict__ dst, const uint8_t* __restrict__ smem,
+                                             int nbytes, bool vec_ok) {
+    if (vec_ok && (nbytes & 15) == 0) {
+        int4* d4 = reinterpret_cast<int4*>(dst);
+        const int4* s4 = reinterpret_cast<const int4*>(smem);
+        for (int c = threadIdx.x; c < nbytes / 16; c += CODEC_THREADS) d4[c] = s4[c];
+    } else {
+        for (int b = threadIdx.x; b < nbytes; b += CODEC_THREADS) dst[b] = smem[b];
+    }
+}
+
+// ── TQ3 optimal rounding (scripts/tq3_rounding.py:74-125) ───────────────────
+// Coordinate descent over adjacent levels with a least-squares scale.  For an
+// assignment with Sxl = sum x*L and Sll = sum L^2 the least-squares block MSE
+// is (sum x^2 - Sxl^2 / Sll) / 32, so "new_mse < best_mse" is exactly
+// Sxl'^2 * Sll > Sxl^2 * Sll'.  Sums are float64 over the float64 levels of the
+// Python prototype and are updated incrementally per accepted move.
+struct OptEntry { double lvl, dl_dn, dll_dn, dl_up, dll_up; };
+
+__device__ __forceinline__ double tq3_opt_refine(const float (&v)[QK], int (&idx)[QK], int n_passes,
+                                                 const OptEntry* __restrict__ tbl) {
+    double A = 0.0, Cx = 0.0;
+#pragma unroll
+    for (int j = 0; j < QK; ++j) {
+        const double l = tbl[idx[j]].lvl;
+        A += l * l;
+        Cx += (double)v[j] * l;
+    }
+    double E = Cx * Cx;
+    for (int pass = 0; pass < n_passes; ++pass) {
+        bool improved = false;
+#pragma unroll
+        for (int j = 0; j < QK; ++j) {
+            const int i = idx[j];
+            const OptEntry e = tbl[i];
+            const double xd = (double)v[j];
+            // lower neighbour first, then upper (first strict improvement wins)
+            const double Cd = fma(xd, e.dl_dn, Cx), Ad = A + e.dll_dn;
+            const double Cu = fma(xd, e.dl_up, Cx), Au = A + e.dll_up;
+            const bool acc_dn = i > 0 && Cd * Cd * A > E * Ad;
+            const bool acc_up = !acc_dn && i < 7 && Cu * Cu * A > E * Au;
+            if (acc_dn) { Cx = Cd; A = Ad; E = Cd * Cd; idx[j] = i - 1; improved = true; }
+            if (acc_up) { Cx = Cu; A = Au; E = Cu * Cu; idx[j] = i + 1; improved = true; }
+        }
+        if (!improved) break;
+    }
+    return A == 0.0 ? 0.0 : Cx / A;
+}
+
+// ── quantize ────────────────────────────────────────────────────────────────
+// MODE 0: nearest level (reference).  MODE 1: TQ3 optimal rounding.
+template <int QT, typename IN, int MODE>
+__global__ void __launch_bounds__(CODEC_THREADS)
+quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nblocks,
+                int log2_hd, float norm, int n_passes, int x_vec, int y_vec) {
+    constexpr int EB = ElemBits<IN>::bytes;
+    constexpr int ROW_BYTES = QK * EB;
+    constexpr int BB = QT == 4 ? TQ4_BYTES : TQ3_BYTES;
+    __shared__ __align__(16) uint8_t s_in[CODEC_THREADS * ROW_BYTES];
+    __shared__ __align__(16) uint8_t s_out[CODEC_THREADS * BB];
+    __shared__ OptEntry s_tbl[8];
+
+    if (MODE == 1 && threadIdx.x < 8) {
+        const int i = threadIdx.x;
+        const double L = tq3_level_f64(i);
+        const double Ld = i > 0 ? tq3_level_f64(i - 1) : L;
+        const double Lu = i < 7 ? tq3_level_f64(i + 1) : L;
+        s_tbl[i] = OptEntry{L, Ld - L, Ld * Ld - L * L, Lu - L, Lu * Lu - L * L};
+    }
+
+    const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int64_t b0 = tile * CODEC_THREADS;
+        const int nrows = (int)(nblocks - b0 < CODEC_THREADS ? nblocks - b0 : CODEC_THREADS);
+        __syncthreads();   // previous tile fully consumed (s_in, s_out reusable)
+        load_tile<IN>(s_in, x + b0 * QK, nrows, x_vec != 0);
+        __syncthreads();
+
+        float v[QK];
+        read_row<IN>(s_in, threadIdx.x < nrows ? threadIdx.x : 0, v);
+        fwht_block(v, log2_hd, norm);
+
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < QK; ++j) amax = fmaxf(amax, fabsf(v[j]));   // NaN never wins
+        const float inv = amax > 0.0f ? 1.0f / amax : 0.0f;
+
+        uint16_t dh;
+        if constexpr (QT == 4) {
+            dh = half_trunc(amax);
+            uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int lo = tq4_nearest(__fmul_rn(v[j], inv));
+                const int hi = tq4_nearest(__fmul_rn(v[j + 16], inv));
+                w[j >> 2] |= (uint32_t)(lo | (hi << 4)) << (8 * (j & 3));
+            }
+            if (threadIdx.x < nrows) stage_block<4>(s_out, threadIdx.x * BB, dh, w);
+        } else {
+            int idx[QK];
+#pragma unroll
+            for (int j = 0; j < QK; ++j) idx[j] = tq3_nearest(__fmul_rn(v[j], inv));
+            if constexpr (MODE == 1) {
+                if (amax > 0.0f) {
+                    const double d = tq3_opt_refine(v, idx, n_passes, s_tbl);
+                    float df = (float)d;
+                    if (df != df) df = fabsf(df);
+                    dh = half_trunc(df);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < QK; ++j) idx[j] = 0;
+                    dh = 0;
+                }
+            } else {
+                dh = half_trunc(amax);
+            }
+            uint32_t g[4];
+#pragma unroll
+            for (int gi = 0; gi < 4; ++gi) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) word |= (uint32_t)idx[8 * gi + i] << (3 * i);
+                g[gi] = word;   // 24 bits
+            }
+            // 12 code bytes as 3 little-endian words
+            const uint32_t w[3] = {g[0] | (g[1] << 24), (g[1] >> 8) | (g[2] << 16), (g[2] >> 16) | (g[3] << 8)};
+            if (threadIdx.x < nrows) stage_block<3>(s_out, threadIdx.x * BB, dh, w);
+        }
+        __syncthreads();
+        store_staged(y + b0 * BB, s_out, nrows * BB, y_vec != 0);
+    }
+}
+
+// ── in-place FWHT (hadamard_transform_row) on fp32 ──────────────────────────
+__global__ void __launch_bounds__(CODEC_THREADS)
+fwht_kernel(float* __restrict__ x, int64_t nblocks, int log2_hd, float norm, int x_vec) {
+    constexpr int ROW_BYTES = QK * 4;
+    __shared__ __align__(16) uint8_t s_in[CODEC_THREADS * ROW_BYTES];
+    const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int64_t b0 = tile * CODEC_THREADS;
+        const int nrows = (int)(nblocks - b0 < CODEC_THREADS ? nblocks - b0 : CODEC_THREADS);
+        __syncthreads();
+        load_tile<float>(s_in, x + b0 * QK, nrows, x_vec != 0);
+        __syncthreads();
+        float v[QK];
+        const int r = threadIdx.x < nrows ? threadIdx.x : 0;
+        read_row<float>(s_in, r, v);
+        fwht_block(v, log2_hd, norm);
+        __syncthreads();
+        if (threadIdx.x < nrows) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                *reinterpret_cast<float4*>(s_in + tile_chunk_addr<ROW_BYTES>(r, q)) =
+                    make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+        __syncthreads();
+        float* dst = x + b0 * QK;
+        if (x_vec) {
+            for (int c = threadIdx.x; c < nrows * 8; c += CODEC_THREADS)
+                reinterpret_cast<int4*>(dst)[c] =
+                    *reinterpret_cast<const int4*>(s_in + tile_chunk_addr<ROW_BYTES>(c / 8, c % 8));
+        } else {
+            for (int e = threadIdx.x; e < nrows * QK; e += CODEC_THREADS) {
+                const int rr = e / QK, cc = e % QK;
+                dst[e] = *reinterpret_cast<const float*>(s_in + tile_chunk_addr<ROW_BYTES>(rr, cc >> 2) + 4 * (cc & 3));
+            }
+        }
+    }
+}
+
+// ── dequantize ──────────────────────────────────────────────────────────────
+// 8 lanes per block, each producing 4 consecutive outputs (one 16-byte store
+// for fp32), so a warp writes 4 whole blocks = 512 contiguous bytes.
+constexpr int DQ_THREADS = 256;
+constexpr int DQ_TILE = 256;   // blocks per tile
+
+template <typename OUT> __device__ __forceinline__ OUT from_float(float f);
+template <> __device__ __forceinline__ float from_float<float>(float f) { return f; }
+template <> __device__ __forceinline__ __half from_float<__half>(float f) { return __float2half_rn(f); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float f) { return __float2bfloat16_rn(f); }
+
+template <typename OUT>
+__device__ __forceinline__ void store4(OUT* dst, float a, float b, float c, float d);
+template <> __device__ __forceinline__ void store4<float>(float* dst, float a, float b, float c, float d) {
+    *reinterpret_cast<float4*>(dst) = make_float4(a, b, c, d);
+}
+template <> __device__ __forceinline__ void store4<__half>(__half* dst, float a, float b, float c, float d) {
+    const __half2 lo = __floats2half2_rn(a, b), hi = __floats2half2_rn(c, d);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&lo);
+    u.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(dst) = u;
+}
+template <> __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* dst, float a, float b, float c, float d) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&lo);
+    u.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(dst) = u;
+}
+
+template <int QT, typename OUT>
+__global__ void __launch_bounds__(DQ_THREADS)
+dequantize_kernel(const uint8_t* __restrict__ xq, OUT* __restrict__ y, int64_t nblocks, int x_vec, int y_vec) {
+    constexpr int BB = QT == 4 ? TQ4_BYTES : TQ3_BYTES;
+    constexpr int NL = QT == 4 ? 16 : 8;
+    __shared__ __align__(16) uint8_t s_in[DQ_TILE * BB];
+    __shared__ float s_lvl[NL];
+    if (threadIdx.x < NL) s_lvl[threadIdx.x] = QT == 4 ? tq4_level(threadIdx.x) : tq3_level(threadIdx.x);
+
+    const int64_t ntiles = (nblocks + DQ_TILE - 1) / DQ_TILE;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int64_t b0 = tile * DQ_TILE;
+        const int nrows = (int)(nblocks - b0 < DQ_TILE ? nblocks - b0 : DQ_TILE);
+        const int nbytes = nrows * BB;
+        __syncthreads();
+        const uint8_t* src = xq + b0 * BB;
+        if (x_vec && (nbytes & 15) == 0) {
+            for (int c = threadIdx.x; c < nbytes / 16; c += DQ_THREADS)
+                reinterpret_cast<int4*>(s_in)[c] = __ldg(reinterpret_cast<const int4*>(src) + c);
+        } else {
+            for (int b = threadIdx.x; b < nbytes; b += DQ_THREADS) s_in[b] = src[b];
+        }
+        __syncthreads();
+        const int part = threadIdx.x & 7;
+        for (int r = threadIdx.x >> 3; r < nrows; r += DQ_THREADS / 8) {
+            const uint8_t* blk = s_in + r * BB;
+            const float d = half_decode((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+            uint32_t c0, c1, c2, c3;
+            if constexpr (QT == 4) {
+                // elements 4p..4p+3: low nibbles of bytes 4p.. (p < 4) or high nibbles of 4(p-4)..
+                const int q = 2 + 4 * (part & 3);
+                const uint32_t w = (uint32_t)blk[q] | ((uint32_t)blk[q + 1] << 8) |
+                                   ((uint32_t)blk[q + 2] << 16) | ((uint32_t)blk[q + 3] << 24);
+                const uint32_t nib = part < 4 ? (w & 0x0F0F0F0Fu) : ((w >> 4) & 0x0F0F0F0Fu);
+                c0 = nib & 15u; c1 = (nib >> 8) & 15u; c2 = (nib >> 16) & 15u; c3 = nib >> 24;
+            } else {
+                // group g = part/2 (3 bytes, 8 codes), half = part%2 -> codes 4*half..+3
+                const int q = 2 + 3 * (part >> 1);
+                const uint32_t w = (uint32_t)blk[q] | ((uint32_t)blk[q + 1] << 8) | ((uint32_t)blk[q + 2] << 16);
+                const uint32_t s = w >> (12 * (part & 1));
+                c0 = s & 7u; c1 = (s >> 3) & 7u; c2 = (s >> 6) & 7u; c3 = (s >> 9) & 7u;
+            }
+            const float o0 = __fmul_rn(s_lvl[c0], d), o1 = __fmul_rn(s_lvl[c1], d);
+            const float o2 = __fmul_rn(s_lvl[c2], d), o3 = __fmul_rn(s_lvl[c3], d);
+            OUT* dst = y + (b0 + r) * QK + 4 * part;
+            if (y_vec) {
+                store4<OUT>(dst, o0, o1, o2, o3);
+            } else {
+                dst[0] = from_float<OUT>(o0); dst[1] = from_float<OUT>(o1);
+                dst[2] = from_float<OUT>(o2); dst[3] = from_float<OUT>(o3);
+            }
+        }
+    }
+}
+
+// ── launchers ───────────────────────────────────────────────────────────────
+
+int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (cached[dev] == 0) {
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+        cached[dev] = sms;
+    }
+    return cached[dev];
+}
+
+static int codec_grid(int64_t ntiles, int per_sm) {
+    const int sms = sm_count();
+    const int64_t cap = (int64_t)sms * per_sm;
+    return (int)(ntiles < cap ? (ntiles > 0 ? ntiles : 1) : cap);
+}
+
+template <int QT, typename IN>
+static cudaError_t launch_quant_t(const void* x, void* y, int64_t nblocks, int log2_hd, float norm,
+                                  int n_passes, cudaStream_t st) {
+    const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
+    const int grid = codec_grid(ntiles, 16);
+    const int xv = ((uintptr_t)x & 15) == 0, yv = ((uintptr_t)y & 15) == 0;
+    if (QT == 3 && n_passes > 0)
+        quantize_kernel<QT, IN, 1><<<grid, CODEC_THREADS, 0, st>>>((const IN*)x, (uint8_t*)y, nblocks, log2_hd,
+                                                                   norm, n_passes, xv, yv);
+    else
+        quantize_kernel<QT, IN, 0><<<grid, CODEC_THREADS, 0, st>>>((const IN*)x, (uint8_t*)y, nblocks, log2_hd,
+                                                                   norm, 0, xv, yv);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize(int qtype, int in_dtype, const void* x, void* y, int64_t nblocks, int log2_hd,
+                            float norm, int n_passes, cudaStream_t st) {
+    if (nblocks <= 0) return cudaSuccess;
+    if (qtype == 4) {
+        switch (in_dtype) {
+            case DT_F32: return launch_quant_t<4, float>(x, y, nblocks, log2_hd, norm, 0, st);
+            case DT_F16: return launch_quant_t<4, __half>(x, y, nblocks, log2_hd, norm, 0, st);
+            default: return launch_quant_t<4, __nv_bfloat16>(x, y, nblocks, log2_hd, norm, 0, st);
+        }
+    }
+    switch (in_dtype) {
+        case DT_F32: return launch_quant_t<3, float>(x, y, nblocks, log2_hd, norm, n_passes, st);
+        case DT_F16: return launch_quant_t<3, __half>(x, y, nblocks, log2_hd, norm, n_passes, st);
+        default: return launch_quant_t<3, __nv_bfloat16>(x, y, nblocks, log2_hd, norm, n_passes, st);
+    }
+}
+
+cudaError_t launch_fwht(float* x, int64_t nblocks, int log2_hd, float norm, cudaStream_t st) {
+    if (nblocks <= 0) return cudaSuccess;
+    const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
+    fwht_kernel<<<codec_grid(ntiles, 16), CODEC_THREADS, 0, st>>>(x, nblocks, log2_hd, norm,
+                                                                  ((uintptr_t)x & 15) == 0);
+    return cudaGetLastError();
+}
+
+template <int QT, typename OUT>
+static cudaError_t launch_dq_t(const void* x, void* y, int64_t nblocks, cudaStream_t st) {
+    const int64_t ntiles = (nblocks + DQ_TILE - 1) / DQ_TILE;
+    dequantize_kernel<QT, OUT><<<codec_grid(ntiles, 8), DQ_THREADS, 0, st>>>(
+        (const uint8_t*)x, (OUT*)y, nblocks, ((uintptr_t)x & 15) == 0,
+        ((uintptr_t)y & (sizeof(OUT) == 4 ? 15 : 7)) == 0);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize(int qtype, int out_dtype, const void* x, void* y, int64_t nblocks, cudaStream_t st) {
+    if (nblocks <= 0) return cudaSuccess;
+    if (qtype == 4) {
+        switch (out_dtype) {
+            case DT_F32: return launch_dq_t<4, float>(x, y, nblocks, st);
+            case DT_F16: return launch_dq_t<4, __half>(x, y, nblocks, st);
+            default: return launch_dq_t<4, __nv_bfloat16>(x, y, nblocks, st);
+        }
+    }
+    switch (out_dtype) {
+        case DT_F32: return launch_dq_t<3, float>(x, y, nblocks, st);
+        case DT_F16: return launch_dq_t<3, __half>(x, y, nblocks, st);
+        default: return launch_dq_t<3, __nv_bfloat16>(x, y, nblocks, st);
+    }
+}
+
+}  // namespace tq
+
+namespace tq {
+
+// ── FWHT for rows that do not fill whole 32-element tiles or exceed 1024 ────
+
+__global__ void fwht_tail_kernel(float* __restrict__ x, int n, int log2_hd, float norm) {
+    // one thread; n < 32 and heads of 2^log2_hd < 32 elements (same stage order)
+    const int d = 1 << log2_hd;
+    for (int base = 0; base + d <= n; base += d) {
+        for (int h = 1; h < d; h <<= 1)
+            for (int j = 0; j < d; ++j) {
+                if (j & h) continue;
+                const float a = x[base + j], b = x[base + j + h];
+                x[base + j] = a + b;
+                x[base + j + h] = a - b;
+            }
+        for (int j = 0; j < d; ++j) x[base + j] = __fmul_rn(x[base + j], norm);
+    }
+}
+
+constexpr int FWHT_LARGE_THREADS = 512;
+
+__global__ void __launch_bounds__(FWHT_LARGE_THREADS)
+fwht_large_kernel(float* __restrict__ x, int log2_hd, float norm) {
+    extern __shared__ float srow[];
+    const int d = 1 << log2_hd;
+    float* row = x + (int64_t)blockIdx.x * d;
+    for (int i = threadIdx.x; i < d; i += FWHT_LARGE_THREADS) srow[i] = row[i];
+    __syncthreads();
+    for (int s = 0; s < log2_hd; ++s) {
+        const int h = 1 << s;
+        for (int p = threadIdx.x; p < d / 2; p += FWHT_LARGE_THREADS) {
+            const int j = ((p >> s) << (s + 1)) | (p & (h - 1));   // p-th pair of stage h
+            const float a = srow[j], b = srow[j + h];
+            srow[j] = a + b;
+            srow[j + h] = a - b;
+        }
+        __syncthreads();
+    }
+    for (int i = threadIdx.x; i < d; i += FWHT_LARGE_THREADS) row[i] = __fmul_rn(srow[i], norm);
+}
+
+cudaError_t launch_fwht_tail(float* x, int n, int log2_hd, float norm, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    fwht_tail_kernel<<<1, 1, 0, st>>>(x, n, log2_hd, norm);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fwht_large(float* x, int64_t nrows, int log2_hd, float norm, cudaStream_t st) {
+    if (nrows <= 0) return cudaSuccess;
+    const size_t smem = sizeof(float) << log2_hd;
+    cudaError_t e = cudaFuncSetAttribute(fwht_large_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    for (int64_t r0 = 0; r0 < nrows; r0 += 65535) {
+        const int64_t nr = nrows - r0 < 65535 ? nrows - r0 : 65535;
+        fwht_large_kernel<<<(unsigned)nr, FWHT_LARGE_THREADS, smem, st>>>(x + (r0 << log2_hd), log2_hd, norm);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace tq

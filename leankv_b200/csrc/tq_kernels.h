@@ -1,0 +1,23 @@
+// tq_kernels.h — internal launchers (C++ linkage, not part of the public ABI).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace tq {
+
+int sm_count();
+
+// [FWHT over heads of 2^log2_hd elements when log2_hd >= 0] + quantize nblocks blocks.
+// qtype 3 or 4; in_dtype DT_F32/DT_F16/DT_BF16; n_passes > 0 selects TQ3 optimal rounding.
+cudaError_t launch_quantize(int qtype, int in_dtype, const void* x, void* y, int64_t nblocks, int log2_hd,
+                            float norm, int n_passes, cudaStream_t st);
+// in-place FWHT of nblocks 32-element rows (heads of 2^log2_hd <= 1024 elements)
+cudaError_t launch_fwht(float* x, int64_t nblocks, int log2_hd, float norm, cudaStream_t st);
+// FWHT of a tail shorter than 32 elements (heads smaller than 32)
+cudaError_t launch_fwht_tail(float* x, int n, int log2_hd, float norm, cudaStream_t st);
+// FWHT of rows longer than 1024 elements, one CTA per row
+cudaError_t launch_fwht_large(float* x, int64_t nrows, int log2_hd, float norm, cudaStream_t st);
+cudaError_t launch_dequantize(int qtype, int out_dtype, const void* x, void* y, int64_t nblocks, cudaStream_t st);
+
+}  // namespace tq

@@ -1,0 +1,99 @@
+"""Torch-tensor front end of the C ABI (device pointers, current CUDA stream).
+
+Every op requires CUDA tensors and raises otherwise: there is no CPU path.
+Packed blocks are uint8 tensors whose last two dims are (n_blocks, 18) for
+TQ4_0 or (n_blocks, 14) for TQ3_0 — the byte layout of src/ggml-tq.h:131-141.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib as L
+
+QK = L.QK
+TQ3_0, TQ4_0 = L.TYPE_TQ3_0, L.TYPE_TQ4_0
+BLOCK_BYTES = L.BLOCK_BYTES
+_DTYPES = {torch.float32: L.DTYPE_F32, torch.float16: L.DTYPE_F16, torch.bfloat16: L.DTYPE_BF16}
+
+
+def _stream(t: torch.Tensor) -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _need_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise ValueError("leankv_b200 ops take CUDA tensors only (there is no CPU fallback)")
+
+
+def _qtype(qtype) -> int:
+    q = {3: TQ3_0, 4: TQ4_0, "tq3_0": TQ3_0, "tq4_0": TQ4_0}.get(qtype)
+    if q is None:
+        raise ValueError(f"unknown TQ type {qtype!r}")
+    return q
+
+
+def quantize(x: torch.Tensor, qtype=4, fwht_head_dim: int = 0, opt_passes: int = 0,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """[FWHT per fwht_head_dim run] + TQ quantize of a contiguous f32/f16/bf16 tensor.
+
+    Returns uint8 blocks shaped (*x.shape[:-1], x.shape[-1] // 32, block_bytes).
+    Bit-exact with hadamard_transform_row + quantize_row_tq*_0_ref
+    (src/ggml-tq.c) on x.float(); opt_passes=2 with qtype=3 is LeanKV's TQ3
+    optimal rounding (scripts/tq3_rounding.py:74-125).
+    """
+    _need_cuda(x)
+    q = _qtype(qtype)
+    if x.dtype not in _DTYPES:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    if not x.is_contiguous():
+        raise ValueError("x must be contiguous")
+    if x.shape[-1] % QK:
+        raise ValueError("the last dimension must be a multiple of 32")
+    shape = (*x.shape[:-1], x.shape[-1] // QK, BLOCK_BYTES[q])
+    if out is None:
+        out = torch.empty(shape, dtype=torch.uint8, device=x.device)
+    else:
+        _need_cuda(out)
+        if out.dtype != torch.uint8 or out.numel() != x.numel() // QK * BLOCK_BYTES[q] or not out.is_contiguous():
+            raise ValueError("out must be a contiguous uint8 tensor of the block size")
+    L.check(L.load().tq_quantize_cuda(q, x.data_ptr(), _DTYPES[x.dtype], out.data_ptr(), x.numel(),
+                                      int(fwht_head_dim), int(opt_passes), _stream(x)))
+    return out
+
+
+def dequantize(blocks: torch.Tensor, qtype=4, dtype: torch.dtype = torch.float32,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """dequantize_row_tq*_0 over uint8 blocks (..., n_blocks, block_bytes) -> (..., n_blocks*32)."""
+    _need_cuda(blocks)
+    q = _qtype(qtype)
+    if blocks.dtype != torch.uint8 or not blocks.is_contiguous():
+        raise ValueError("blocks must be a contiguous uint8 tensor")
+    bb = BLOCK_BYTES[q]
+    if blocks.numel() % bb:
+        raise ValueError("block buffer size is not a multiple of the block size")
+    nb = blocks.numel() // bb
+    if blocks.dim() >= 2 and blocks.shape[-1] == bb:
+        shape = (*blocks.shape[:-2], blocks.shape[-2] * QK)
+    else:
+        shape = (nb * QK,)
+    if out is None:
+        out = torch.empty(shape, dtype=dtype, device=blocks.device)
+    else:
+        _need_cuda(out)
+        if out.numel() != nb * QK or not out.is_contiguous() or out.dtype not in _DTYPES:
+            raise ValueError("bad out tensor")
+    L.check(L.load().tq_dequantize_cuda(q, blocks.data_ptr(), out.data_ptr(), _DTYPES[out.dtype], nb * QK,
+                                        _stream(blocks)))
+    return out
+
+
+def hadamard_(x: torch.Tensor, head_dim: int) -> torch.Tensor:
+    """In-place hadamard_transform_row (src/ggml-tq.c:398-404) on a contiguous float32 tensor."""
+    _need_cuda(x)
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous float32 tensor")
+    L.check(L.load().tq_hadamard_cuda(x.data_ptr(), x.numel(), int(head_dim), _stream(x)))
+    return x

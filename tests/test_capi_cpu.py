@@ -1,0 +1,103 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol the
+public headers declare, and rejects bad arguments with the documented status
+before touching a device."""
+import ctypes as C
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from leankv_b200 import _lib as L
+
+
+def test_library_builds_and_loads():
+    from leankv_b200 import build
+    build.build()
+    lib = L.load()
+    assert lib.tq_abi_version() == 1
+
+
+def test_every_header_symbol_is_exported():
+    names = L.header_functions()
+    # the ggml drop-ins plus the tq_* API must all be declared
+    for n in ("quantize_row_tq3_0_ref", "quantize_row_tq4_0_ref", "dequantize_row_tq3_0", "dequantize_row_tq4_0",
+              "quantize_row_tq3_0", "quantize_row_tq4_0", "hadamard_transform", "hadamard_transform_row",
+              "tq_quantize_cuda", "tq_dequantize_cuda", "tq_hadamard_cuda"):
+        assert n in names
+    out = subprocess.run(["nm", "-D", "--defined-only", L.LIB_PATH], capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    missing = [n for n in names if n not in exported]
+    assert not missing, missing
+
+
+def test_every_header_symbol_has_a_python_signature():
+    missing = [n for n in L.header_functions() if n not in L.SIGNATURES]
+    assert not missing, missing
+
+
+def test_header_compiles_as_c_and_cpp(tmp_path):
+    src = tmp_path / "t.c"
+    src.write_text('#include "leankv_tq.h"\nint main(void){ return (int)sizeof(block_tq4_0) - 18 + (int)sizeof(block_tq3_0) - 14; }\n')
+    for cc, ext in (("gcc", "c"), ("g++", "cpp")):
+        f = tmp_path / f"t.{ext}"
+        f.write_text(src.read_text())
+        exe = tmp_path / f"t_{ext}"
+        subprocess.run([cc, "-std=c11" if ext == "c" else "-std=c++17", "-I", L.HEADER_DIR, str(f), "-o", str(exe)],
+                       check=True)
+        assert subprocess.run([str(exe)]).returncode == 0
+
+
+@pytest.mark.parametrize("call,status", [
+    (lambda lib: lib.tq_quantize_cuda(4, None, 0, None, 33, 0, 0, None), 1),        # k % 32
+    (lambda lib: lib.tq_quantize_cuda(5, None, 0, None, 32, 0, 0, None), 1),        # bad type
+    (lambda lib: lib.tq_quantize_cuda(4, None, 7, None, 32, 0, 0, None), 1),        # bad dtype
+    (lambda lib: lib.tq_quantize_cuda(4, None, 0, None, 32, 0, 0, None), 1),        # null pointers
+    (lambda lib: lib.tq_quantize_cuda(4, 16, 0, 16, 32, 0, 2, None), 2),            # opt rounding on TQ4
+    (lambda lib: lib.tq_quantize_cuda(3, 16, 0, 16, 96, 48, 0, None), 1),           # head_dim not pow2
+    (lambda lib: lib.tq_quantize_cuda(3, 16, 0, 16, 4096, 2048, 0, None), 2),       # fused FWHT > 1024
+    (lambda lib: lib.tq_quantize_cuda(3, 18, 0, 16, 64, 0, 0, None), 3),            # x misaligned for f32
+    (lambda lib: lib.tq_dequantize_cuda(4, 16, 18, 0, 64, None), 3),                # y misaligned
+    (lambda lib: lib.tq_hadamard_cuda(16, 96, 64, None), 1),                        # n % head_dim
+    (lambda lib: lib.tq_hadamard_cuda(16, 1 << 17, 1 << 16, None), 2),              # head_dim > 32768
+    (lambda lib: lib.tq_quantize_host(4, None, 0, None, 31, 0, 0), 1),
+])
+def test_argument_errors(call, status):
+    lib = L.load()
+    assert call(lib) == status
+    assert lib.tq_last_error_string()  # a message is set
+
+
+def test_zero_length_is_a_noop():
+    lib = L.load()
+    assert lib.tq_quantize_cuda(4, None, 0, None, 0, 0, 0, None) == 0
+    assert lib.tq_dequantize_cuda(3, None, None, 0, 0, None) == 0
+
+
+def test_status_strings():
+    lib = L.load()
+    for s in range(8):
+        assert lib.tq_status_string(s)
+
+
+def test_dropin_aborts_like_reference_assert():
+    """k % 32 != 0 aborts (the reference asserts) — checked in a child process."""
+    code = ("import ctypes, numpy as np\n"
+            f"lib = ctypes.CDLL({L.LIB_PATH!r})\n"
+            "x = np.zeros(33, np.float32); y = np.zeros(64, np.uint8)\n"
+            "lib.quantize_row_tq4_0_ref(ctypes.c_void_p(x.ctypes.data), ctypes.c_void_p(y.ctypes.data), ctypes.c_int64(33))\n")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True)
+    assert r.returncode != 0
+    assert "k % 32" in r.stderr
+
+
+def test_ops_reject_cpu_tensors():
+    import torch
+    from leankv_b200 import ops
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.quantize(torch.zeros(64), 4)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.dequantize(torch.zeros(18, dtype=torch.uint8), 4)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.hadamard_(torch.zeros(64), 64)

@@ -184,18 +184,18 @@ def c1_input(seed: int, tokens=4096, heads=8, hd=128):
 class Codec:
     """One workload of the codec family: step() launches the hot path once."""
 
-    def __init__(self, name, rank):
+    def __init__(self, name, rank, tokens=None):
         import torch
         from leankv_b200 import ops
         self.name = name
         if name == "tq3opt":
-            self.x = c2_input(2 + 1000 * rank)
+            self.x = c2_input(2 + 1000 * rank, tokens=tokens or 32768)
             self.qtype, self.hd, self.passes = 3, 128, 2
             self.config = {"workload": "TQ3_0 optimal-rounding quantize (2 CD passes + LS scale), FWHT fused",
                            "input": "bf16 [32768 tokens, 8 KV heads, 128], Student-t(4) x log-normal channel scales",
                            "blocks_per_step": self.x.numel() // 32}
         else:
-            self.x = c1_input(1 + 1000 * rank)
+            self.x = c1_input(1 + 1000 * rank, tokens=tokens or 4096)
             self.qtype, self.hd, self.passes = 4, 128, 0
             self.config = {"workload": "TQ4_0 quantize, FWHT fused (fp32 [4096, 8, 128], N(0,1) + 4 outlier ch x20)",
                            "blocks_per_step": self.x.numel() // 32}
@@ -242,7 +242,7 @@ class Codec:
 
 def run_ours(args, ws, rank, local):
     import torch
-    wl = Codec(args.workload, rank)
+    wl = Codec(args.workload, rank, args.tokens)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     for _ in range(args.warmup):
         wl.step()
@@ -268,16 +268,21 @@ def run_ours(args, ws, rank, local):
     peak, peak_kind = hbm_peak()
     achieved = wl.bytes_per_step / (ms * 1e-3) / 1e9
 
-    # e2e through the C ABI (host buffers), K steps
-    wl.e2e_setup()
-    wl.e2e_step()
-    barrier(ws)
-    t0 = time.perf_counter()
-    for _ in range(args.steps if args.steps <= 50 else 50):
+    # e2e through the C ABI (host buffers)
+    e2e = None
+    if not args.no_e2e:
+        wl.e2e_setup()
         wl.e2e_step()
-    e2e_s = (time.perf_counter() - t0) / (args.steps if args.steps <= 50 else 50)
-    e2e_s = max_over_ranks(e2e_s, ws)
-    h2d, d2h = wl.e2e_bytes()
+        n_e2e = min(args.steps, 50)
+        barrier(ws)
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            wl.e2e_step()
+        e2e_s = max_over_ranks((time.perf_counter() - t0) / n_e2e, ws)
+        h2d, d2h = wl.e2e_bytes()
+        e2e = {"value": round(wl.bytes_per_step * ws / e2e_s / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "path": "tq_quantize_host (C ABI, pinned host buffers)", "steps": n_e2e}
 
     out = None
     if rank == 0:
@@ -302,9 +307,7 @@ def run_ours(args, ws, rank, local):
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "traffic": profile_traffic(args.workload),
                          "algorithmic_bytes_per_launch": wl.bytes_per_step},
-            "e2e": {"value": round(wl.bytes_per_step * ws / e2e_s / 1e9, 3), "unit": "GB/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "tq_quantize_host (C ABI, pinned host buffers)"},
+            "e2e": e2e,
             "gpu_launches": args.steps,
             "clocks": clk.summary(),
             "wall_s_timed_region": round(wall, 4),
@@ -359,6 +362,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["tq3opt", "tq4"], default="tq3opt")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-API measurement (profiling runs)")
+    ap.add_argument("--tokens", type=int, default=None, help="override the token count (profiling runs)")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 3 if args.impl == "reference" else 2000

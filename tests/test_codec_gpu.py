@@ -18,9 +18,10 @@ DEV = "cuda:0"
 
 
 def u32(a):
+    """Bit pattern of a float32 array, flattened (comparisons are shape-agnostic)."""
     if isinstance(a, torch.Tensor):
         a = a.detach().cpu().numpy()
-    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    return np.ascontiguousarray(a, dtype=np.float32).reshape(-1).view(np.uint32)
 
 
 def gpu(a, dtype=None):

@@ -13,7 +13,7 @@ import pytest
 
 
 def u32(a):
-    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    return np.ascontiguousarray(a, dtype=np.float32).reshape(-1).view(np.uint32)
 
 
 @pytest.mark.parametrize("t", [3, 4])

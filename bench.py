@@ -204,6 +204,8 @@ class Codec:
         self.y = torch.empty(self.k // 32 * bb, dtype=torch.uint8, device="cuda")
         self.bytes_per_step = self.k * self.x.element_size() + self.k // 32 * bb
         self.ops = ops
+        self.launches_per_step = 1
+        self.dtype = "bf16->u8 (fp32/fp64 math)" if self.passes else "f32->u8"
 
     def step(self):
         self.ops.quantize(self.x, self.qtype, fwht_head_dim=self.hd, opt_passes=self.passes, out=self.y)
@@ -240,10 +242,75 @@ class Codec:
         return sample_bytes / dt / 1e9, tokens
 
 
+class Attn:
+    """Fused TQ4/TQ4 decode attention, B16 Hq32 Hkv8 D128 ctx 32768 (3 launches per step)."""
+
+    def __init__(self, rank, tokens=None):
+        import torch
+        from leankv_b200 import attention, ops
+        self.attention = attention
+        B, Hq, Hkv, D = 16, 32, 8, 128
+        T = tokens or 32768
+        g = torch.Generator(device="cuda").manual_seed(3 + 1000 * rank)
+        kc = torch.empty(B, Hkv, T, D // 32, 18, dtype=torch.uint8, device="cuda")
+        vc = torch.empty_like(kc)
+        for cache in (kc, vc):          # N(0,1) rows, 4 outlier channels per head x20, rotated + quantized
+            for b in range(B):
+                x = torch.randn(Hkv, T, D, generator=g, device="cuda")
+                for h in range(Hkv):
+                    ch = torch.randperm(D, generator=g, device="cuda")[:4]
+                    x[h, :, ch] *= 20.0
+                ops.quantize(x, 4, fwht_head_dim=D, out=cache[b])
+        self.kc, self.vc = kc, vc
+        self.q = torch.randn(B, Hq, D, generator=g, device="cuda").half()
+        self.out = torch.empty(B, Hq, D, dtype=torch.float16, device="cuda")
+        kv_bytes = kc.numel() + vc.numel()
+        self.bytes_per_step = kv_bytes + self.q.numel() * 2 + self.out.numel() * 2
+        self.launches_per_step = 3
+        self.config = {"workload": "fused TQ4_0/TQ4_0 decode attention (FWHT(q), split-KV, LSE combine, FWHT(o))",
+                       "shape": f"B={B} Hq={Hq} Hkv={Hkv} D={D} ctx={T}, fp16 q/out",
+                       "kv_bytes": kv_bytes}
+        self.dtype = "TQ4 blocks -> f16 MMA, f32 accumulate"
+
+    def step(self):
+        self.attention.decode_attention(self.q, self.kc, self.vc, out=self.out)
+
+    def e2e_setup(self):
+        self.hq = self.q.cpu().pin_memory()
+        self.hout = self.out.cpu().pin_memory()
+
+    def e2e_step(self):
+        import torch
+        self.q.copy_(self.hq, non_blocking=True)
+        self.attention.decode_attention(self.q, self.kc, self.vc, out=self.out)
+        self.hout.copy_(self.out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    def e2e_bytes(self):
+        return self.hq.numel() * 2, self.hout.numel() * 2
+
+    def cpu_run(self, frac, nthreads, impl):
+        from oracle import oracle as O
+        n = max(1, self.q.shape[0] // frac)
+        q = self.q[:n].float().cpu().numpy()
+        kc, vc = self.kc[:n].cpu().numpy(), self.vc[:n].cpu().numpy()
+        t0 = time.perf_counter()
+        O.decode_attention(q, kc, 4, vc, 4, self.kc.shape[1], nthreads=nthreads)
+        dt = time.perf_counter() - t0
+        return self.bytes_per_step * n / self.q.shape[0] / dt / 1e9, n
+
+
+def make_workload(name, rank, tokens):
+    if name == "attn":
+        return Attn(rank, tokens)
+    return Codec(name, rank, tokens)
+
+
 def run_ours(args, ws, rank, local):
     import torch
-    wl = Codec(args.workload, rank, args.tokens)
+    wl = make_workload(args.workload, rank, args.tokens)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    flush_l2 = args.workload != "attn"     # the attention step streams 604 MB (> L2) by itself
     for _ in range(args.warmup):
         wl.step()
     torch.cuda.synchronize()
@@ -254,7 +321,8 @@ def run_ours(args, ws, rank, local):
     with ClockSampler(local) as clk:
         t0 = time.perf_counter()
         for i in range(args.steps):
-            flush.zero_()                      # evict inputs from L2 between steps
+            if flush_l2:
+                flush.zero_()                  # evict inputs from L2 between steps
             starts[i].record()
             wl.step()
             ends[i].record()
@@ -289,26 +357,36 @@ def run_ours(args, ws, rank, local):
         cpu = None
         if ws == 1 and not args.no_cpu_baseline:
             n = os.cpu_count() or 1
-            impl = "port" if wl.passes else "reference"
-            v, tokens = wl.cpu_run(16, n, impl)
-            cpu = {"value": round(v, 4), "unit": "GB/s", "cores": n,
-                   "kind": "port" if wl.passes else "reference",
-                   "sample": f"{tokens} of {wl.x.shape[0]} tokens (1/16 of the workload), {n} threads; "
-                             + ("C restatement of scripts/tq3_rounding.py + reference hadamard_transform_row"
-                                if wl.passes else "reference src/ggml-tq.c hadamard_transform_row + quantize_row")}
+            if isinstance(wl, Attn):
+                v, nseq = wl.cpu_run(16, n, "port")
+                cpu = {"value": round(v, 4), "unit": "GB/s", "cores": n, "kind": "port",
+                       "sample": f"{nseq} of {wl.q.shape[0]} sequences (1/16 of the step), {n} threads; float64 "
+                                 "restatement: reference dequantize_row_tq4_0 + hadamard_transform + exact softmax"}
+            else:
+                impl = "port" if wl.passes else "reference"
+                v, tokens = wl.cpu_run(16, n, impl)
+                cpu = {"value": round(v, 4), "unit": "GB/s", "cores": n,
+                       "kind": "port" if wl.passes else "reference",
+                       "sample": f"{tokens} of {wl.x.shape[0]} tokens (1/16 of the workload), {n} threads; "
+                                 + ("C restatement of scripts/tq3_rounding.py + reference hadamard_transform_row"
+                                    if wl.passes else "reference src/ggml-tq.c hadamard_transform_row + quantize_row")}
         out = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max, 6), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16->u8 (fp32/fp64 math)" if wl.passes else "f32->u8",
+            "vs_baseline": None, "dtype": wl.dtype,
             "data": "synthetic (seeded)",
-            "config": {**wl.config, "parallelism": f"token-row shards x{ws}, no collective",
-                       "l2": "flushed (256 MiB write) between timed steps"},
+            "config": {**wl.config,
+                       "parallelism": (f"{ws} independent replicas of the step (batch x KV-head shards), no collective"
+                                       if isinstance(wl, Attn) else f"token-row shards x{ws}, no collective"),
+                       "l2": ("inputs 604 MB > L2 (126 MB), no flush" if isinstance(wl, Attn)
+                              else "flushed (256 MiB write) between timed steps")},
+            "us_per_step": round(ms_max * 1e3, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "traffic": profile_traffic(args.workload),
                          "algorithmic_bytes_per_launch": wl.bytes_per_step},
             "e2e": e2e,
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * wl.launches_per_step,
             "clocks": clk.summary(),
             "wall_s_timed_region": round(wall, 4),
             "cpu_baseline": cpu,
@@ -324,7 +402,21 @@ def run_reference(args, ws, rank):
     from oracle import oracle as O
     n = os.cpu_count() or 1
     torch.manual_seed(0)
-    if args.workload == "tq3opt":
+    if args.workload == "attn":
+        import numpy as np
+        Hq, Hkv, D, T = 32, 8, 128, 32768
+        rng = np.random.default_rng(3)
+        x = rng.standard_normal((2, Hkv, T, D), dtype=np.float32)
+        x[:, :, :, :4] *= 20.0
+        blocks = O.ref_quantize(4, O.ref_fwht(x, D)).reshape(2, 1, Hkv, T, D // 32, 18)
+        kc, vc = blocks[0], blocks[1]
+        q = rng.standard_normal((1, Hq, D), dtype=np.float32)
+        bytes_ = kc.size + vc.size + q.size * 4
+        fn = lambda: O.decode_attention(q, kc, 4, vc, 4, Hkv, nthreads=n)  # noqa: E731
+        kind, sample = "port", ("1 of the 16 sequences of B16 Hq32 Hkv8 D128 ctx 32768 per step; float64 restatement "
+                                "(reference dequantize_row_tq4_0 + hadamard_transform + exact softmax), no reference "
+                                "CPU attention exists in-tree")
+    elif args.workload == "tq3opt":
         tokens = 32768 // 16
         x = torch.randn(tokens, 8 * 128) * torch.exp(torch.randn(1, 8 * 128))
         arr = x.to(torch.bfloat16).view(torch.int16).numpy().view("uint16")
@@ -347,7 +439,8 @@ def run_reference(args, ws, rank):
     v = bytes_ / dt / 1e9
     return {"metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16->u8" if args.workload == "tq3opt" else "f32->u8",
+            "vs_baseline": None,
+            "dtype": {"tq3opt": "bf16->u8", "tq4": "f32->u8", "attn": "f64"}[args.workload],
             "data": "synthetic (seeded)", "impl": "reference",
             "config": {"workload": args.workload, "parallelism": "host threads"},
             "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": n, "kind": kind, "sample": sample},
@@ -360,13 +453,13 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["tq3opt", "tq4"], default="tq3opt")
+    ap.add_argument("--workload", choices=["tq3opt", "tq4", "attn"], default="tq3opt")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-API measurement (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the token count (profiling runs)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 3 if args.impl == "reference" else 2000
+        args.steps = 3 if args.impl == "reference" else (200 if args.workload == "attn" else 2000)
     if args.warmup is None:
         args.warmup = 3 if args.impl == "reference" else 20
     args.warmup = max(args.warmup, 3)

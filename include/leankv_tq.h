@@ -124,6 +124,50 @@ tq_status tq_quantize_host(tq_type type, const void *x, tq_dtype x_dtype, void *
 tq_status tq_dequantize_host(tq_type type, const void *x, void *y, tq_dtype y_dtype, int64_t k);
 tq_status tq_hadamard_host(float *x, int64_t n, int head_dim);
 
+/* ── fused decode attention over packed K/V blocks ──────────────────────────
+ *
+ * For each sequence b and query head h (GQA: KV head h / (n_q_heads / n_kv_heads)):
+ *   q~ = FWHT(q) when rotate_q (K blocks hold Hadamard-rotated keys),
+ *   s_t = sm_scale * q~ . K^_t, p = softmax(s) over the first kv_len[b] tokens,
+ *   out = sum_t p_t V^_t, followed by FWHT when v_rotated (V blocks hold rotated values),
+ * where K^ / V^ are dequantize_row_tq*_0 of the blocks.  This is the decode path the
+ * LeanKV llama.cpp fork runs on GPU (docs/CUDA-RESULTS.md:10-52; math of
+ * src/test-tq.c:532-559), fused: the dequantized cache is never written to memory.
+ *
+ * Cache layout: [batch][n_kv_heads][kv_capacity][head_dim/32 blocks] of block_tq4_0
+ * (or block_tq3_0), i.e. every token's head row is head_dim/32 consecutive blocks.
+ * q / out: [batch][n_q_heads][head_dim].  lse (optional): [batch][n_q_heads],
+ * natural log of sum_t exp(s_t); -inf and a zero output for kv_len == 0.
+ * Requirements: head_dim 128; n_q_heads / n_kv_heads in {1, 2, 4, 8}; kv_capacity
+ * even; cache pointers 16-byte aligned.  Supported block types: TQ4_0 K and V.
+ * Work memory: tq_decode_attention_workspace_size() bytes of device memory.
+ */
+typedef struct {
+    int batch, n_q_heads, n_kv_heads, head_dim;
+    const void *q;            tq_dtype q_dtype;
+    const void *k_cache;      tq_type k_type;
+    const void *v_cache;      tq_type v_type;
+    int64_t kv_capacity;      /* tokens allocated per (sequence, KV head) */
+    const int32_t *kv_len;    /* device [batch] valid tokens, or NULL = kv_capacity */
+    int64_t max_kv_len;       /* upper bound of kv_len (sizes the split-KV plan); 0 = kv_capacity */
+    float sm_scale;           /* 0 = 1/sqrt(head_dim) */
+    int rotate_q;             /* apply the Hadamard rotation to q */
+    int v_rotated;            /* apply the Hadamard rotation to the output */
+    void *out;                tq_dtype out_dtype;
+    float *lse;               /* optional */
+    void *workspace;          size_t workspace_bytes;
+} tq_decode_attention_args;
+
+/* bytes of device work memory tq_decode_attention_cuda needs for these arguments */
+size_t tq_decode_attention_workspace_size(const tq_decode_attention_args *a);
+/* fused decode attention (new; the fork's CUDA FA vec_dot_fattn_vec_KQ_tq* path) */
+tq_status tq_decode_attention_cuda(const tq_decode_attention_args *a, void *stream);
+/* log-sum-exp merge of n_parts partial results o[n_parts][n_rows][head_dim] with
+ * natural-log lse[n_parts][n_rows] into out[n_rows][head_dim] (+ lse_out, optional):
+ * the split-by-sequence combine of the multi-GPU path (new) */
+tq_status tq_lse_combine_cuda(int n_parts, int64_t n_rows, int head_dim, const float *o, const float *lse,
+                              float *out, float *lse_out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

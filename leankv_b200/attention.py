@@ -1,0 +1,135 @@
+"""Fused decode attention over packed TurboQuant K/V caches (torch front end).
+
+Cache tensors are uint8 with shape [batch, n_kv_heads, capacity, head_dim/32, 18]
+(TQ4_0 blocks, src/ggml-tq.h:137-141).  K and V hold Hadamard-rotated rows
+(quantize with fwht_head_dim=head_dim); the query is rotated inside, and the
+output rotated back, so the result is attention in the original space.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib as L
+from .ops import _DTYPES, _need_cuda, _stream
+
+
+class AttnArgs(C.Structure):
+    """Mirror of tq_decode_attention_args (include/leankv_tq.h)."""
+    _fields_ = [
+        ("batch", C.c_int), ("n_q_heads", C.c_int), ("n_kv_heads", C.c_int), ("head_dim", C.c_int),
+        ("q", C.c_void_p), ("q_dtype", C.c_int),
+        ("k_cache", C.c_void_p), ("k_type", C.c_int),
+        ("v_cache", C.c_void_p), ("v_type", C.c_int),
+        ("kv_capacity", C.c_int64),
+        ("kv_len", C.c_void_p),
+        ("max_kv_len", C.c_int64),
+        ("sm_scale", C.c_float),
+        ("rotate_q", C.c_int),
+        ("v_rotated", C.c_int),
+        ("out", C.c_void_p), ("out_dtype", C.c_int),
+        ("lse", C.c_void_p),
+        ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+    ]
+
+
+def _bind():
+    lib = L.load()
+    lib.tq_decode_attention_workspace_size.restype = C.c_size_t
+    lib.tq_decode_attention_workspace_size.argtypes = [C.POINTER(AttnArgs)]
+    lib.tq_decode_attention_cuda.restype = C.c_int
+    lib.tq_decode_attention_cuda.argtypes = [C.POINTER(AttnArgs), C.c_void_p]
+    lib.tq_lse_combine_cuda.restype = C.c_int
+    lib.tq_lse_combine_cuda.argtypes = [C.c_int, C.c_int64, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                        C.c_void_p, C.c_void_p]
+    return lib
+
+
+_workspaces: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    key = (device.type, device.index)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def make_args(q, k_cache, v_cache, kv_len=None, max_kv_len=0, sm_scale=0.0, rotate_q=True, v_rotated=True,
+              out=None, lse=None, k_type=4, v_type=4):
+    B, Hq, D = q.shape
+    Hkv, cap = k_cache.shape[1], k_cache.shape[2]
+    a = AttnArgs()
+    a.batch, a.n_q_heads, a.n_kv_heads, a.head_dim = B, Hq, Hkv, D
+    a.q, a.q_dtype = q.data_ptr(), _DTYPES[q.dtype]
+    a.k_cache, a.k_type = k_cache.data_ptr(), k_type
+    a.v_cache, a.v_type = v_cache.data_ptr(), v_type
+    a.kv_capacity = cap
+    a.kv_len = kv_len.data_ptr() if kv_len is not None else None
+    a.max_kv_len = int(max_kv_len)
+    a.sm_scale = float(sm_scale)
+    a.rotate_q, a.v_rotated = int(rotate_q), int(v_rotated)
+    a.out, a.out_dtype = out.data_ptr(), _DTYPES[out.dtype]
+    a.lse = lse.data_ptr() if lse is not None else None
+    return a
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     kv_len: torch.Tensor | None = None, max_kv_len: int | None = None,
+                     sm_scale: float | None = None, rotate_q: bool = True, v_rotated: bool = True,
+                     out_dtype: torch.dtype = torch.float32, return_lse: bool = False,
+                     out: torch.Tensor | None = None):
+    """softmax(q~ K^T * sm_scale) V over packed caches; q [B, Hq, D] -> out [B, Hq, D].
+
+    kv_len: int32 CUDA tensor [B] of valid tokens (default: the whole capacity);
+    max_kv_len: host-side upper bound of kv_len used to plan the split-KV work
+    (default: the capacity).
+    """
+    _need_cuda(q, k_cache, v_cache)
+    if q.dim() != 3 or not q.is_contiguous():
+        raise ValueError("q must be a contiguous [B, Hq, D] tensor")
+    if k_cache.dtype != torch.uint8 or v_cache.dtype != torch.uint8:
+        raise ValueError("caches must be uint8 block tensors")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("caches must be contiguous")
+    if kv_len is not None:
+        _need_cuda(kv_len)
+        if kv_len.dtype != torch.int32 or kv_len.numel() != q.shape[0]:
+            raise ValueError("kv_len must be int32 [batch]")
+        kv_len = kv_len.contiguous()
+    B, Hq, D = q.shape
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=out_dtype, device=q.device)
+    lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device) if return_lse else None
+    k_type = 4 if k_cache.shape[-1] == 18 else 3
+    v_type = 4 if v_cache.shape[-1] == 18 else 3
+    a = make_args(q, k_cache, v_cache, kv_len, max_kv_len or 0, sm_scale or 0.0, rotate_q, v_rotated, out, lse,
+                  k_type, v_type)
+    lib = _bind()
+    need = lib.tq_decode_attention_workspace_size(C.byref(a))
+    if need == 0:
+        # argument error: let the launch report it with a message
+        L.check(lib.tq_decode_attention_cuda(C.byref(a), _stream(q)))
+    ws = _workspace(q.device, need)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    L.check(lib.tq_decode_attention_cuda(C.byref(a), _stream(q)))
+    return (out, lse) if return_lse else out
+
+
+def lse_combine(o: torch.Tensor, lse: torch.Tensor, return_lse: bool = False):
+    """Merge partial results o [P, n, D] (normalized) with natural-log lse [P, n]."""
+    _need_cuda(o, lse)
+    if o.dtype != torch.float32 or lse.dtype != torch.float32:
+        raise ValueError("float32 partials expected")
+    o = o.contiguous()
+    lse = lse.contiguous()
+    P, n, D = o.shape
+    out = torch.empty((n, D), dtype=torch.float32, device=o.device)
+    lo = torch.empty((n,), dtype=torch.float32, device=o.device) if return_lse else None
+    lib = _bind()
+    L.check(lib.tq_lse_combine_cuda(P, n, D, o.data_ptr(), lse.data_ptr(), out.data_ptr(),
+                                    lo.data_ptr() if lo is not None else None, _stream(o)))
+    return (out, lo) if return_lse else out

@@ -1,0 +1,38 @@
+// tq_attn.h — internal interface of the decode-attention kernels.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace tq {
+
+struct AttnPlan {
+    int splits = 1;              // token splits per (sequence, KV head)
+    int64_t split_tokens = 0;    // tokens per split (multiple of 256)
+    size_t part_bytes = 0;
+};
+
+struct AttnRun {
+    int B = 0, Hq = 0, Hkv = 0, grp = 0, D = 0;
+    const void* q = nullptr;
+    int q_dtype = 0;
+    const void* k = nullptr;
+    const void* v = nullptr;
+    int k_type = 4, v_type = 4;
+    int64_t cap = 0;
+    const int32_t* kv_len = nullptr;
+    float sm_scale = 0.0f;
+    int rotate_q = 1, v_rotated = 1;
+    void* out = nullptr;
+    int out_dtype = 0;
+    float* lse = nullptr;
+};
+
+AttnPlan attn_plan(int B, int Hkv, int64_t cap, int64_t max_len);
+size_t attn_workspace_bytes(int B, int Hkv, int D, const AttnPlan& p);
+cudaError_t launch_decode_attention(const AttnRun& r, const AttnPlan& p, void* workspace, cudaStream_t st);
+cudaError_t launch_lse_combine(const float* o, const float* lse, float* out, float* lse_out, int P, int64_t n, int D,
+                               cudaStream_t st);
+
+}  // namespace tq

@@ -1,0 +1,70 @@
+// tq_capi_attn.cu — extern "C" entry points of the decode attention.
+#include <cmath>
+
+#include "leankv_tq.h"
+#include "tq_attn.h"
+#include "tq_capi_internal.h"
+#include "tq_common.cuh"
+
+using namespace tq;
+
+static tq_status attn_check(const tq_decode_attention_args* a, AttnRun* r, AttnPlan* p) {
+    if (!a) return set_error(TQ_ERROR_INVALID_VALUE, "null argument block");
+    if (a->batch < 0 || a->n_q_heads <= 0 || a->n_kv_heads <= 0)
+        return set_error(TQ_ERROR_INVALID_VALUE, "bad batch / head counts");
+    if (a->n_q_heads % a->n_kv_heads) return set_error(TQ_ERROR_INVALID_VALUE, "n_q_heads %% n_kv_heads != 0");
+    const int grp = a->n_q_heads / a->n_kv_heads;
+    if (grp != 1 && grp != 2 && grp != 4 && grp != 8)
+        return set_error(TQ_ERROR_UNSUPPORTED, "GQA group size %d (supported: 1, 2, 4, 8)", grp);
+    if (a->head_dim != 128) return set_error(TQ_ERROR_UNSUPPORTED, "head_dim %d (supported: 128)", a->head_dim);
+    if (a->k_type != TQ_TYPE_TQ4_0 || a->v_type != TQ_TYPE_TQ4_0)
+        return set_error(TQ_ERROR_UNSUPPORTED, "block types K=%d V=%d (supported: TQ4_0/TQ4_0)", (int)a->k_type,
+                         (int)a->v_type);
+    if (!dtype_ok(a->q_dtype) || !dtype_ok(a->out_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "bad dtype");
+    if (a->kv_capacity < 0 || (a->kv_capacity & 1)) return set_error(TQ_ERROR_INVALID_VALUE, "kv_capacity must be even");
+    if (a->max_kv_len < 0 || a->max_kv_len > a->kv_capacity)
+        return set_error(TQ_ERROR_INVALID_VALUE, "max_kv_len outside [0, kv_capacity]");
+    if (a->batch > 0 && (!a->q || !a->out || (a->kv_capacity > 0 && (!a->k_cache || !a->v_cache))))
+        return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    if ((((uintptr_t)a->k_cache) | ((uintptr_t)a->v_cache)) & 15)
+        return set_error(TQ_ERROR_MISALIGNED, "cache pointers must be 16-byte aligned");
+    if (((uintptr_t)a->q) % dtype_bytes(a->q_dtype) || ((uintptr_t)a->out) % dtype_bytes(a->out_dtype))
+        return set_error(TQ_ERROR_MISALIGNED, "q / out not aligned to their element size");
+    r->B = a->batch; r->Hq = a->n_q_heads; r->Hkv = a->n_kv_heads; r->grp = grp; r->D = a->head_dim;
+    r->q = a->q; r->q_dtype = a->q_dtype; r->k = a->k_cache; r->v = a->v_cache;
+    r->k_type = a->k_type; r->v_type = a->v_type; r->cap = a->kv_capacity; r->kv_len = a->kv_len;
+    r->sm_scale = a->sm_scale != 0.0f ? a->sm_scale : 1.0f / sqrtf((float)a->head_dim);
+    r->rotate_q = a->rotate_q != 0; r->v_rotated = a->v_rotated != 0;
+    r->out = a->out; r->out_dtype = a->out_dtype; r->lse = a->lse;
+    *p = attn_plan(a->batch, a->n_kv_heads, a->kv_capacity, a->max_kv_len > 0 ? a->max_kv_len : a->kv_capacity);
+    return TQ_SUCCESS;
+}
+
+extern "C" size_t tq_decode_attention_workspace_size(const tq_decode_attention_args* a) {
+    AttnRun r;
+    AttnPlan p;
+    if (attn_check(a, &r, &p) != TQ_SUCCESS) return 0;
+    return attn_workspace_bytes(r.B, r.Hkv, r.D, p);
+}
+
+extern "C" tq_status tq_decode_attention_cuda(const tq_decode_attention_args* a, void* stream) {
+    AttnRun r;
+    AttnPlan p;
+    tq_status s = attn_check(a, &r, &p);
+    if (s) return s;
+    if (r.B == 0) return TQ_SUCCESS;
+    const size_t need = attn_workspace_bytes(r.B, r.Hkv, r.D, p);
+    if (!a->workspace || a->workspace_bytes < need)
+        return set_error(TQ_ERROR_INVALID_VALUE, "workspace of %zu bytes needed", need);
+    if (((uintptr_t)a->workspace) & 255) return set_error(TQ_ERROR_MISALIGNED, "workspace must be 256-byte aligned");
+    return cuda_status(launch_decode_attention(r, p, a->workspace, (cudaStream_t)stream), "decode attention launch");
+}
+
+extern "C" tq_status tq_lse_combine_cuda(int n_parts, int64_t n_rows, int head_dim, const float* o, const float* lse,
+                                         float* out, float* lse_out, void* stream) {
+    if (n_parts <= 0 || n_rows < 0 || head_dim <= 0) return set_error(TQ_ERROR_INVALID_VALUE, "bad sizes");
+    if (n_rows == 0) return TQ_SUCCESS;
+    if (!o || !lse || !out) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    return cuda_status(launch_lse_combine(o, lse, out, lse_out, n_parts, n_rows, head_dim, (cudaStream_t)stream),
+                       "lse combine launch");
+}

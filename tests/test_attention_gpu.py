@@ -1,0 +1,177 @@
+"""GPU parity of the fused decode attention.
+
+Reference: the float64 oracle (reference dequantization + FWHT + exact softmax),
+and at full size a torch float32 evaluation on caches dequantized by the
+bit-exact dequantizer.  Tolerance (floating-point kernel, fp16 tensor-core
+operands, fp32 accumulation): max |out - ref| <= 1e-3 * max |ref| + 1e-5, and
+|lse - lse_ref| <= 1e-3 * max(1, |lse_ref|).
+"""
+import numpy as np
+import pytest
+import torch
+
+from leankv_b200 import attention, ops
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+RTOL = 1e-3
+
+
+def make_cache(B, Hkv, T, D, seed, qtype=4, outliers=True):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(B, Hkv, T, D, generator=g)
+    if outliers:
+        for h in range(Hkv):
+            ch = torch.randperm(D, generator=g)[:4]
+            x[:, h, :, ch] *= 20.0
+    blocks = ops.quantize(x.to(DEV).contiguous(), qtype, fwht_head_dim=D)   # rotated + quantized
+    return blocks   # [B, Hkv, T, D/32, bb]
+
+
+def check(out, ref, lse=None, lse_ref=None):
+    out = np.asarray(out, np.float64)
+    ref = np.asarray(ref, np.float64)
+    err = np.abs(out - ref).max()
+    tol = RTOL * np.abs(ref).max() + 1e-5
+    assert err <= tol, f"max abs err {err:.3g} > tol {tol:.3g}"
+    if lse is not None:
+        fin = np.isfinite(lse_ref)
+        assert np.array_equal(np.isfinite(lse), fin)
+        d = np.abs(np.asarray(lse, np.float64)[fin] - lse_ref[fin]).max() if fin.any() else 0.0
+        assert d <= RTOL * max(1.0, np.abs(lse_ref[fin]).max() if fin.any() else 1.0)
+    return err / max(np.abs(ref).max(), 1e-30)
+
+
+@pytest.mark.parametrize("grp", [1, 2, 4, 8])
+def test_attention_vs_oracle_grp(orc, grp):
+    B, Hkv, T, D = 2, 2, 700, 128
+    Hq = Hkv * grp
+    kc = make_cache(B, Hkv, T, D, 10 + grp)
+    vc = make_cache(B, Hkv, T, D, 20 + grp)
+    q = torch.randn(B, Hq, D, generator=torch.Generator().manual_seed(grp)).to(torch.float16)
+    lens = torch.tensor([700, 333], dtype=torch.int32)
+    out, lse = attention.decode_attention(q.to(DEV), kc, vc, kv_len=lens.to(DEV), return_lse=True)
+    ref, lref = orc.decode_attention(q.float().numpy(), kc.cpu().numpy(), 4, vc.cpu().numpy(), 4, Hkv,
+                                     kv_len=lens.numpy(), nthreads=8)
+    rel = check(out.cpu().numpy(), ref, lse.cpu().numpy(), lref)
+    print(f"grp {grp}: rel err {rel:.3g}")
+
+
+@pytest.mark.parametrize("T,lens", [(16, [16]), (34, [1]), (1026, [1026]), (4000, [0]), (5000, [4999]),
+                                    (2, [2]), (9000, [8191])])
+def test_attention_ragged_lengths(orc, T, lens):
+    B, Hkv, D, grp = len(lens), 1, 128, 4
+    kc = make_cache(B, Hkv, T, D, 7)
+    vc = make_cache(B, Hkv, T, D, 8)
+    q = torch.randn(B, Hkv * grp, D, generator=torch.Generator().manual_seed(T))
+    lt = torch.tensor(lens, dtype=torch.int32)
+    out, lse = attention.decode_attention(q.to(DEV), kc, vc, kv_len=lt.to(DEV), return_lse=True)
+    ref, lref = orc.decode_attention(q.numpy(), kc.cpu().numpy(), 4, vc.cpu().numpy(), 4, Hkv,
+                                     kv_len=lt.numpy(), nthreads=8)
+    check(out.cpu().numpy(), ref, lse.cpu().numpy(), lref)
+    if lens[0] == 0:
+        assert torch.all(out == 0) and torch.isinf(lse).all() and (lse < 0).all()
+
+
+@pytest.mark.parametrize("rotate_q,v_rotated", [(True, False), (False, True), (False, False)])
+def test_attention_rotation_flags(orc, rotate_q, v_rotated):
+    B, Hkv, T, D, grp = 1, 2, 512, 128, 2
+    kc = make_cache(B, Hkv, T, D, 3)
+    vc = make_cache(B, Hkv, T, D, 4)
+    q = torch.randn(B, Hkv * grp, D, generator=torch.Generator().manual_seed(1))
+    out = attention.decode_attention(q.to(DEV), kc, vc, rotate_q=rotate_q, v_rotated=v_rotated)
+    ref, _ = orc.decode_attention(q.numpy(), kc.cpu().numpy(), 4, vc.cpu().numpy(), 4, Hkv,
+                                  rotate_q=rotate_q, v_rotated=v_rotated, nthreads=4)
+    check(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("qd,od", [(torch.float32, torch.float16), (torch.bfloat16, torch.bfloat16),
+                                   (torch.float16, torch.float32)])
+def test_attention_dtypes(orc, qd, od):
+    B, Hkv, T, D, grp = 2, 1, 300, 128, 8
+    kc = make_cache(B, Hkv, T, D, 5)
+    vc = make_cache(B, Hkv, T, D, 6)
+    q = torch.randn(B, Hkv * grp, D, generator=torch.Generator().manual_seed(2)).to(qd)
+    out = attention.decode_attention(q.to(DEV), kc, vc, out_dtype=od)
+    assert out.dtype == od
+    ref, _ = orc.decode_attention(q.float().numpy(), kc.cpu().numpy(), 4, vc.cpu().numpy(), 4, Hkv, nthreads=4)
+    tol_scale = 1.0 if od == torch.float32 else 4.0
+    err = (out.float().cpu().numpy() - ref).__abs__().max()
+    assert err <= tol_scale * (RTOL * np.abs(ref).max() + 1e-5) + (8e-3 * np.abs(ref).max() if od == torch.bfloat16 else 0)
+
+
+def test_attention_custom_scale_and_peaky_scores(orc):
+    """Large sm_scale makes the softmax nearly one-hot (stresses the running max)."""
+    B, Hkv, T, D, grp = 1, 1, 2048, 128, 4
+    kc = make_cache(B, Hkv, T, D, 11)
+    vc = make_cache(B, Hkv, T, D, 12)
+    q = torch.randn(B, grp, D, generator=torch.Generator().manual_seed(3)) * 3
+    out, lse = attention.decode_attention(q.to(DEV), kc, vc, sm_scale=0.9, return_lse=True)
+    ref, lref = orc.decode_attention(q.numpy(), kc.cpu().numpy(), 4, vc.cpu().numpy(), 4, Hkv, sm_scale=0.9,
+                                     nthreads=4)
+    check(out.cpu().numpy(), ref, lse.cpu().numpy(), lref)
+
+
+def torch_reference(q, kc, vc, D):
+    """float32 torch evaluation on bit-exact dequantized caches."""
+    B, Hkv, T = kc.shape[:3]
+    Hq = q.shape[1]
+    grp = Hq // Hkv
+    kd = ops.dequantize(kc.reshape(B, Hkv, T * (D // 32), 18), 4).reshape(B, Hkv, T, D)
+    vd = ops.dequantize(vc.reshape(B, Hkv, T * (D // 32), 18), 4).reshape(B, Hkv, T, D)
+    H = torch.tensor([[1.0]], device=DEV)
+    while H.shape[0] < D:
+        H = torch.cat([torch.cat([H, H], 1), torch.cat([H, -H], 1)], 0)
+    H = H / np.sqrt(D)
+    qr = (q.float() @ H).reshape(B, Hkv, grp, D)
+    s = torch.einsum("bhgd,bhtd->bhgt", qr, kd) / np.sqrt(D)
+    p = torch.softmax(s, dim=-1)
+    o = torch.einsum("bhgt,bhtd->bhgd", p, vd) @ H
+    return o.reshape(B, Hq, D), torch.logsumexp(s, dim=-1).reshape(B, Hq)
+
+
+def test_c3_full_size_tq4(orc):
+    """B16 Hq32 Hkv8 D128 ctx 32768, TQ4_0 K/V, fp16 queries: torch fp32 for all, oracle for 2 sequences."""
+    B, Hq, Hkv, T, D = 16, 32, 8, 32768, 128
+    g = torch.Generator(device=DEV).manual_seed(3)
+    kc = ops.quantize(torch.randn(B, Hkv, T, D, device=DEV, generator=g), 4, fwht_head_dim=D)
+    vc = ops.quantize(torch.randn(B, Hkv, T, D, device=DEV, generator=g), 4, fwht_head_dim=D)
+    q = torch.randn(B, Hq, D, device=DEV, generator=g).half()
+    out, lse = attention.decode_attention(q, kc, vc, return_lse=True)
+    ref, lref = torch_reference(q, kc, vc, D)
+    rel = check(out.cpu().numpy(), ref.cpu().numpy(), lse.cpu().numpy(), lref.cpu().numpy())
+    print(f"C3 vs torch fp32: rel err {rel:.3g}")
+    sel = [0, 9]
+    o_ref, l_ref = orc.decode_attention(q[sel].float().cpu().numpy(), kc[sel].cpu().numpy(), 4,
+                                        vc[sel].cpu().numpy(), 4, Hkv, nthreads=16)
+    rel = check(out[sel].cpu().numpy(), o_ref, lse[sel].cpu().numpy(), l_ref)
+    print(f"C3 vs float64 oracle (2 sequences): rel err {rel:.3g}")
+
+
+def test_lse_combine_matches_oracle(orc):
+    rng = np.random.default_rng(5)
+    o = rng.standard_normal((4, 33, 128)).astype(np.float32)
+    lse = rng.standard_normal((4, 33)).astype(np.float32)
+    lse[2, 5] = -np.inf
+    lse[:, 7] = -np.inf
+    out, lo = attention.lse_combine(torch.from_numpy(o).to(DEV), torch.from_numpy(lse).to(DEV), return_lse=True)
+    ref, lref = orc.lse_combine(o, lse)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(lo.cpu().numpy(), lref, rtol=1e-5, atol=1e-6)
+
+
+def test_split_by_sequence_combine_equals_full(orc):
+    """Attention over a context split in P pieces + lse_combine == attention over the whole context."""
+    B, Hkv, T, D, grp, P = 2, 2, 4096, 128, 8, 4
+    kc = make_cache(B, Hkv, T, D, 31)
+    vc = make_cache(B, Hkv, T, D, 32)
+    q = torch.randn(B, Hkv * grp, D, generator=torch.Generator().manual_seed(9)).to(DEV)
+    full = attention.decode_attention(q, kc, vc)
+    parts, lses = [], []
+    for p in range(P):
+        sl = slice(p * T // P, (p + 1) * T // P)
+        o, l = attention.decode_attention(q, kc[:, :, sl].contiguous(), vc[:, :, sl].contiguous(), return_lse=True)
+        parts.append(o.reshape(-1, D))
+        lses.append(l.reshape(-1))
+    comb = attention.lse_combine(torch.stack(parts), torch.stack(lses)).reshape(full.shape)
+    check(comb.cpu().numpy(), full.cpu().numpy())

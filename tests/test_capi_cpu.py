@@ -101,3 +101,47 @@ def test_ops_reject_cpu_tensors():
         ops.dequantize(torch.zeros(18, dtype=torch.uint8), 4)
     with pytest.raises(ValueError, match="CUDA"):
         ops.hadamard_(torch.zeros(64), 64)
+
+
+def test_attention_argument_errors():
+    """The attention entry point validates its argument block before any device work."""
+    import torch
+    from leankv_b200 import attention as A
+    lib = A._bind()
+    a = A.AttnArgs()
+    a.batch, a.n_q_heads, a.n_kv_heads, a.head_dim = 1, 12, 8, 128          # 12 % 8 != 0
+    a.k_type = a.v_type = 4
+    a.kv_capacity = 64
+    assert lib.tq_decode_attention_cuda(C.byref(a), None) == 1
+    a.n_q_heads = 64                                                         # group 8 ok, head_dim 64 not
+    a.head_dim = 64
+    assert lib.tq_decode_attention_cuda(C.byref(a), None) == 2
+    a.head_dim = 128
+    a.kv_capacity = 63                                                       # odd capacity
+    assert lib.tq_decode_attention_cuda(C.byref(a), None) == 1
+    a.kv_capacity = 64
+    a.q = a.out = 16
+    a.k_cache = 24                                                           # not 16-byte aligned
+    a.v_cache = 32
+    assert lib.tq_decode_attention_cuda(C.byref(a), None) == 3
+    a.k_cache = 32
+    assert lib.tq_decode_attention_workspace_size(C.byref(a)) > 0
+    assert lib.tq_decode_attention_cuda(C.byref(a), None) == 1               # no workspace
+    assert ctypes_sizeof_matches_c()
+
+
+def ctypes_sizeof_matches_c(tmp=None):
+    """sizeof(tq_decode_attention_args) in C equals the ctypes mirror."""
+    import tempfile
+    from leankv_b200 import attention as A
+    with tempfile.TemporaryDirectory() as td:
+        src = os.path.join(td, "s.c")
+        open(src, "w").write('#include "leankv_tq.h"\n#include <stdio.h>\n#include <stddef.h>\n'
+                             'int main(void){printf("%zu %zu %zu\\n", sizeof(tq_decode_attention_args),'
+                             ' offsetof(tq_decode_attention_args, workspace_bytes),'
+                             ' offsetof(tq_decode_attention_args, sm_scale)); return 0;}\n')
+        exe = os.path.join(td, "s")
+        subprocess.run(["gcc", "-I", L.HEADER_DIR, src, "-o", exe], check=True)
+        sz, off_ws, off_sc = map(int, subprocess.run([exe], capture_output=True, text=True).stdout.split())
+    return (sz == C.sizeof(A.AttnArgs) and off_ws == A.AttnArgs.workspace_bytes.offset
+            and off_sc == A.AttnArgs.sm_scale.offset)

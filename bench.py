@@ -350,7 +350,9 @@ def run_ours(args, ws, rank, local):
         h2d, d2h = wl.e2e_bytes()
         e2e = {"value": round(wl.bytes_per_step * ws / e2e_s / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "path": "tq_quantize_host (C ABI, pinned host buffers)", "steps": n_e2e}
+               "path": ("leankv_b200.attention.decode_attention, q H2D and out D2H from pinned host memory"
+                        if isinstance(wl, Attn) else "tq_quantize_host (C ABI, pinned host buffers)"),
+               "steps": n_e2e}
 
     out = None
     if rank == 0:

@@ -33,6 +33,7 @@
 //     K-chunk = the warp's 16 tokens.  The V block scales multiply P (fp16).
 #include <cstdint>
 #include <cstdio>
+#include <type_traits>
 
 #include "leankv_tq.h"
 #include "tq_attn.h"
@@ -198,79 +199,162 @@ __global__ void __launch_bounds__(128) attn_qprep_kernel(const QT* __restrict__ 
 }
 
 // ── decode kernel ─────────────────────────────────────────────────────────────
+//
+// Work split: the (sequence, KV head, token) space, each pair padded to a
+// nominal length Lnom (a multiple of 16), is cut into equal contiguous chunks,
+// one per CTA, so every SM streams the same number of bytes.  A chunk covers
+// one or more pair segments; within a segment warp w takes tiles w, w+16, ...
+// (16 tokens each) through its private 4-stage bulk-copy ring.  At the end of a
+// segment the 16 warps merge their (max, sum, O) in shared memory and the CTA
+// writes one partial for (pair, slot), slot = CTA index - first CTA of the pair.
 
 struct AttnKernelArgs {
     const uint32_t* qfrag;      // [pairs][D/16][32][2]
     const uint8_t* k;
     const uint8_t* v;
     const int32_t* kv_len;      // [B] or null
-    float* part;                // [pairs][splits][ATT_N][D + 2]
+    float* part;                // [pairs][slots][ATT_N][D + 2]
     int* err;
     int64_t cap;                // token capacity per (sequence, KV head)
-    int64_t split_tokens;       // multiple of ATT_WARPS * ATT_TILE
-    int B, Hkv, grp, splits;
+    int64_t lnom;               // nominal tokens per pair (multiple of 16, >= every kv_len used)
+    int64_t chunk;              // tokens per CTA (multiple of 256)
+    int B, Hkv, slots;
 };
 
-template <int D, int KT, int VT>
+template <int RES>
+__device__ __forceinline__ uint32_t lut_ld(uint32_t word, uint32_t lane4, uint32_t sel) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(prmt(word, lane4, sel)), "n"(RES));
+    return v;
+}
+template <int OFF>
+__device__ __forceinline__ uint32_t ld16(uint32_t base) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1+%2];" : "=h"(v) : "r"(base), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ __forceinline__ uint32_t ld32(uint32_t base) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(base), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ __forceinline__ float4 ld128f(uint32_t base) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4+%5];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(base), "n"(OFF));
+    return v;
+}
+
+__device__ __forceinline__ void mma16816_zc(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+// bulk copy issued by lane 0 only (predicated, no branch)
+__device__ __forceinline__ void bulk_issue(bool pred, uint32_t dst_k, const void* src_k, uint32_t bk,
+                                           uint32_t dst_v, const void* src_v, uint32_t bv, uint32_t bar) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.u32 p, %8, 0;\n\t"
+        "@p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%6], %7;\n\t"
+        "@p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%6];\n\t"
+        "@p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%3], [%4], %5, [%6];\n\t}"
+        ::"r"(dst_k), "l"(src_k), "r"(bk), "r"(dst_v), "l"(src_v), "r"(bv), "r"(bar), "r"(bk + bv),
+        "r"((uint32_t)pred)
+        : "memory");
+}
+
+constexpr float M_FLOOR = -1.0e30f;   // finite "minus infinity" for the running max
+
+// compile-time loop: f(std::integral_constant<int, I>) for I in [B, E)
+template <int B, int E, typename F>
+__device__ __forceinline__ void static_for(F&& f) {
+    if constexpr (B < E) {
+        f(std::integral_constant<int, B>{});
+        static_for<B + 1, E>(f);
+    }
+}
+
+template <int D, int KT, int VT, int RES>
 __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnKernelArgs a) {
     constexpr int NBLK = D / 32;
     constexpr int KB = (KT == 4 ? TQ4_BYTES : TQ3_BYTES) * NBLK;   // bytes per token
     constexpr int VB = (VT == 4 ? TQ4_BYTES : TQ3_BYTES) * NBLK;
     constexpr int KTILE = ATT_TILE * KB, VTILE = ATT_TILE * VB;
-    constexpr int NCH = D / 16;                 // QK k-chunks
-    constexpr int NMT = D / 16;                 // PV m-tiles
-    static_assert(KT == 4 && VT == 4, "this build covers TQ4_0 K and V");
+    constexpr int STAGE = KTILE + VTILE;
+    constexpr int NCH = D / 16;
+    constexpr int NMT = D / 16;
+    constexpr int SCR = ATT_TILE * NBLK * 4 + NBLK * ATT_TILE * 2;   // per-warp scale scratch bytes
+    static_assert(KT == 4 && VT == 4, "TQ4_0 K and V");
+    static_assert(D == 128, "head_dim 128");
 
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t* lut = smem;
-    uint8_t* stages = smem + LUT_BYTES;                                        // [warp][stage][K|V]
-    float* dks = reinterpret_cast<float*>(stages + ATT_WARPS * ATT_STAGES * (KTILE + VTILE));   // [warp][16][NBLK]
-    uint16_t* dvs = reinterpret_cast<uint16_t*>(dks + ATT_WARPS * ATT_TILE * NBLK);               // [warp][NBLK][16]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(dvs + ATT_WARPS * NBLK * ATT_TILE);             // [warp][stage]
+    // layout: LUT | stages [warp][stage] | scale scratch [warp] | barriers [warp][stage] | flag
+    uint8_t* stages = smem + LUT_BYTES;
+    uint8_t* scratch = stages + ATT_WARPS * ATT_STAGES * STAGE;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + ATT_WARPS * SCR);
+    int* s_abort = reinterpret_cast<int*>(bars + ATT_WARPS * ATT_STAGES);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;
     const uint32_t lane4 = (uint32_t)lane << 2;
 
-    // codebook table (TQ4 rows)
+    if (smem_u32(smem) != (uint32_t)RES) {        // the LUT offset is an instruction immediate
+        if (threadIdx.x == 0) atomicExch(a.err, (int)TQ_ERROR_UNSUPPORTED);
+        return;                                    // uniform: no barrier has been used yet
+    }
     for (int i = threadIdx.x; i < 256 * 32; i += ATT_THREADS) {
         const int k = i >> 5, l = i & 31;
-        const uint32_t v = pack_h2(tq4_level(k & 15), tq4_level(k >> 4));
-        *reinterpret_cast<uint32_t*>(lut + (k << 8) + (l << 2)) = v;
+        *reinterpret_cast<uint32_t*>(smem + (k << 8) + (l << 2)) = pack_h2(tq4_level(k & 15), tq4_level(k >> 4));
     }
     if (lane == 0)
         for (int s = 0; s < ATT_STAGES; ++s) mbar_init(smem_u32(&bars[warp * ATT_STAGES + s]), 1);
+    if (threadIdx.x == 0) *s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     __syncthreads();
 
-    __shared__ int s_abort;
-    if (threadIdx.x == 0) s_abort = 0;
-    const uint32_t lut_base = smem_u32(lut);
-    uint8_t* my_stage = stages + warp * ATT_STAGES * (KTILE + VTILE);
-    float* my_dk = dks + warp * ATT_TILE * NBLK;
-    uint16_t* my_dv = dvs + warp * NBLK * ATT_TILE;
-    uint32_t phase_bits = 0;   // parity per stage
+    const uint32_t stage0 = smem_u32(stages + warp * ATT_STAGES * STAGE);
+    const uint32_t scr = smem_u32(scratch + warp * SCR);               // dK f32 [16][4] | dV f16 [4][16]
+    const uint32_t bar0 = smem_u32(&bars[warp * ATT_STAGES]);
+    // per-lane fixed offsets
+    const uint32_t k_off = gq * KB + 2 * tq + 2;                        // + blk*18 + 8h (+ 8 tokens)
+    const uint32_t v_off = (2 * tq) * VB + 2 * gq + 2;                   // + tok {0,1,8,9} + blk*18
+    // scale extraction: lane handles entries e = lane + 32 r, r = 0..3 (0..63 K, 64..127 V)
+    uint32_t x_src[4], x_dst[4];
+    const int x_tok = lane >> 2;              // token of entries r = 0, 2; entries r = 1, 3 hold token + 8
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int e = lane + 32 * r, isv = e >= 64, ee = e & 63, tok = ee >> 2, blk = ee & 3;
+        x_src[r] = (isv ? KTILE + tok * VB : tok * KB) + blk * TQ4_BYTES;
+        x_dst[r] = isv ? ATT_TILE * NBLK * 4 + (blk * ATT_TILE + tok) * 2 : (tok * NBLK + blk) * 4;
+    }
+    uint32_t phase_bits = 0;
 
     const int64_t pairs = (int64_t)a.B * a.Hkv;
-    const int64_t items = pairs * a.splits;
-    const int64_t per_warp = a.split_tokens / ATT_WARPS;
+    const int64_t total = pairs * a.lnom;
+    int64_t gpos = (int64_t)blockIdx.x * a.chunk;
+    const int64_t gend = gpos + a.chunk < total ? gpos + a.chunk : total;
 
-    for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
-        const int64_t pair = item / a.splits;
-        const int split = (int)(item % a.splits);
-        const int bseq = (int)(pair / a.Hkv);
-        int64_t len = a.kv_len ? (int64_t)a.kv_len[bseq] : a.cap;
+    while (gpos < gend) {
+        const int64_t pair = gpos / a.lnom;
+        const int64_t t0 = gpos - pair * a.lnom;
+        int64_t t1 = a.lnom - t0 < gend - gpos ? a.lnom : t0 + (gend - gpos);
+        gpos += t1 - t0;
+        const int slot = (int)(blockIdx.x - (pair * a.lnom) / a.chunk);
+        int64_t len = a.kv_len ? (int64_t)a.kv_len[pair / a.Hkv] : a.cap;
         if (len > a.cap) len = a.cap;
-        if (len < 0) len = 0;
-        const int64_t t_begin = (int64_t)split * a.split_tokens + warp * per_warp;
-        int64_t t_end = t_begin + per_warp;
-        if (t_end > len) t_end = len;
-        const int ntiles = t_end > t_begin ? (int)((t_end - t_begin + ATT_TILE - 1) / ATT_TILE) : 0;
+        if (t1 > len) t1 = len;
+        const int ntiles_seg = t1 > t0 ? (int)((t1 - t0 + ATT_TILE - 1) / ATT_TILE) : 0;
+        const int ntiles = ntiles_seg > warp ? (ntiles_seg - warp + ATT_WARPS - 1) / ATT_WARPS : 0;
 
         const uint8_t* kbase = a.k + (size_t)pair * a.cap * KB;
         const uint8_t* vbase = a.v + (size_t)pair * a.cap * VB;
 
-        // B fragments of q~ for this pair
         uint32_t qf[NCH][2];
         {
             const uint32_t* src = a.qfrag + (size_t)pair * NCH * 64;
@@ -280,171 +364,158 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
                 qf[kk][1] = src[kk * 64 + lane * 2 + 1];
             }
         }
-
         float o[NMT][4];
 #pragma unroll
         for (int mt = 0; mt < NMT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
-        float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
+        float m_run0 = M_FLOOR, m_run1 = M_FLOOR, l0 = 0.0f, l1 = 0.0f;
 
-        // issue: one elected lane posts the bulk copies of tile i into stage i % STAGES
         auto issue = [&](int i) {
-            if (lane == 0 && i < ntiles) {
-                const int s = i % ATT_STAGES;
-                const int64_t t0 = t_begin + (int64_t)i * ATT_TILE;
-                int64_t nt = a.cap - t0;
-                if (nt > ATT_TILE) nt = ATT_TILE;
-                const uint32_t kbytes = (uint32_t)(nt * KB), vbytes = (uint32_t)(nt * VB);
-                const uint32_t bar = smem_u32(&bars[warp * ATT_STAGES + s]);
-                uint8_t* dst = my_stage + s * (KTILE + VTILE);
-                mbar_expect_tx(bar, kbytes + vbytes);
-                bulk_g2s(smem_u32(dst), kbase + t0 * KB, kbytes, bar);
-                bulk_g2s(smem_u32(dst + KTILE), vbase + t0 * VB, vbytes, bar);
-            }
+            const int64_t t = t0 + (int64_t)(warp + i * ATT_WARPS) * ATT_TILE;
+            int64_t nt = a.cap - t;
+            if (nt > ATT_TILE) nt = ATT_TILE;
+            const int s = i % ATT_STAGES;
+            const uint32_t dst = stage0 + s * STAGE;
+            bulk_issue(lane == 0 && i < ntiles, dst, kbase + t * KB, (uint32_t)(nt * KB), dst + KTILE,
+                       vbase + t * VB, (uint32_t)(nt * VB), bar0 + 8 * s);
         };
         for (int i = 0; i < ATT_STAGES - 1; ++i) issue(i);
 
-        bool timed_out = false;
         for (int i = 0; i < ntiles; ++i) {
             issue(i + ATT_STAGES - 1);
             const int s = i % ATT_STAGES;
-            const uint32_t bar = smem_u32(&bars[warp * ATT_STAGES + s]);
-            if (!mbar_wait(bar, (phase_bits >> s) & 1u)) {
-                // record the failure, then drain this warp's other copies (bounded) and leave
+            if (!mbar_wait(bar0 + 8 * s, (phase_bits >> s) & 1u)) {
                 if (lane == 0) {
                     atomicExch(a.err, (int)TQ_ERROR_TIMEOUT);
-                    s_abort = 1;
+                    *s_abort = 1;
                 }
-                for (int j = i + 1; j < ntiles && j < i + ATT_STAGES; ++j) {
-                    const int sj = j % ATT_STAGES;
-                    mbar_wait(smem_u32(&bars[warp * ATT_STAGES + sj]), (phase_bits >> sj) & 1u);
-                }
-                timed_out = true;
+                for (int j = i + 1; j < ntiles && j < i + ATT_STAGES; ++j)
+                    mbar_wait(bar0 + 8 * (j % ATT_STAGES), (phase_bits >> (j % ATT_STAGES)) & 1u);
                 break;
             }
             phase_bits ^= 1u << s;
-            const uint8_t* kt = my_stage + s * (KTILE + VTILE);
-            const uint8_t* vt = kt + KTILE;
-            const int64_t t0 = t_begin + (int64_t)i * ATT_TILE;
-            const int valid = (int)((t_end - t0) < ATT_TILE ? (t_end - t0) : ATT_TILE);
+            const uint32_t st = stage0 + s * STAGE;
+            const int64_t tt = t0 + (int64_t)(warp + i * ATT_WARPS) * ATT_TILE;
+            const int valid = (int)(t1 - tt < ATT_TILE ? t1 - tt : ATT_TILE);
 
-            // block scales of this tile: K as fp32 [tok][blk], V as fp16 bits [blk][tok]
-            for (int j = lane; j < ATT_TILE * NBLK; j += 32) {
-                const int tok = j / NBLK, blk = j % NBLK;
-                const uint32_t hk = (uint32_t)kt[tok * KB + blk * TQ4_BYTES] |
-                                    ((uint32_t)kt[tok * KB + blk * TQ4_BYTES + 1] << 8);
-                const uint32_t hv = (uint32_t)vt[tok * VB + blk * TQ4_BYTES] |
-                                    ((uint32_t)vt[tok * VB + blk * TQ4_BYTES + 1] << 8);
-                my_dk[tok * NBLK + blk] = tok < valid ? half_decode(hk) : 0.0f;
-                if (tok < valid && (hv & 0x7C00u) == 0x7C00u) atomicExch(a.err, (int)TQ_ERROR_UNSUPPORTED);
-                my_dv[blk * ATT_TILE + tok] = tok < valid ? (uint16_t)hv : (uint16_t)0;
+            // block scales: K -> f32 [tok][blk], V -> f16 bits [blk][tok]; tokens past the
+            // valid range (stale or never-written stage bytes) get scale 0
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const bool xv = x_tok + 8 * (r & 1) < valid;
+                uint16_t h;
+                asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(st + x_src[r]));
+                h = xv ? h : (uint16_t)0;
+                // exponent 31 (|x| >= 65536) decodes as a finite value in the reference but as
+                // inf/nan in IEEE fp16 arithmetic: reported, not computed with
+                if ((h & 0x7C00u) == 0x7C00u) atomicExch(a.err, (int)TQ_ERROR_UNSUPPORTED);
+                if (r < 2) {
+                    const float f = __half2float(__ushort_as_half(h));
+                    asm volatile("st.shared.f32 [%0], %1;" ::"r"(scr + x_dst[r]), "f"(f));
+                } else {
+                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(scr + x_dst[r]), "h"(h));
+                }
             }
             __syncwarp();
 
-            // ---- S = K q~^T (16 tokens x 8 heads) ----
+            // ---- S = K q~^T ----
             float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            const uint32_t krow0 = smem_u32(kt) + gq * KB, krow1 = krow0 + 8 * KB;
-#pragma unroll
-            for (int blk = 0; blk < NBLK; ++blk) {
-                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint32_t off = blk * TQ4_BYTES + 2 + 8 * h + 2 * tq;
-                    const uint32_t w0 = lds_u16(krow0 + off), w1 = lds_u16(krow1 + off);
-                    uint32_t af[4];
-                    af[0] = lds_u32(lut_base + lut_addr(w0, lane4, LUT_SEL0));
-                    af[1] = lds_u32(lut_base + lut_addr(w1, lane4, LUT_SEL0));
-                    af[2] = lds_u32(lut_base + lut_addr(w0, lane4, LUT_SEL1));
-                    af[3] = lds_u32(lut_base + lut_addr(w1, lane4, LUT_SEL1));
-                    mma16816(acc, af, qf[2 * blk + h][0], qf[2 * blk + h][1]);
-                }
-                const float d0 = my_dk[gq * NBLK + blk], d1 = my_dk[(gq + 8) * NBLK + blk];
-                sc[0] = fmaf(d0, acc[0], sc[0]);
-                sc[1] = fmaf(d0, acc[1], sc[1]);
-                sc[2] = fmaf(d1, acc[2], sc[2]);
-                sc[3] = fmaf(d1, acc[3], sc[3]);
-            }
-            // mask tokens beyond the valid range
+            const uint32_t kr = st + k_off;
+            const float4 dk0 = ld128f<0>(scr + gq * 16), dk1 = ld128f<8 * 16>(scr + gq * 16);
+            const float dka[4] = {dk0.x, dk0.y, dk0.z, dk0.w}, dkb[4] = {dk1.x, dk1.y, dk1.z, dk1.w};
+            static_for<0, NBLK>([&](auto blk_c) {
+                constexpr int blk = decltype(blk_c)::value;
+                float acc[4];
+                uint32_t w0, w1;
+                uint32_t af[4];
+#define TQ_KCHUNK(H, FIRST)                                                            \
+                w0 = ld16<blk * TQ4_BYTES + 8 * (H)>(kr);                              \
+                w1 = ld16<blk * TQ4_BYTES + 8 * (H) + 8 * KB>(kr);                     \
+                af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);                              \
+                af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);                              \
+                af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);                              \
+                af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);                              \
+                if (FIRST) mma16816_zc(acc, af, qf[2 * blk + (H)][0], qf[2 * blk + (H)][1]); \
+                else mma16816(acc, af, qf[2 * blk + (H)][0], qf[2 * blk + (H)][1]);
+                TQ_KCHUNK(0, true)
+                TQ_KCHUNK(1, false)
+#undef TQ_KCHUNK
+                sc[0] = fmaf(dka[blk], acc[0], sc[0]);
+                sc[1] = fmaf(dka[blk], acc[1], sc[1]);
+                sc[2] = fmaf(dkb[blk], acc[2], sc[2]);
+                sc[3] = fmaf(dkb[blk], acc[3], sc[3]);
+            });
             if (gq >= valid) { sc[0] = -INFINITY; sc[1] = -INFINITY; }
             if (gq + 8 >= valid) { sc[2] = -INFINITY; sc[3] = -INFINITY; }
 
-            // ---- online softmax (log2 domain; heads 2tq, 2tq+1 per lane) ----
+            // ---- online softmax (log2 domain) ----
             float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
 #pragma unroll
             for (int sh = 4; sh < 32; sh <<= 1) {
                 mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
                 mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, sh));
             }
-            const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
-            const float al0 = mn0 == -INFINITY ? 1.0f : ex2(m_run[0] - mn0);
-            const float al1 = mn1 == -INFINITY ? 1.0f : ex2(m_run[1] - mn1);
-            m_run[0] = mn0;
-            m_run[1] = mn1;
-            if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {
+            if (__any_sync(0xffffffffu, mx0 > m_run0 || mx1 > m_run1)) {
+                const float mn0 = fmaxf(m_run0, mx0), mn1 = fmaxf(m_run1, mx1);
+                const float al0 = ex2(m_run0 - mn0), al1 = ex2(m_run1 - mn1);
+                m_run0 = mn0;
+                m_run1 = mn1;
 #pragma unroll
                 for (int mt = 0; mt < NMT; ++mt) {
                     o[mt][0] *= al0; o[mt][1] *= al1; o[mt][2] *= al0; o[mt][3] *= al1;
                 }
-                l_run[0] *= al0;
-                l_run[1] *= al1;
+                l0 *= al0;
+                l1 *= al1;
             }
-            const float p0 = mn0 == -INFINITY ? 0.0f : ex2(sc[0] - mn0);
-            const float p1 = mn1 == -INFINITY ? 0.0f : ex2(sc[1] - mn1);
-            const float p2 = mn0 == -INFINITY ? 0.0f : ex2(sc[2] - mn0);
-            const float p3 = mn1 == -INFINITY ? 0.0f : ex2(sc[3] - mn1);
-            l_run[0] += p0 + p2;
-            l_run[1] += p1 + p3;
-            // P^T as the mma B operand: lane (g, t) gets head g, tokens (2t, 2t+1) and (2t+8, 2t+9)
+            const float p0 = ex2(sc[0] - m_run0), p1 = ex2(sc[1] - m_run1);
+            const float p2 = ex2(sc[2] - m_run0), p3 = ex2(sc[3] - m_run1);
+            l0 += p0 + p2;
+            l1 += p1 + p3;
             const uint32_t pb01 = movmatrix_t(pack_h2(p0, p1));
             const uint32_t pb23 = movmatrix_t(pack_h2(p2, p3));
 
             // ---- O^T += V^T P' ----
-            const uint32_t vtok0 = smem_u32(vt) + (2 * tq) * VB, vtok1 = vtok0 + VB;
-            const uint32_t vtok2 = vtok0 + 8 * VB, vtok3 = vtok2 + VB;
-#pragma unroll
-            for (int blk = 0; blk < NBLK; ++blk) {
-                const uint32_t off = blk * TQ4_BYTES + 2 + 2 * gq;
-                const uint32_t w0 = lds_u16(vtok0 + off), w1 = lds_u16(vtok1 + off);
-                const uint32_t w2 = lds_u16(vtok2 + off), w3 = lds_u16(vtok3 + off);
-                // bytes [B0(t), B0(t+1), B1(t), B1(t+1)] for the token pairs (2t,2t+1), (2t+8,2t+9)
+            const uint32_t vr = st + KTILE + v_off;
+            const uint32_t sdv = scr + ATT_TILE * NBLK * 4 + 4 * tq;
+            static_for<0, NBLK>([&](auto blk_c) {
+                constexpr int blk = decltype(blk_c)::value;
+                const uint32_t w0 = ld16<blk * TQ4_BYTES>(vr), w1 = ld16<blk * TQ4_BYTES + VB>(vr);
+                const uint32_t w2 = ld16<blk * TQ4_BYTES + 8 * VB>(vr), w3 = ld16<blk * TQ4_BYTES + 9 * VB>(vr);
                 const uint32_t ra = prmt(w0, w1, 0x5140u), rb = prmt(w2, w3, 0x5140u);
                 const uint32_t ra4 = ra >> 4, rb4 = rb >> 4;
-                const uint32_t xa = (ra & 0x000F000Fu) | (ra4 & 0x00F000F0u);   // lo nibbles, byte 0 / 2
-                const uint32_t ya = (ra4 & 0x000F000Fu) | ((ra >> 8) & 0x00F000F0u);   // hi nibbles
+                const uint32_t xa = (ra & 0x000F000Fu) | (ra4 & 0x00F000F0u);
+                const uint32_t ya = (ra4 & 0x000F000Fu) | ((ra >> 8) & 0x00F000F0u);
                 const uint32_t xb = (rb & 0x000F000Fu) | (rb4 & 0x00F000F0u);
                 const uint32_t yb = (rb4 & 0x000F000Fu) | ((rb >> 8) & 0x00F000F0u);
-                // V scales of this block for the lane's token pairs, folded into P
-                const uint32_t dv01 = *reinterpret_cast<const uint32_t*>(my_dv + blk * ATT_TILE + 2 * tq);
-                const uint32_t dv89 = *reinterpret_cast<const uint32_t*>(my_dv + blk * ATT_TILE + 2 * tq + 8);
-                const uint32_t b0 = h2_mul(pb01, dv01), b1 = h2_mul(pb23, dv89);
-#pragma unroll
-                for (int par = 0; par < 2; ++par) {
-                    const uint32_t sel = par ? LUT_SEL2 : LUT_SEL0;
-                    uint32_t af[4];
-                    af[0] = lds_u32(lut_base + lut_addr(xa, lane4, sel));   // row g, tokens 2t, 2t+1
-                    af[1] = lds_u32(lut_base + lut_addr(ya, lane4, sel));   // row g+8
-                    af[2] = lds_u32(lut_base + lut_addr(xb, lane4, sel));   // row g, tokens 2t+8, 2t+9
-                    af[3] = lds_u32(lut_base + lut_addr(yb, lane4, sel));   // row g+8
-                    mma16816(o[2 * blk + par], af, b0, b1);
-                }
-            }
-            __syncwarp();   // stage s and the scale scratch are free for reuse
+                const uint32_t b0 = h2_mul(pb01, ld32<blk * ATT_TILE * 2>(sdv));
+                const uint32_t b1 = h2_mul(pb23, ld32<blk * ATT_TILE * 2 + 16>(sdv));
+                uint32_t af[4];
+                af[0] = lut_ld<RES>(xa, lane4, LUT_SEL0);
+                af[1] = lut_ld<RES>(ya, lane4, LUT_SEL0);
+                af[2] = lut_ld<RES>(xb, lane4, LUT_SEL0);
+                af[3] = lut_ld<RES>(yb, lane4, LUT_SEL0);
+                mma16816(o[2 * blk], af, b0, b1);
+                af[0] = lut_ld<RES>(xa, lane4, LUT_SEL2);
+                af[1] = lut_ld<RES>(ya, lane4, LUT_SEL2);
+                af[2] = lut_ld<RES>(xb, lane4, LUT_SEL2);
+                af[3] = lut_ld<RES>(yb, lane4, LUT_SEL2);
+                mma16816(o[2 * blk + 1], af, b0, b1);
+            });
+            __syncwarp();   // stage s and the scratch may be overwritten from here on
         }
 
-        // ---- merge the 16 warps of this CTA, write the split partial ----
-        float l0 = l_run[0], l1 = l_run[1];
+        // ---- merge the 16 warps, write the (pair, slot) partial ----
 #pragma unroll
         for (int sh = 4; sh < 32; sh <<= 1) {
             l0 += __shfl_xor_sync(0xffffffffu, l0, sh);
             l1 += __shfl_xor_sync(0xffffffffu, l1, sh);
         }
-        (void)timed_out;
-        __syncthreads();   // every warp is done with its stages; reuse them as scratch
-        if (s_abort) return;   // uniform: every thread reads the flag after the barrier
+        __syncthreads();   // all warps done with their stages; reuse them as merge scratch
+        if (*s_abort) return;
         float* red = reinterpret_cast<float*>(stages);   // [warp][ATT_N][D + 2]
         float* mine = red + warp * ATT_N * (D + 2);
         if (gq == 0) {
-            mine[(2 * tq) * (D + 2) + 0] = m_run[0];
-            mine[(2 * tq + 1) * (D + 2) + 0] = m_run[1];
+            mine[(2 * tq) * (D + 2) + 0] = m_run0;
+            mine[(2 * tq + 1) * (D + 2) + 0] = m_run1;
             mine[(2 * tq) * (D + 2) + 1] = l0;
             mine[(2 * tq + 1) * (D + 2) + 1] = l1;
         }
@@ -457,23 +528,20 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
             mine[(2 * tq + 1) * (D + 2) + 2 + e0 + 16] = o[mt][3];
         }
         __syncthreads();
-        float* dst = a.part + (size_t)item * ATT_N * (D + 2);
+        float* dst = a.part + ((size_t)pair * a.slots + slot) * ATT_N * (D + 2);
         for (int idx = threadIdx.x; idx < ATT_N * (D + 2); idx += ATT_THREADS) {
             const int h = idx / (D + 2), c = idx % (D + 2);
-            float M = -INFINITY;
+            float M = M_FLOOR;
             for (int w = 0; w < ATT_WARPS; ++w) M = fmaxf(M, red[w * ATT_N * (D + 2) + h * (D + 2)]);
-            float acc = 0.0f;
-            if (c == 0) {
-                acc = M;
-            } else if (M != -INFINITY) {
-                for (int w = 0; w < ATT_WARPS; ++w) {
-                    const float mw = red[w * ATT_N * (D + 2) + h * (D + 2)];
-                    if (mw != -INFINITY) acc += ex2(mw - M) * red[w * ATT_N * (D + 2) + idx];
-                }
+            float acc = M;
+            if (c > 0) {
+                acc = 0.0f;
+                for (int w = 0; w < ATT_WARPS; ++w)
+                    acc += ex2(red[w * ATT_N * (D + 2) + h * (D + 2)] - M) * red[w * ATT_N * (D + 2) + idx];
             }
             dst[idx] = acc;
         }
-        __syncthreads();   // scratch (= stages) free before the next item
+        __syncthreads();   // scratch (= stages) free before the next segment's copies
     }
 }
 
@@ -487,29 +555,27 @@ template <> __device__ __forceinline__ void store_out<__nv_bfloat16>(__nv_bfloat
 template <typename OT, int D>
 __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restrict__ part, OT* __restrict__ out,
                                                            float* __restrict__ lse, int Hq, int Hkv, int grp,
-                                                           int splits, int v_rotated, float fwht_norm) {
+                                                           int slots, int64_t lnom, int64_t chunk, int v_rotated,
+                                                           float fwht_norm) {
     __shared__ float so[D];
-    __shared__ float sw[64];
     const int bh = blockIdx.x;             // sequence * Hq + head
     const int b = bh / Hq, h = bh % Hq;
     const int g = h / grp, hh = h % grp;
     const int64_t pair = (int64_t)b * Hkv + g;
-    const float* p0 = part + ((size_t)pair * splits) * ATT_N * (D + 2) + hh * (D + 2);
+    // the CTAs whose chunks intersect this pair wrote slots 0 .. nslot-1
+    const int64_t c_first = (pair * lnom) / chunk, c_last = ((pair + 1) * lnom - 1) / chunk;
+    const int nslot = (int)(c_last - c_first + 1);
     const size_t sstride = (size_t)ATT_N * (D + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < splits; ++s) M = fmaxf(M, p0[s * sstride]);
+    const float* p0 = part + (size_t)pair * slots * sstride + hh * (D + 2);
+    float M = M_FLOOR;
+    for (int s = 0; s < nslot; ++s) M = fmaxf(M, p0[s * sstride]);
     float L = 0.0f;
-    for (int s = 0; s < splits; ++s) {
-        const float ms = p0[s * sstride];
-        if (ms != -INFINITY) L += ex2(ms - M) * p0[s * sstride + 1];
-    }
+    for (int s = 0; s < nslot; ++s) L += ex2(p0[s * sstride] - M) * p0[s * sstride + 1];
+    const bool empty = !(L > 0.0f);
     for (int e = threadIdx.x; e < D; e += 128) {
         float acc = 0.0f;
-        if (M != -INFINITY) {
-            for (int s = 0; s < splits; ++s) {
-                const float ms = p0[s * sstride];
-                if (ms != -INFINITY) acc += ex2(ms - M) * p0[s * sstride + 2 + e];
-            }
+        if (!empty) {
+            for (int s = 0; s < nslot; ++s) acc += ex2(p0[s * sstride] - M) * p0[s * sstride + 2 + e];
             acc /= L;
         }
         so[e] = acc;
@@ -528,9 +594,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restri
         }
     }
     for (int e = threadIdx.x; e < D; e += 128) store_out<OT>(out + (size_t)bh * D + e, v_rotated ? so[e] * fwht_norm : so[e]);
-    if (lse && threadIdx.x == 0)
-        lse[bh] = M == -INFINITY ? -INFINITY : (M + __log2f(L)) * 0.6931471805599453f;
-    (void)sw;
+    if (lse && threadIdx.x == 0) lse[bh] = empty ? -INFINITY : (M + __log2f(L)) * 0.6931471805599453f;
 }
 
 // log-sum-exp merge of P partial results (natural-log lse), e.g. from several ranks
@@ -565,35 +629,30 @@ static size_t decode_smem_bytes() {
     constexpr int KB = (KT == 4 ? TQ4_BYTES : TQ3_BYTES) * NBLK;
     constexpr int VB = (VT == 4 ? TQ4_BYTES : TQ3_BYTES) * NBLK;
     size_t s = LUT_BYTES;
-    s += (size_t)ATT_WARPS * ATT_STAGES * ATT_TILE * (KB + VB);
-    s += (size_t)ATT_WARPS * ATT_TILE * NBLK * 4;
-    s += (size_t)ATT_WARPS * NBLK * ATT_TILE * 2;
-    s += (size_t)ATT_WARPS * ATT_STAGES * 8;
-    const size_t red = (size_t)ATT_WARPS * ATT_N * (D + 2) * 4;   // warp merge scratch reuses the stages
     const size_t stg = (size_t)ATT_WARPS * ATT_STAGES * ATT_TILE * (KB + VB);
-    if (red > stg) s += red - stg;
+    const size_t red = (size_t)ATT_WARPS * ATT_N * (D + 2) * 4;   // warp merge scratch reuses the stages
+    s += stg > red ? stg : red;
+    s += (size_t)ATT_WARPS * (ATT_TILE * NBLK * 4 + NBLK * ATT_TILE * 2);
+    s += (size_t)ATT_WARPS * ATT_STAGES * 8;
+    s += 16;
     return s;
 }
 
 AttnPlan attn_plan(int B, int Hkv, int64_t cap, int64_t max_len) {
     AttnPlan p;
     const int64_t pairs = (int64_t)B * Hkv;
-    const int sms = sm_count();
-    const int64_t unit = ATT_WARPS * ATT_TILE;                 // 256 tokens
     const int64_t len = max_len > 0 ? max_len : cap;
-    // enough (pair, split) items for a few waves over the SMs, splits of >= 1024 tokens
-    int64_t want = (int64_t)sms * 4;
-    int64_t splits = (want + pairs - 1) / pairs;
-    int64_t max_splits = (len + 4 * unit - 1) / (4 * unit);
-    if (splits > max_splits) splits = max_splits;
-    if (splits < 1) splits = 1;
-    int64_t st = (len + splits - 1) / splits;
-    st = (st + unit - 1) / unit * unit;
-    splits = (len + st - 1) / st;
-    if (splits < 1) splits = 1;
-    p.splits = (int)splits;
-    p.split_tokens = st;
-    p.part_bytes = (size_t)pairs * splits * ATT_N * 130 * sizeof(float);   // refined by D below
+    p.lnom = (len + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
+    if (p.lnom == 0) p.lnom = ATT_TILE;
+    const int64_t total = pairs * p.lnom;
+    const int64_t unit = ATT_WARPS * ATT_TILE;
+    const int sms = sm_count();
+    int64_t chunk = (total + sms - 1) / sms;
+    chunk = (chunk + unit - 1) / unit * unit;
+    if (chunk < unit) chunk = unit;
+    p.chunk = chunk;
+    p.grid = (int)((total + chunk - 1) / chunk);
+    p.slots = (int)((p.lnom + chunk - 1) / chunk + 1);
     return p;
 }
 
@@ -602,8 +661,23 @@ size_t attn_workspace_bytes(int B, int Hkv, int D, const AttnPlan& p) {
     size_t bytes = 256;                                           // error word (+ alignment)
     bytes += pairs * (D / 16) * 64 * sizeof(uint32_t);            // q fragments
     bytes = (bytes + 255) & ~size_t(255);
-    bytes += pairs * p.splits * ATT_N * (D + 2) * sizeof(float);  // split partials
+    bytes += pairs * p.slots * ATT_N * (D + 2) * sizeof(float);   // split partials
     return bytes;
+}
+
+static int reserved_smem() {
+    static int cached[64];
+    static bool init[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!init[dev]) {
+        int v = -1;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess) v = -1;
+        cached[dev] = v;
+        init[dev] = true;
+    }
+    return cached[dev];
 }
 
 template <typename QT, int D>
@@ -615,9 +689,19 @@ static cudaError_t launch_qprep(const void* q, uint32_t* qfrag, int B, int Hq, i
 
 template <typename OT, int D>
 static cudaError_t launch_combine(const float* part, void* out, float* lse, int B, int Hq, int Hkv, int grp,
-                                  int splits, int v_rotated, cudaStream_t st) {
-    attn_combine_kernel<OT, D><<<B * Hq, 128, 0, st>>>(part, (OT*)out, lse, Hq, Hkv, grp, splits, v_rotated,
-                                                        fwht_norm(D));
+                                  const AttnPlan& p, int v_rotated, cudaStream_t st) {
+    attn_combine_kernel<OT, D><<<B * Hq, 128, 0, st>>>(part, (OT*)out, lse, Hq, Hkv, grp, p.slots, p.lnom,
+                                                        p.chunk, v_rotated, fwht_norm(D));
+    return cudaGetLastError();
+}
+
+template <int D, int RES>
+static cudaError_t launch_decode_kernel(const AttnKernelArgs& a, int grid, cudaStream_t st) {
+    const size_t smem = decode_smem_bytes<D, 4, 4>();
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, 4, 4, RES>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attn_decode_kernel<D, 4, 4, RES><<<grid, ATT_THREADS, smem, st>>>(a);
     return cudaGetLastError();
 }
 
@@ -646,23 +730,20 @@ static cudaError_t run_decode(const AttnRun& r, const AttnPlan& p, uint8_t* ws, 
     a.part = part;
     a.err = err;
     a.cap = r.cap;
-    a.split_tokens = p.split_tokens;
+    a.lnom = p.lnom;
+    a.chunk = p.chunk;
     a.B = r.B;
     a.Hkv = r.Hkv;
-    a.grp = r.grp;
-    a.splits = p.splits;
-    const size_t smem = decode_smem_bytes<D, 4, 4>();
-    e = cudaFuncSetAttribute(attn_decode_kernel<D, 4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    const int64_t items = (int64_t)r.B * r.Hkv * p.splits;
-    const int grid = (int)(items < sm_count() ? items : sm_count());
-    attn_decode_kernel<D, 4, 4><<<grid, ATT_THREADS, smem, st>>>(a);
-    e = cudaGetLastError();
+    a.slots = p.slots;
+    const int res = reserved_smem();
+    if (res == 0) e = launch_decode_kernel<D, 0>(a, p.grid, st);
+    else if (res == 1024) e = launch_decode_kernel<D, 1024>(a, p.grid, st);
+    else return cudaErrorNotSupported;
     if (e != cudaSuccess) return e;
     switch (r.out_dtype) {
-        case DT_F32: return launch_combine<float, D>(part, r.out, r.lse, r.B, r.Hq, r.Hkv, r.grp, p.splits, r.v_rotated, st);
-        case DT_F16: return launch_combine<__half, D>(part, r.out, r.lse, r.B, r.Hq, r.Hkv, r.grp, p.splits, r.v_rotated, st);
-        default: return launch_combine<__nv_bfloat16, D>(part, r.out, r.lse, r.B, r.Hq, r.Hkv, r.grp, p.splits, r.v_rotated, st);
+        case DT_F32: return launch_combine<float, D>(part, r.out, r.lse, r.B, r.Hq, r.Hkv, r.grp, p, r.v_rotated, st);
+        case DT_F16: return launch_combine<__half, D>(part, r.out, r.lse, r.B, r.Hq, r.Hkv, r.grp, p, r.v_rotated, st);
+        default: return launch_combine<__nv_bfloat16, D>(part, r.out, r.lse, r.B, r.Hq, r.Hkv, r.grp, p, r.v_rotated, st);
     }
 }
 

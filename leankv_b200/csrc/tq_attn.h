@@ -8,9 +8,10 @@
 namespace tq {
 
 struct AttnPlan {
-    int splits = 1;              // token splits per (sequence, KV head)
-    int64_t split_tokens = 0;    // tokens per split (multiple of 256)
-    size_t part_bytes = 0;
+    int64_t lnom = 0;            // nominal tokens per (sequence, KV head), multiple of 16
+    int64_t chunk = 0;           // tokens per CTA (multiple of 256)
+    int grid = 0;                // CTAs
+    int slots = 0;               // partial slots per (sequence, KV head)
 };
 
 struct AttnRun {

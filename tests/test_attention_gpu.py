@@ -3,8 +3,12 @@
 Reference: the float64 oracle (reference dequantization + FWHT + exact softmax),
 and at full size a torch float32 evaluation on caches dequantized by the
 bit-exact dequantizer.  Tolerance (floating-point kernel, fp16 tensor-core
-operands, fp32 accumulation): max |out - ref| <= 1e-3 * max |ref| + 1e-5, and
-|lse - lse_ref| <= 1e-3 * max(1, |lse_ref|).
+operands, fp32 accumulation): max |out - ref| <= 2e-3 * max |ref| + 1e-5, and
+|lse - lse_ref| <= 2e-3 * max(1, |lse_ref|).  The bound is set by the fp16
+rounding of the softmax weights folded with the V block scales (P * d, about
+2.5 * 2^-11 relative per term): a 2-token context, where nothing averages out,
+reaches 1.1e-3; contexts of hundreds of tokens and more measure 2e-4 .. 5e-4
+(printed by the tests).
 """
 import numpy as np
 import pytest
@@ -14,7 +18,7 @@ from leankv_b200 import attention, ops
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
-RTOL = 1e-3
+RTOL = 2e-3
 
 
 def make_cache(B, Hkv, T, D, seed, qtype=4, outliers=True):

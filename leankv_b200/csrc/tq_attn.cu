@@ -322,16 +322,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
     const uint32_t scr = smem_u32(scratch + warp * SCR);               // dK f32 [16][4] | dV f16 [4][16]
     const uint32_t bar0 = smem_u32(&bars[warp * ATT_STAGES]);
     // per-lane fixed offsets
-    const uint32_t k_off = gq * KB + 2 * tq + 2;                        // + blk*18 + 8h (+ 8 tokens)
-    const uint32_t v_off = (2 * tq) * VB + 2 * gq + 2;                   // + tok {0,1,8,9} + blk*18
+    // Token order inside a 16-token tile: mma row / k index r holds token pi(r) = 2r (r < 8),
+    // 2(r-8)+1 (r >= 8).  With the 72-byte token pitch this makes both the K loads (rows g,
+    // g+8 -> tokens 2g, 2g+1) and the V loads (k = 2t, 2t+1, 2t+8, 2t+9 -> tokens 4t, 4t+2,
+    // 4t+1, 4t+3) hit distinct banks; the softmax sum over tokens is order-free.
+    const uint32_t k_off = (2 * gq) * KB + 2 * tq + 2;                  // + blk*18 + 8h (+1 token: row g+8)
+    const uint32_t v_off = (4 * tq) * VB + 2 * gq + 2;                   // + tok {0,2,1,3} + blk*18
     // scale extraction: lane handles entries e = lane + 32 r, r = 0..3 (0..63 K, 64..127 V)
     uint32_t x_src[4], x_dst[4];
     const int x_tok = lane >> 2;              // token of entries r = 0, 2; entries r = 1, 3 hold token + 8
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
         const int e = lane + 32 * r, isv = e >= 64, ee = e & 63, tok = ee >> 2, blk = ee & 3;
+        const int row = (tok & 1) ? 8 + (tok >> 1) : (tok >> 1);      // pi^-1(tok)
         x_src[r] = (isv ? KTILE + tok * VB : tok * KB) + blk * TQ4_BYTES;
-        x_dst[r] = isv ? ATT_TILE * NBLK * 4 + (blk * ATT_TILE + tok) * 2 : (tok * NBLK + blk) * 4;
+        x_dst[r] = isv ? ATT_TILE * NBLK * 4 + (blk * ATT_TILE + row) * 2 : (row * NBLK + blk) * 4;
     }
     uint32_t phase_bits = 0;
 
@@ -369,139 +374,164 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
         for (int mt = 0; mt < NMT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
         float m_run0 = M_FLOOR, m_run1 = M_FLOOR, l0 = 0.0f, l1 = 0.0f;
 
-        auto issue = [&](int i) {
-            const int64_t t = t0 + (int64_t)(warp + i * ATT_WARPS) * ATT_TILE;
-            int64_t nt = a.cap - t;
-            if (nt > ATT_TILE) nt = ATT_TILE;
-            const int s = i % ATT_STAGES;
-            const uint32_t dst = stage0 + s * STAGE;
-            bulk_issue(lane == 0 && i < ntiles, dst, kbase + t * KB, (uint32_t)(nt * KB), dst + KTILE,
-                       vbase + t * VB, (uint32_t)(nt * VB), bar0 + 8 * s);
+        // copy sources advance by one CTA tile row (16 warps x 16 tokens) per warp tile
+        const uint8_t* ksrc = kbase + (t0 + (int64_t)warp * ATT_TILE) * KB;
+        const uint8_t* vsrc = vbase + (t0 + (int64_t)warp * ATT_TILE) * VB;
+        const int64_t tok_first = t0 + (int64_t)warp * ATT_TILE;      // first token of tile 0
+        // tokens of the last tile that exist in memory (capacity), for the copy size
+        const int64_t t_last = tok_first + (int64_t)(ntiles > 0 ? ntiles - 1 : 0) * ATT_WARPS * ATT_TILE;
+        const uint32_t last_nt = (uint32_t)(a.cap - t_last < ATT_TILE ? a.cap - t_last : ATT_TILE);
+        // tokens of the last tile below the valid length (tiles before it are full)
+        const int last_valid = (int)(t1 - t_last < ATT_TILE ? t1 - t_last : ATT_TILE);
+        int issued = 0;
+        auto issue_next = [&](auto stage_c) {
+            constexpr int S = decltype(stage_c)::value;
+            const bool last = issued == ntiles - 1;
+            const uint32_t nt = last ? last_nt : (uint32_t)ATT_TILE;
+            bulk_issue(lane == 0 && issued < ntiles, stage0 + S * STAGE, ksrc, nt * KB, stage0 + S * STAGE + KTILE,
+                       vsrc, nt * VB, bar0 + 8 * S);
+            ksrc += (size_t)ATT_WARPS * ATT_TILE * KB;
+            vsrc += (size_t)ATT_WARPS * ATT_TILE * VB;
+            ++issued;
         };
-        for (int i = 0; i < ATT_STAGES - 1; ++i) issue(i);
+        static_for<0, ATT_STAGES - 1>([&](auto sc) { issue_next(sc); });
 
-        for (int i = 0; i < ntiles; ++i) {
-            issue(i + ATT_STAGES - 1);
-            const int s = i % ATT_STAGES;
-            if (!mbar_wait(bar0 + 8 * s, (phase_bits >> s) & 1u)) {
-                if (lane == 0) {
-                    atomicExch(a.err, (int)TQ_ERROR_TIMEOUT);
-                    *s_abort = 1;
+        uint32_t bad_scale = 0;
+        bool timed_out = false;
+        for (int i0 = 0; i0 < ntiles && !timed_out; i0 += ATT_STAGES) {
+            static_for<0, ATT_STAGES>([&](auto stage_c) {
+                constexpr int S = decltype(stage_c)::value;
+                const int i = i0 + S;
+                if (i >= ntiles || timed_out) return;
+                issue_next(std::integral_constant<int, (S + ATT_STAGES - 1) % ATT_STAGES>{});
+                if (!mbar_wait(bar0 + 8 * S, (phase_bits >> S) & 1u)) {
+                    timed_out = true;
+                    return;
                 }
-                for (int j = i + 1; j < ntiles && j < i + ATT_STAGES; ++j)
-                    mbar_wait(bar0 + 8 * (j % ATT_STAGES), (phase_bits >> (j % ATT_STAGES)) & 1u);
-                break;
-            }
-            phase_bits ^= 1u << s;
-            const uint32_t st = stage0 + s * STAGE;
-            const int64_t tt = t0 + (int64_t)(warp + i * ATT_WARPS) * ATT_TILE;
-            const int valid = (int)(t1 - tt < ATT_TILE ? t1 - tt : ATT_TILE);
+                phase_bits ^= 1u << S;
+                const uint32_t st = stage0 + S * STAGE;
+                const int valid = i == ntiles - 1 ? last_valid : ATT_TILE;
 
-            // block scales: K -> f32 [tok][blk], V -> f16 bits [blk][tok]; tokens past the
-            // valid range (stale or never-written stage bytes) get scale 0
+                // block scales: K -> f32 [tok][blk], V -> f16 bits [blk][tok]; tokens past the
+                // valid range (stale or never-written stage bytes) get scale 0
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const bool xv = x_tok + 8 * (r & 1) < valid;
-                uint16_t h;
-                asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(st + x_src[r]));
-                h = xv ? h : (uint16_t)0;
-                // exponent 31 (|x| >= 65536) decodes as a finite value in the reference but as
-                // inf/nan in IEEE fp16 arithmetic: reported, not computed with
-                if ((h & 0x7C00u) == 0x7C00u) atomicExch(a.err, (int)TQ_ERROR_UNSUPPORTED);
-                if (r < 2) {
-                    const float f = __half2float(__ushort_as_half(h));
-                    asm volatile("st.shared.f32 [%0], %1;" ::"r"(scr + x_dst[r]), "f"(f));
-                } else {
-                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(scr + x_dst[r]), "h"(h));
+                for (int r = 0; r < 4; ++r) {
+                    const bool xv = x_tok + 8 * (r & 1) < valid;
+                    uint16_t h;
+                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(st + x_src[r]));
+                    h = xv ? h : (uint16_t)0;
+                    // |d| >= 2^15: exponent 31 decodes as a finite value in the reference but as
+                    // inf/nan in IEEE fp16, and P * d could overflow fp16: reported once per segment
+                    bad_scale |= (h & 0x7C00u) >= 0x7800u;
+                    if (r < 2) {
+                        const float f = __half2float(__ushort_as_half(h));
+                        asm volatile("st.shared.f32 [%0], %1;" ::"r"(scr + x_dst[r]), "f"(f));
+                    } else {
+                        asm volatile("st.shared.u16 [%0], %1;" ::"r"(scr + x_dst[r]), "h"(h));
+                    }
                 }
-            }
-            __syncwarp();
+                __syncwarp();
 
-            // ---- S = K q~^T ----
-            float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            const uint32_t kr = st + k_off;
-            const float4 dk0 = ld128f<0>(scr + gq * 16), dk1 = ld128f<8 * 16>(scr + gq * 16);
-            const float dka[4] = {dk0.x, dk0.y, dk0.z, dk0.w}, dkb[4] = {dk1.x, dk1.y, dk1.z, dk1.w};
-            static_for<0, NBLK>([&](auto blk_c) {
-                constexpr int blk = decltype(blk_c)::value;
-                float acc[4];
-                uint32_t w0, w1;
-                uint32_t af[4];
-#define TQ_KCHUNK(H, FIRST)                                                            \
-                w0 = ld16<blk * TQ4_BYTES + 8 * (H)>(kr);                              \
-                w1 = ld16<blk * TQ4_BYTES + 8 * (H) + 8 * KB>(kr);                     \
-                af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);                              \
-                af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);                              \
-                af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);                              \
-                af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);                              \
-                if (FIRST) mma16816_zc(acc, af, qf[2 * blk + (H)][0], qf[2 * blk + (H)][1]); \
-                else mma16816(acc, af, qf[2 * blk + (H)][0], qf[2 * blk + (H)][1]);
-                TQ_KCHUNK(0, true)
-                TQ_KCHUNK(1, false)
-#undef TQ_KCHUNK
-                sc[0] = fmaf(dka[blk], acc[0], sc[0]);
-                sc[1] = fmaf(dka[blk], acc[1], sc[1]);
-                sc[2] = fmaf(dkb[blk], acc[2], sc[2]);
-                sc[3] = fmaf(dkb[blk], acc[3], sc[3]);
+                // ---- S = K q~^T ----
+                float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                const uint32_t kr = st + k_off;
+                const float4 dk0 = ld128f<0>(scr + gq * 16), dk1 = ld128f<8 * 16>(scr + gq * 16);
+                const float dka[4] = {dk0.x, dk0.y, dk0.z, dk0.w}, dkb[4] = {dk1.x, dk1.y, dk1.z, dk1.w};
+                static_for<0, NBLK>([&](auto blk_c) {
+                    constexpr int blk = decltype(blk_c)::value;
+                    float acc[4];
+                    uint32_t af[4];
+                    uint32_t w0 = ld16<blk * TQ4_BYTES>(kr), w1 = ld16<blk * TQ4_BYTES + KB>(kr);
+                    af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
+                    af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);
+                    af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
+                    af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
+                    mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
+                    w0 = ld16<blk * TQ4_BYTES + 8>(kr);
+                    w1 = ld16<blk * TQ4_BYTES + 8 + KB>(kr);
+                    af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
+                    af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);
+                    af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
+                    af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
+                    mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
+                    sc[0] = fmaf(dka[blk], acc[0], sc[0]);
+                    sc[1] = fmaf(dka[blk], acc[1], sc[1]);
+                    sc[2] = fmaf(dkb[blk], acc[2], sc[2]);
+                    sc[3] = fmaf(dkb[blk], acc[3], sc[3]);
+                });
+                if (valid < ATT_TILE) {
+                    if (2 * gq >= valid) { sc[0] = -INFINITY; sc[1] = -INFINITY; }
+                    if (2 * gq + 1 >= valid) { sc[2] = -INFINITY; sc[3] = -INFINITY; }
+                }
+
+                // ---- online softmax (log2 domain) ----
+                float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+                for (int sh = 4; sh < 32; sh <<= 1) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, sh));
+                }
+                // the running max moves only when a score exceeds it by more than one log2 unit,
+                // so P <= 2 (scales of 2^15 and above are reported as unsupported)
+                if (__any_sync(0xffffffffu, mx0 > m_run0 + 1.0f || mx1 > m_run1 + 1.0f)) {
+                    const float mn0 = fmaxf(m_run0, mx0), mn1 = fmaxf(m_run1, mx1);
+                    const float al0 = ex2(m_run0 - mn0), al1 = ex2(m_run1 - mn1);
+                    m_run0 = mn0;
+                    m_run1 = mn1;
+#pragma unroll
+                    for (int mt = 0; mt < NMT; ++mt) {
+                        o[mt][0] *= al0; o[mt][1] *= al1; o[mt][2] *= al0; o[mt][3] *= al1;
+                    }
+                    l0 *= al0;
+                    l1 *= al1;
+                }
+                const float p0 = ex2(sc[0] - m_run0), p1 = ex2(sc[1] - m_run1);
+                const float p2 = ex2(sc[2] - m_run0), p3 = ex2(sc[3] - m_run1);
+                l0 += p0 + p2;
+                l1 += p1 + p3;
+                const uint32_t pb01 = movmatrix_t(pack_h2(p0, p1));
+                const uint32_t pb23 = movmatrix_t(pack_h2(p2, p3));
+
+                // ---- O^T += V^T P' ----
+                const uint32_t vr = st + KTILE + v_off;
+                const uint32_t sdv = scr + ATT_TILE * NBLK * 4 + 4 * tq;
+                static_for<0, NBLK>([&](auto blk_c) {
+                    constexpr int blk = decltype(blk_c)::value;
+                    const uint32_t w0 = ld16<blk * TQ4_BYTES>(vr), w1 = ld16<blk * TQ4_BYTES + 2 * VB>(vr);
+                    const uint32_t w2 = ld16<blk * TQ4_BYTES + VB>(vr), w3 = ld16<blk * TQ4_BYTES + 3 * VB>(vr);
+                    const uint32_t ra = prmt(w0, w1, 0x5140u), rb = prmt(w2, w3, 0x5140u);
+                    const uint32_t ra4 = ra >> 4, rb4 = rb >> 4;
+                    const uint32_t xa = (ra & 0x000F000Fu) | (ra4 & 0x00F000F0u);
+                    const uint32_t ya = (ra4 & 0x000F000Fu) | ((ra >> 8) & 0x00F000F0u);
+                    const uint32_t xb = (rb & 0x000F000Fu) | (rb4 & 0x00F000F0u);
+                    const uint32_t yb = (rb4 & 0x000F000Fu) | ((rb >> 8) & 0x00F000F0u);
+                    const uint32_t b0 = h2_mul(pb01, ld32<blk * ATT_TILE * 2>(sdv));
+                    const uint32_t b1 = h2_mul(pb23, ld32<blk * ATT_TILE * 2 + 16>(sdv));
+                    uint32_t af[4];
+                    af[0] = lut_ld<RES>(xa, lane4, LUT_SEL0);
+                    af[1] = lut_ld<RES>(ya, lane4, LUT_SEL0);
+                    af[2] = lut_ld<RES>(xb, lane4, LUT_SEL0);
+                    af[3] = lut_ld<RES>(yb, lane4, LUT_SEL0);
+                    mma16816(o[2 * blk], af, b0, b1);
+                    af[0] = lut_ld<RES>(xa, lane4, LUT_SEL2);
+                    af[1] = lut_ld<RES>(ya, lane4, LUT_SEL2);
+                    af[2] = lut_ld<RES>(xb, lane4, LUT_SEL2);
+                    af[3] = lut_ld<RES>(yb, lane4, LUT_SEL2);
+                    mma16816(o[2 * blk + 1], af, b0, b1);
+                });
+                __syncwarp();   // stage S and the scratch may be overwritten from here on
             });
-            if (gq >= valid) { sc[0] = -INFINITY; sc[1] = -INFINITY; }
-            if (gq + 8 >= valid) { sc[2] = -INFINITY; sc[3] = -INFINITY; }
-
-            // ---- online softmax (log2 domain) ----
-            float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
-#pragma unroll
-            for (int sh = 4; sh < 32; sh <<= 1) {
-                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
-                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, sh));
-            }
-            if (__any_sync(0xffffffffu, mx0 > m_run0 || mx1 > m_run1)) {
-                const float mn0 = fmaxf(m_run0, mx0), mn1 = fmaxf(m_run1, mx1);
-                const float al0 = ex2(m_run0 - mn0), al1 = ex2(m_run1 - mn1);
-                m_run0 = mn0;
-                m_run1 = mn1;
-#pragma unroll
-                for (int mt = 0; mt < NMT; ++mt) {
-                    o[mt][0] *= al0; o[mt][1] *= al1; o[mt][2] *= al0; o[mt][3] *= al1;
-                }
-                l0 *= al0;
-                l1 *= al1;
-            }
-            const float p0 = ex2(sc[0] - m_run0), p1 = ex2(sc[1] - m_run1);
-            const float p2 = ex2(sc[2] - m_run0), p3 = ex2(sc[3] - m_run1);
-            l0 += p0 + p2;
-            l1 += p1 + p3;
-            const uint32_t pb01 = movmatrix_t(pack_h2(p0, p1));
-            const uint32_t pb23 = movmatrix_t(pack_h2(p2, p3));
-
-            // ---- O^T += V^T P' ----
-            const uint32_t vr = st + KTILE + v_off;
-            const uint32_t sdv = scr + ATT_TILE * NBLK * 4 + 4 * tq;
-            static_for<0, NBLK>([&](auto blk_c) {
-                constexpr int blk = decltype(blk_c)::value;
-                const uint32_t w0 = ld16<blk * TQ4_BYTES>(vr), w1 = ld16<blk * TQ4_BYTES + VB>(vr);
-                const uint32_t w2 = ld16<blk * TQ4_BYTES + 8 * VB>(vr), w3 = ld16<blk * TQ4_BYTES + 9 * VB>(vr);
-                const uint32_t ra = prmt(w0, w1, 0x5140u), rb = prmt(w2, w3, 0x5140u);
-                const uint32_t ra4 = ra >> 4, rb4 = rb >> 4;
-                const uint32_t xa = (ra & 0x000F000Fu) | (ra4 & 0x00F000F0u);
-                const uint32_t ya = (ra4 & 0x000F000Fu) | ((ra >> 8) & 0x00F000F0u);
-                const uint32_t xb = (rb & 0x000F000Fu) | (rb4 & 0x00F000F0u);
-                const uint32_t yb = (rb4 & 0x000F000Fu) | ((rb >> 8) & 0x00F000F0u);
-                const uint32_t b0 = h2_mul(pb01, ld32<blk * ATT_TILE * 2>(sdv));
-                const uint32_t b1 = h2_mul(pb23, ld32<blk * ATT_TILE * 2 + 16>(sdv));
-                uint32_t af[4];
-                af[0] = lut_ld<RES>(xa, lane4, LUT_SEL0);
-                af[1] = lut_ld<RES>(ya, lane4, LUT_SEL0);
-                af[2] = lut_ld<RES>(xb, lane4, LUT_SEL0);
-                af[3] = lut_ld<RES>(yb, lane4, LUT_SEL0);
-                mma16816(o[2 * blk], af, b0, b1);
-                af[0] = lut_ld<RES>(xa, lane4, LUT_SEL2);
-                af[1] = lut_ld<RES>(ya, lane4, LUT_SEL2);
-                af[2] = lut_ld<RES>(xb, lane4, LUT_SEL2);
-                af[3] = lut_ld<RES>(yb, lane4, LUT_SEL2);
-                mma16816(o[2 * blk + 1], af, b0, b1);
-            });
-            __syncwarp();   // stage s and the scratch may be overwritten from here on
         }
+        if (timed_out) {
+            // record the failure, drain this warp's copies still in flight (bounded), leave
+            if (lane == 0) {
+                atomicExch(a.err, (int)TQ_ERROR_TIMEOUT);
+                *s_abort = 1;
+            }
+#pragma unroll
+            for (int s2 = 0; s2 < ATT_STAGES; ++s2) mbar_wait(bar0 + 8 * s2, (phase_bits >> s2) & 1u);
+        }
+        if (__any_sync(0xffffffffu, bad_scale != 0) && lane == 0) atomicExch(a.err, (int)TQ_ERROR_UNSUPPORTED);
 
         // ---- merge the 16 warps, write the (pair, slot) partial ----
 #pragma unroll

@@ -162,6 +162,25 @@ typedef struct {
 size_t tq_decode_attention_workspace_size(const tq_decode_attention_args *a);
 /* fused decode attention (new; the fork's CUDA FA vec_dot_fattn_vec_KQ_tq* path) */
 tq_status tq_decode_attention_cuda(const tq_decode_attention_args *a, void *stream);
+/*
+ * Allocation-free variant of tq_decode_attention_cuda, for callers that cannot
+ * allocate device memory when they run attention (an allocator-free serving
+ * step, a plugin whose host framework owns all device allocations).  No
+ * counterpart in the reference.  Same arguments and results; a->workspace and
+ * a->workspace_bytes are ignored.  The work memory is a static device array of
+ * TQ_STATIC_SCRATCH_BYTES compiled into the library, which every GPU that
+ * loads the library holds until the process exits.  Arguments that need more
+ * work memory than that (tq_decode_attention_workspace_size) are rejected with
+ * TQ_ERROR_INVALID_VALUE.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress): make that first call before any
+ * stream capture.  All calls share the one array, so calls that can overlap on
+ * the GPU (different streams, or different host threads) race and must be
+ * serialized by the caller.  This entry point calls no cudaMalloc, cudaFree or
+ * other allocating routine.
+ */
+#define TQ_STATIC_SCRATCH_BYTES (16u << 20)
+tq_status tq_decode_attention_static_cuda(const tq_decode_attention_args *a, void *stream);
+
 /* log-sum-exp merge of n_parts partial results o[n_parts][n_rows][head_dim] with
  * natural-log lse[n_parts][n_rows] into out[n_rows][head_dim] (+ lse_out, optional):
  * the split-by-sequence combine of the multi-GPU path (new) */

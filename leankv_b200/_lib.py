@@ -63,6 +63,7 @@ SIGNATURES = {
     # decode attention (argument block pointer; leankv_b200.attention binds the struct type)
     "tq_decode_attention_workspace_size": (C.c_size_t, [_v]),
     "tq_decode_attention_cuda": (_i32, [_v, _v]),
+    "tq_decode_attention_static_cuda": (_i32, [_v, _v]),
     "tq_lse_combine_cuda": (_i32, [_i32, _i64, _i32, _v, _v, _v, _v, _v]),
 }
 

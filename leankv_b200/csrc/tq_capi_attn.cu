@@ -1,5 +1,6 @@
 // tq_capi_attn.cu — extern "C" entry points of the decode attention.
 #include <cmath>
+#include <mutex>
 
 #include "leankv_tq.h"
 #include "tq_attn.h"
@@ -67,4 +68,59 @@ extern "C" tq_status tq_lse_combine_cuda(int n_parts, int64_t n_rows, int head_d
     if (!o || !lse || !out) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
     return cuda_status(launch_lse_combine(o, lse, out, lse_out, n_parts, n_rows, head_dim, (cudaStream_t)stream),
                        "lse combine launch");
+}
+
+// ── fixed-scratch variant ────────────────────────────────────────────────────
+//
+// Some callers cannot allocate device memory at the point where they run
+// decode attention: code that executes inside an allocator-free region (a
+// serving loop that forbids cudaMalloc/cudaFree between steps, a plugin whose
+// host framework owns every allocation, a pre-built execution plan).  This
+// entry point runs the same kernels with their work memory in a static device
+// array compiled into the library, so it allocates nothing.
+//
+// The array's host-side name is only a stand-in for the device object; its
+// device address is looked up once per device with cudaGetSymbolAddress while
+// that device is current.
+
+static __device__ __align__(256) unsigned char g_attn_static_scratch[TQ_STATIC_SCRATCH_BYTES];
+
+static std::mutex g_static_mu;
+static void* g_static_ptr[64];
+static bool g_static_ready[64];
+
+static tq_status static_scratch(void** out) {
+    int dev = 0;
+    tq_status s = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+    if (s) return s;
+    if (dev < 0 || dev >= 64) return set_error(TQ_ERROR_UNSUPPORTED, "device ordinal %d >= 64", dev);
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_ready[dev]) {
+        void* p = nullptr;
+        s = cuda_status(cudaGetSymbolAddress(&p, g_attn_static_scratch), "cudaGetSymbolAddress(static scratch)");
+        if (s) return s;
+        g_static_ptr[dev] = p;
+        g_static_ready[dev] = true;
+    }
+    *out = g_static_ptr[dev];
+    return TQ_SUCCESS;
+}
+
+extern "C" tq_status tq_decode_attention_static_cuda(const tq_decode_attention_args* a, void* stream) {
+    AttnRun r;
+    AttnPlan p;
+    tq_status s = attn_check(a, &r, &p);
+    if (s) return s;
+    if (r.B == 0) return TQ_SUCCESS;
+    const size_t need = attn_workspace_bytes(r.B, r.Hkv, r.D, p);
+    if (need > TQ_STATIC_SCRATCH_BYTES)
+        return set_error(TQ_ERROR_INVALID_VALUE,
+                         "these arguments need %zu bytes of work memory; the fixed scratch holds %zu "
+                         "(use tq_decode_attention_cuda with a caller workspace)",
+                         need, (size_t)TQ_STATIC_SCRATCH_BYTES);
+    void* ws = nullptr;
+    if ((s = static_scratch(&ws))) return s;
+    // the error word is cleared and every partial / q fragment is written before it is read,
+    // so the previous call's contents never leak into this one
+    return cuda_status(launch_decode_attention(r, p, ws, (cudaStream_t)stream), "decode attention launch");
 }

@@ -404,7 +404,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
                 const int i = i0 + S;
                 if (i >= ntiles || timed_out) return;
                 issue_next(std::integral_constant<int, (S + ATT_STAGES - 1) % ATT_STAGES>{});
-                if (!mbar_wait(bar0 + 8 * S, (phase_bits >> S) & 1u)) {
+                // every lane waits; the outcome is made warp-uniform before any warp collective
+                const bool arrived = __all_sync(0xffffffffu, mbar_wait(bar0 + 8 * S, (phase_bits >> S) & 1u));
+                if (!arrived) {
                     timed_out = true;
                     return;
                 }

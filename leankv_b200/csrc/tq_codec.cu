@@ -112,32 +112,51 @@ __device__ __forceinline__ void read_row(const uint8_t* __restrict__ smem, int r
 // Stage h combines elements j and j+h as (x[j] + x[j+h], x[j] - x[j+h]),
 // h = 1, 2, 4, ... (src/ggml-tq.c:365-374), then scales by norm.
 __device__ __forceinline__ void fwht_block(float (&v)[QK], int log2_hd, float norm) {
+    // Packed fp32x2 adds: every lane of an f32x2 operation is an ordinary
+    // round-to-nearest fp32 operation, and a - b is computed as fma(b, -1, a)
+    // (b * -1 is exact, one rounding), so the results equal the scalar code.
+    const float2 m1 = make_float2(-1.0f, -1.0f);
+    if (log2_hd >= 1) {   // h = 1: pairs (j, j+1); two butterflies per packed op
 #pragma unroll
-    for (int s = 0; s < 5; ++s) {
+        for (int j = 0; j < QK; j += 4) {
+            const float2 a = make_float2(v[j], v[j + 2]), b = make_float2(v[j + 1], v[j + 3]);
+            const float2 sum = __fadd2_rn(a, b), dif = __ffma2_rn(b, m1, a);
+            v[j] = sum.x; v[j + 2] = sum.y; v[j + 1] = dif.x; v[j + 3] = dif.y;
+        }
+    }
+#pragma unroll
+    for (int s = 1; s < 5; ++s) {   // h = 2 .. 16: elements j, j+1 share the stage's lower half
         if (s < log2_hd) {
             const int h = 1 << s;
 #pragma unroll
-            for (int j = 0; j < QK; ++j) {
+            for (int j = 0; j < QK; j += 2) {
                 if (j & h) continue;
-                const float a = v[j], b = v[j + h];
-                v[j] = a + b;
-                v[j + h] = a - b;
+                const float2 a = make_float2(v[j], v[j + 1]), b = make_float2(v[j + h], v[j + h + 1]);
+                const float2 sum = __fadd2_rn(a, b), dif = __ffma2_rn(b, m1, a);
+                v[j] = sum.x; v[j + 1] = sum.y; v[j + h] = dif.x; v[j + h + 1] = dif.y;
             }
         }
     }
-    for (int s = 5; s < log2_hd; ++s) {
+    for (int s = 5; s < log2_hd; ++s) {   // h >= 32: partner lane = lane ^ (h / 32)
         const int lane_bit = 1 << (s - 5);
-        const bool upper = (threadIdx.x & lane_bit) != 0;
+        // lower element: self + partner = fma(self, 1, partner); upper: partner - self = fma(self, -1, partner)
+        const float sg = (threadIdx.x & lane_bit) ? -1.0f : 1.0f;
+        const float2 sg2 = make_float2(sg, sg);
 #pragma unroll
-        for (int j = 0; j < QK; ++j) {
-            const float p = __shfl_xor_sync(0xffffffffu, v[j], lane_bit);
-            // lower element: self + partner; upper element: partner - self
-            v[j] = upper ? (p - v[j]) : (v[j] + p);
+        for (int j = 0; j < QK; j += 2) {
+            const float p0 = __shfl_xor_sync(0xffffffffu, v[j], lane_bit);
+            const float p1 = __shfl_xor_sync(0xffffffffu, v[j + 1], lane_bit);
+            const float2 r = __ffma2_rn(make_float2(v[j], v[j + 1]), sg2, make_float2(p0, p1));
+            v[j] = r.x; v[j + 1] = r.y;
         }
     }
     if (log2_hd >= 0) {
+        const float2 n2 = make_float2(norm, norm);
 #pragma unroll
-        for (int j = 0; j < QK; ++j) v[j] = __fmul_rn(v[j], norm);
+        for (int j = 0; j < QK; j += 2) {
+            const float2 r = __fmul2_rn(make_float2(v[j], v[j + 1]), n2);
+            v[j] = r.x; v[j + 1] = r.y;
+        }
     }
 }
 
@@ -176,40 +195,63 @@ __device__ __forceinline__ void store_staged(uint8_t* __restrict__ dst, const ui
 
 // ── TQ3 optimal rounding (scripts/tq3_rounding.py:74-125) ───────────────────
 // Coordinate descent over adjacent levels with a least-squares scale.  For an
-// assignment with Sxl = sum x*L and Sll = sum L^2 the least-squares block MSE
-// is (sum x^2 - Sxl^2 / Sll) / 32, so "new_mse < best_mse" is exactly
-// Sxl'^2 * Sll > Sxl^2 * Sll'.  Sums are float64 over the float64 levels of the
-// Python prototype and are updated incrementally per accepted move.
-struct OptEntry { double lvl, dl_dn, dll_dn, dl_up, dll_up; };
+// assignment with C = sum x*L and A = sum L^2 the least-squares block MSE is
+// (sum x^2 - C^2 / A) / 32, so moving element j by (dL, dLL = L'^2 - L^2)
+// improves the MSE ("new_mse < best_mse") exactly when
+//     T = A * p * (p + 2C) - C^2 * dLL > 0,   p = x_j * dL
+// (that is C'^2 * A > C^2 * A' with C' = C + p, A' = A + dLL).  The levels are
+// the float64 decimals of the Python prototype.
+//
+struct Tq3OptTables {
+    double4 mv64[8];   // per code: {dL down, dLL down, dL up, dLL up} (missing neighbour: zeros, never accepted)
+    double lv[8];      // float64 levels
+};
 
-__device__ __forceinline__ double tq3_opt_refine(const float (&v)[QK], int (&idx)[QK], int n_passes,
-                                                 const OptEntry* __restrict__ tbl) {
-    double A = 0.0, Cx = 0.0;
+__device__ __forceinline__ uint32_t code_of(const uint32_t (&g)[4], int j) {   // code j of the group words
+    return (g[j >> 3] >> (3 * (j & 7))) & 7u;
+}
+
+// Float64 coordinate descent on codes held in registers (one int per element).
+// Each element-step evaluates both neighbours from one table entry (dL, dLL for
+// the lower and upper level) with the incremental form of the exact test and
+// accepts the first strict improvement.
+__device__ __forceinline__ double tq3_opt_refine(const float (&v)[QK], uint32_t (&g)[4], int n_passes,
+                                                 const Tq3OptTables* __restrict__ t) {
+    int idx[QK];
+#pragma unroll
+    for (int j = 0; j < QK; ++j) idx[j] = (int)code_of(g, j);
+    double A = 0.0, C = 0.0;
 #pragma unroll
     for (int j = 0; j < QK; ++j) {
-        const double l = tbl[idx[j]].lvl;
-        A += l * l;
-        Cx += (double)v[j] * l;
+        const double l = t->lv[idx[j]];
+        A = fma(l, l, A);
+        C = fma((double)v[j], l, C);
     }
-    double E = Cx * Cx;
+    double E = C * C;
     for (int pass = 0; pass < n_passes; ++pass) {
         bool improved = false;
 #pragma unroll
         for (int j = 0; j < QK; ++j) {
             const int i = idx[j];
-            const OptEntry e = tbl[i];
+            const double4 e = t->mv64[i];   // dL down, dLL down, dL up, dLL up
             const double xd = (double)v[j];
-            // lower neighbour first, then upper (first strict improvement wins)
-            const double Cd = fma(xd, e.dl_dn, Cx), Ad = A + e.dll_dn;
-            const double Cu = fma(xd, e.dl_up, Cx), Au = A + e.dll_up;
-            const bool acc_dn = i > 0 && Cd * Cd * A > E * Ad;
+            const double Cd = fma(xd, e.x, C), Ad = A + e.y;
+            const double Cu = fma(xd, e.z, C), Au = A + e.w;
+            const bool acc_dn = i > 0 && Cd * Cd * A > E * Ad;          // lower neighbour first
             const bool acc_up = !acc_dn && i < 7 && Cu * Cu * A > E * Au;
-            if (acc_dn) { Cx = Cd; A = Ad; E = Cd * Cd; idx[j] = i - 1; improved = true; }
-            if (acc_up) { Cx = Cu; A = Au; E = Cu * Cu; idx[j] = i + 1; improved = true; }
+            if (acc_dn) { C = Cd; A = Ad; E = Cd * Cd; idx[j] = i - 1; improved = true; }
+            if (acc_up) { C = Cu; A = Au; E = Cu * Cu; idx[j] = i + 1; improved = true; }
         }
         if (!improved) break;
     }
-    return A == 0.0 ? 0.0 : Cx / A;
+#pragma unroll
+    for (int gi = 0; gi < 4; ++gi) {
+        uint32_t w = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w |= (uint32_t)idx[8 * gi + i] << (3 * i);
+        g[gi] = w;
+    }
+    return A == 0.0 ? 0.0 : C / A;
 }
 
 // ── quantize ────────────────────────────────────────────────────────────────
@@ -223,14 +265,15 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
     constexpr int BB = QT == 4 ? TQ4_BYTES : TQ3_BYTES;
     __shared__ __align__(16) uint8_t s_in[CODEC_THREADS * ROW_BYTES];
     __shared__ __align__(16) uint8_t s_out[CODEC_THREADS * BB];
-    __shared__ OptEntry s_tbl[8];
+    __shared__ Tq3OptTables s_tbl;
 
     if (MODE == 1 && threadIdx.x < 8) {
         const int i = threadIdx.x;
         const double L = tq3_level_f64(i);
         const double Ld = i > 0 ? tq3_level_f64(i - 1) : L;
         const double Lu = i < 7 ? tq3_level_f64(i + 1) : L;
-        s_tbl[i] = OptEntry{L, Ld - L, Ld * Ld - L * L, Lu - L, Lu * Lu - L * L};
+        s_tbl.lv[i] = L;
+        s_tbl.mv64[i] = make_double4(Ld - L, Ld * Ld - L * L, Lu - L, Lu * Lu - L * L);
     }
 
     const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
@@ -262,30 +305,27 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
             }
             if (threadIdx.x < nrows) stage_block<4>(s_out, threadIdx.x * BB, dh, w);
         } else {
-            int idx[QK];
-#pragma unroll
-            for (int j = 0; j < QK; ++j) idx[j] = tq3_nearest(__fmul_rn(v[j], inv));
-            if constexpr (MODE == 1) {
-                if (amax > 0.0f) {
-                    const double d = tq3_opt_refine(v, idx, n_passes, s_tbl);
-                    float df = (float)d;
-                    if (df != df) df = fabsf(df);
-                    dh = half_trunc(df);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < QK; ++j) idx[j] = 0;
-                    dh = 0;
-                }
-            } else {
-                dh = half_trunc(amax);
-            }
+            // codes as the four 24-bit group words of the TQ3 layout (code i of a group at bits 3i..3i+2)
             uint32_t g[4];
 #pragma unroll
             for (int gi = 0; gi < 4; ++gi) {
                 uint32_t word = 0;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) word |= (uint32_t)idx[8 * gi + i] << (3 * i);
-                g[gi] = word;   // 24 bits
+                for (int i = 0; i < 8; ++i) word |= (uint32_t)tq3_nearest(__fmul_rn(v[8 * gi + i], inv)) << (3 * i);
+                g[gi] = word;
+            }
+            if constexpr (MODE == 1) {
+                if (amax > 0.0f) {
+                    const double d = tq3_opt_refine(v, g, n_passes, &s_tbl);
+                    float df = (float)d;
+                    if (df != df) df = fabsf(df);
+                    dh = half_trunc(df);
+                } else {
+                    g[0] = g[1] = g[2] = g[3] = 0u;
+                    dh = 0;
+                }
+            } else {
+                dh = half_trunc(amax);
             }
             // 12 code bytes as 3 little-endian words
             const uint32_t w[3] = {g[0] | (g[1] << 24), (g[1] >> 8) | (g[2] << 16), (g[2] >> 16) | (g[3] << 8)};

@@ -1,7 +1,8 @@
 """Fused decode attention over packed TurboQuant K/V caches (torch front end).
 
-Cache tensors are uint8 with shape [batch, n_kv_heads, capacity, head_dim/32, 18]
-(TQ4_0 blocks, src/ggml-tq.h:137-141).  K and V hold Hadamard-rotated rows
+Cache tensors are uint8 with shape [batch, n_kv_heads, capacity, head_dim/32, bytes]
+of TQ4_0 (18-byte) or, for K, TQ3_0 (14-byte) blocks (src/ggml-tq.h:131-141);
+head_dim is 128 or 256 and capacity even.  K and V hold Hadamard-rotated rows
 (quantize with fwht_head_dim=head_dim); the query is rotated inside, and the
 output rotated back, so the result is attention in the original space.
 """

@@ -43,8 +43,6 @@
 
 namespace tq {
 
-constexpr int ATT_WARPS = 16;
-constexpr int ATT_THREADS = ATT_WARPS * 32;
 constexpr int ATT_TILE = 16;            // tokens per warp tile
 constexpr int ATT_STAGES = 4;
 constexpr int ATT_N = 8;                // query heads per mma N tile
@@ -161,7 +159,7 @@ template <> __device__ __forceinline__ float load_q<float>(const float* p) { ret
 template <> __device__ __forceinline__ float load_q<__half>(const __half* p) { return __half2float(*p); }
 template <> __device__ __forceinline__ float load_q<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
-template <typename QT, int D>
+template <typename QT, int D, int KT>
 __global__ void __launch_bounds__(128) attn_qprep_kernel(const QT* __restrict__ q, uint32_t* __restrict__ qfrag,
                                                          int Hq, int Hkv, int grp, float scale, int rotate) {
     __shared__ float sq[ATT_N][D];
@@ -192,9 +190,15 @@ __global__ void __launch_bounds__(128) attn_qprep_kernel(const QT* __restrict__ 
         const int kk = i / 32, lane = i % 32;
         const int gl = lane >> 2, t = lane & 3;
         const int blk = kk >> 1, h = kk & 1;
-        const int e0 = 32 * blk + 8 * h + 2 * t;
-        out[kk * 64 + lane * 2 + 0] = pack_h2(sq[gl][e0] * scale, sq[gl][e0 + 16] * scale);
-        out[kk * 64 + lane * 2 + 1] = pack_h2(sq[gl][e0 + 1] * scale, sq[gl][e0 + 17] * scale);
+        if (KT == 4) {   // TQ4 byte pairs: k-cols (2t, 2t+1) = elements (j, j+16), (2t+8, 2t+9) = (j+1, j+17)
+            const int e0 = 32 * blk + 8 * h + 2 * t;
+            out[kk * 64 + lane * 2 + 0] = pack_h2(sq[gl][e0] * scale, sq[gl][e0 + 16] * scale);
+            out[kk * 64 + lane * 2 + 1] = pack_h2(sq[gl][e0 + 1] * scale, sq[gl][e0 + 17] * scale);
+        } else {         // TQ3 group t: k-cols (2t, 2t+1) = codes 4h, 4h+1 of group t, (2t+8, 2t+9) = 4h+2, 4h+3
+            const int e0 = 32 * blk + 8 * t + 4 * h;
+            out[kk * 64 + lane * 2 + 0] = pack_h2(sq[gl][e0] * scale, sq[gl][e0 + 1] * scale);
+            out[kk * 64 + lane * 2 + 1] = pack_h2(sq[gl][e0 + 2] * scale, sq[gl][e0 + 3] * scale);
+        }
     }
 }
 
@@ -280,25 +284,68 @@ __device__ __forceinline__ void static_for(F&& f) {
     }
 }
 
-template <int D, int KT, int VT, int RES>
-__global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnKernelArgs a) {
-    constexpr int NBLK = D / 32;
-    constexpr int KB = (KT == 4 ? TQ4_BYTES : TQ3_BYTES) * NBLK;   // bytes per token
-    constexpr int VB = (VT == 4 ? TQ4_BYTES : TQ3_BYTES) * NBLK;
-    constexpr int KTILE = ATT_TILE * KB, VTILE = ATT_TILE * VB;
-    constexpr int STAGE = KTILE + VTILE;
-    constexpr int NCH = D / 16;
-    constexpr int NMT = D / 16;
-    constexpr int SCR = ATT_TILE * NBLK * 4 + NBLK * ATT_TILE * 2;   // per-warp scale scratch bytes
-    static_assert(KT == 4 && VT == 4, "TQ4_0 K and V");
-    static_assert(D == 128, "head_dim 128");
+// Per-configuration constants.  head_dim 256 runs 8 warps per CTA so that the
+// O and q fragments (96 registers) fit the 255-register limit; head_dim 128
+// runs 16.  Token order inside a 16-token tile (mma row / k index r holds
+// token tok_of_row(r)) is chosen per token pitch so that every fragment load is
+// free of bank conflicts:
+//   head_dim 128 (K pitch 72 or 56 bytes, V pitch 72): r < 8 -> 2r, r >= 8 -> 2(r-8)+1,
+//     so K rows g, g+8 read tokens 2g, 2g+1 and V k-indices 2t, 2t+1, 2t+8, 2t+9
+//     read tokens 4t, 4t+2, 4t+1, 4t+3;
+//   head_dim 256 (K pitch 144 or 112, V pitch 144): identity.
+// The softmax sum over tokens is order-free.
+template <int D, int KT>
+struct AttnCfg {
+    static constexpr int NBLK = D / 32;
+    static constexpr int WARPS = D == 128 ? 16 : 8;
+    static constexpr int THREADS = WARPS * 32;
+    static constexpr int KBB = KT == 4 ? TQ4_BYTES : TQ3_BYTES;   // K bytes per block
+    static constexpr int KB = KBB * NBLK;                          // K bytes per token
+    static constexpr int VB = TQ4_BYTES * NBLK;                    // V bytes per token
+    static constexpr int KTILE = ATT_TILE * KB, VTILE = ATT_TILE * VB;
+    static constexpr int STAGE = KTILE + VTILE;
+    static constexpr int NCH = D / 16, NMT = D / 16;
+    static constexpr int SCR = ATT_TILE * NBLK * 4 + NBLK * ATT_TILE * 2;   // dK f32 [row][blk] | dV f16 [blk][row]
+    static constexpr bool INTERLEAVE = D == 128;
+    __host__ __device__ static constexpr int tok_of_row(int r) {
+        return INTERLEAVE ? (r < 8 ? 2 * r : 2 * (r - 8) + 1) : r;
+    }
+    __host__ __device__ static constexpr int row_of_tok(int t) { return INTERLEAVE ? ((t & 1) ? 8 + (t >> 1) : (t >> 1)) : t; }
+    static_assert(KTILE % 16 == 0 && STAGE % 16 == 0, "bulk-copy destinations must stay 16-byte aligned");
+};
+
+__host__ __device__ constexpr int att_warps(int D) { return D == 128 ? 16 : 8; }
+
+// TQ3 code pairs -> byte address in the codebook table: pair i of a 24-bit group word
+// (codes 2i, 2i+1) indexes row ((w >> 6i) & 63), TQ3 half of the row (byte 128 + 4 * lane).
+template <int I>
+__device__ __forceinline__ uint32_t tq3_lut_addr(uint32_t w, uint32_t lane4x) {
+    const uint32_t f = I == 0 ? (w << 8) : I == 1 ? (w << 2) : I == 2 ? (w >> 4) : (w >> 10);
+    return (f & 0x3F00u) | lane4x;
+}
+template <int RES>
+__device__ __forceinline__ uint32_t lut_ld_addr(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(addr), "n"(RES));
+    return v;
+}
+
+template <int D, int KT, int RES>
+__global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const AttnKernelArgs a) {
+    using Cfg = AttnCfg<D, KT>;
+    constexpr int NBLK = Cfg::NBLK, WARPS = Cfg::WARPS, THREADS = Cfg::THREADS;
+    constexpr int KBB = Cfg::KBB, KB = Cfg::KB, VB = Cfg::VB;
+    constexpr int KTILE = Cfg::KTILE, STAGE = Cfg::STAGE;
+    constexpr int NCH = Cfg::NCH, NMT = Cfg::NMT, SCR = Cfg::SCR;
+    static_assert(KT == 3 || KT == 4, "TQ3_0 or TQ4_0 K");
+    static_assert(D == 128 || D == 256, "head_dim 128 or 256");
 
     extern __shared__ __align__(1024) uint8_t smem[];
     // layout: LUT | stages [warp][stage] | scale scratch [warp] | barriers [warp][stage] | flag
     uint8_t* stages = smem + LUT_BYTES;
-    uint8_t* scratch = stages + ATT_WARPS * ATT_STAGES * STAGE;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + ATT_WARPS * SCR);
-    int* s_abort = reinterpret_cast<int*>(bars + ATT_WARPS * ATT_STAGES);
+    uint8_t* scratch = stages + WARPS * ATT_STAGES * STAGE;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + WARPS * SCR);
+    int* s_abort = reinterpret_cast<int*>(bars + WARPS * ATT_STAGES);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;
@@ -308,9 +355,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
         if (threadIdx.x == 0) atomicExch(a.err, (int)TQ_ERROR_UNSUPPORTED);
         return;                                    // uniform: no barrier has been used yet
     }
-    for (int i = threadIdx.x; i < 256 * 32; i += ATT_THREADS) {
+    for (int i = threadIdx.x; i < 256 * 32; i += THREADS) {
         const int k = i >> 5, l = i & 31;
         *reinterpret_cast<uint32_t*>(smem + (k << 8) + (l << 2)) = pack_h2(tq4_level(k & 15), tq4_level(k >> 4));
+        if (KT == 3 && k < 64)
+            *reinterpret_cast<uint32_t*>(smem + (k << 8) + 128 + (l << 2)) = pack_h2(tq3_level(k & 7), tq3_level(k >> 3));
     }
     if (lane == 0)
         for (int s = 0; s < ATT_STAGES; ++s) mbar_init(smem_u32(&bars[warp * ATT_STAGES + s]), 1);
@@ -319,25 +368,29 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
     __syncthreads();
 
     const uint32_t stage0 = smem_u32(stages + warp * ATT_STAGES * STAGE);
-    const uint32_t scr = smem_u32(scratch + warp * SCR);               // dK f32 [16][4] | dV f16 [4][16]
+    const uint32_t scr = smem_u32(scratch + warp * SCR);
     const uint32_t bar0 = smem_u32(&bars[warp * ATT_STAGES]);
-    // per-lane fixed offsets
-    // Token order inside a 16-token tile: mma row / k index r holds token pi(r) = 2r (r < 8),
-    // 2(r-8)+1 (r >= 8).  With the 72-byte token pitch this makes both the K loads (rows g,
-    // g+8 -> tokens 2g, 2g+1) and the V loads (k = 2t, 2t+1, 2t+8, 2t+9 -> tokens 4t, 4t+2,
-    // 4t+1, 4t+3) hit distinct banks; the softmax sum over tokens is order-free.
-    const uint32_t k_off = (2 * gq) * KB + 2 * tq + 2;                  // + blk*18 + 8h (+1 token: row g+8)
-    const uint32_t v_off = (4 * tq) * VB + 2 * gq + 2;                   // + tok {0,2,1,3} + blk*18
-    // scale extraction: lane handles entries e = lane + 32 r, r = 0..3 (0..63 K, 64..127 V)
-    uint32_t x_src[4], x_dst[4];
-    const int x_tok = lane >> 2;              // token of entries r = 0, 2; entries r = 1, 3 hold token + 8
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const int e = lane + 32 * r, isv = e >= 64, ee = e & 63, tok = ee >> 2, blk = ee & 3;
-        const int row = (tok & 1) ? 8 + (tok >> 1) : (tok >> 1);      // pi^-1(tok)
-        x_src[r] = (isv ? KTILE + tok * VB : tok * KB) + blk * TQ4_BYTES;
-        x_dst[r] = isv ? ATT_TILE * NBLK * 4 + (blk * ATT_TILE + row) * 2 : (row * NBLK + blk) * 4;
-    }
+    // per-lane fixed offsets inside a stage
+    constexpr int KROW8 = (Cfg::tok_of_row(8) - Cfg::tok_of_row(0)) * KB;   // row g+8 relative to row g
+    const int ktok = Cfg::tok_of_row(gq);
+    // TQ4 K: byte pair (8h + 2t, 8h + 2t + 1) of each block
+    const uint32_t k_off = ktok * KB + 2 * tq + 2;
+    // TQ3 K: group t of each block, read as two aligned words and a funnel shift; blocks
+    // start at 14 * blk bytes, which is 0 mod 4 for even and 2 mod 4 for odd blk
+    const uint32_t k3_off_e = ktok * KB + ((2 + 3 * tq) & ~3), k3_sh_e = 8 * ((2 + 3 * tq) & 3);
+    const uint32_t k3_off_o = ktok * KB + ((4 + 3 * tq) & ~3), k3_sh_o = 8 * ((4 + 3 * tq) & 3);
+    const uint32_t lane4x = lane4 | 0x80u;
+    // V: k-indices 2t, 2t+1, 2t+8, 2t+9 of the P fragment
+    constexpr int VT0 = Cfg::tok_of_row(0);
+    constexpr int VO1 = (Cfg::tok_of_row(1) - VT0) * VB, VO8 = (Cfg::tok_of_row(8) - VT0) * VB,
+                  VO9 = (Cfg::tok_of_row(9) - VT0) * VB;
+    const uint32_t v_off = Cfg::tok_of_row(2 * tq) * VB + 2 * gq + 2;
+    // scale extraction: lane handles K entries r = 0 .. NBLK/2-1 and V entries likewise; entry r
+    // of this lane is token xt0 + r * TSTEP, block xb
+    constexpr int TSTEP = 32 / NBLK, ROWSTEP = Cfg::INTERLEAVE ? TSTEP / 2 : TSTEP, NXH = NBLK / 2;
+    const int xt0 = lane / NBLK, xb = lane % NBLK, xrow0 = Cfg::row_of_tok(xt0);
+    const uint32_t xks = xt0 * KB + xb * KBB, xkd = (xrow0 * NBLK + xb) * 4;
+    const uint32_t xvs = KTILE + xt0 * VB + xb * TQ4_BYTES, xvd = ATT_TILE * NBLK * 4 + (xb * ATT_TILE + xrow0) * 2;
     uint32_t phase_bits = 0;
 
     const int64_t pairs = (int64_t)a.B * a.Hkv;
@@ -355,7 +408,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
         if (len > a.cap) len = a.cap;
         if (t1 > len) t1 = len;
         const int ntiles_seg = t1 > t0 ? (int)((t1 - t0 + ATT_TILE - 1) / ATT_TILE) : 0;
-        const int ntiles = ntiles_seg > warp ? (ntiles_seg - warp + ATT_WARPS - 1) / ATT_WARPS : 0;
+        const int ntiles = ntiles_seg > warp ? (ntiles_seg - warp + WARPS - 1) / WARPS : 0;
 
         const uint8_t* kbase = a.k + (size_t)pair * a.cap * KB;
         const uint8_t* vbase = a.v + (size_t)pair * a.cap * VB;
@@ -374,12 +427,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
         for (int mt = 0; mt < NMT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
         float m_run0 = M_FLOOR, m_run1 = M_FLOOR, l0 = 0.0f, l1 = 0.0f;
 
-        // copy sources advance by one CTA tile row (16 warps x 16 tokens) per warp tile
+        // copy sources advance by one CTA tile row (WARPS x 16 tokens) per warp tile
         const uint8_t* ksrc = kbase + (t0 + (int64_t)warp * ATT_TILE) * KB;
         const uint8_t* vsrc = vbase + (t0 + (int64_t)warp * ATT_TILE) * VB;
         const int64_t tok_first = t0 + (int64_t)warp * ATT_TILE;      // first token of tile 0
         // tokens of the last tile that exist in memory (capacity), for the copy size
-        const int64_t t_last = tok_first + (int64_t)(ntiles > 0 ? ntiles - 1 : 0) * ATT_WARPS * ATT_TILE;
+        const int64_t t_last = tok_first + (int64_t)(ntiles > 0 ? ntiles - 1 : 0) * WARPS * ATT_TILE;
         const uint32_t last_nt = (uint32_t)(a.cap - t_last < ATT_TILE ? a.cap - t_last : ATT_TILE);
         // tokens of the last tile below the valid length (tiles before it are full)
         const int last_valid = (int)(t1 - t_last < ATT_TILE ? t1 - t_last : ATT_TILE);
@@ -390,8 +443,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
             const uint32_t nt = last ? last_nt : (uint32_t)ATT_TILE;
             bulk_issue(lane == 0 && issued < ntiles, stage0 + S * STAGE, ksrc, nt * KB, stage0 + S * STAGE + KTILE,
                        vsrc, nt * VB, bar0 + 8 * S);
-            ksrc += (size_t)ATT_WARPS * ATT_TILE * KB;
-            vsrc += (size_t)ATT_WARPS * ATT_TILE * VB;
+            ksrc += (size_t)WARPS * ATT_TILE * KB;
+            vsrc += (size_t)WARPS * ATT_TILE * VB;
             ++issued;
         };
         static_for<0, ATT_STAGES - 1>([&](auto sc) { issue_next(sc); });
@@ -414,56 +467,83 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
                 const uint32_t st = stage0 + S * STAGE;
                 const int valid = i == ntiles - 1 ? last_valid : ATT_TILE;
 
-                // block scales: K -> f32 [tok][blk], V -> f16 bits [blk][tok]; tokens past the
+                // block scales: K -> f32 [row][blk], V -> f16 bits [blk][row]; tokens past the
                 // valid range (stale or never-written stage bytes) get scale 0
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const bool xv = x_tok + 8 * (r & 1) < valid;
+                static_for<0, 2 * NXH>([&](auto r_c) {
+                    constexpr int r = decltype(r_c)::value;
+                    constexpr bool IS_V = r >= NXH;
+                    constexpr int rr = IS_V ? r - NXH : r;
+                    const bool xv = xt0 + rr * TSTEP < valid;
+                    const uint32_t src = IS_V ? xvs + rr * TSTEP * VB : xks + rr * TSTEP * KB;
                     uint16_t h;
-                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(st + x_src[r]));
+                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(st + src));
                     h = xv ? h : (uint16_t)0;
                     // |d| >= 2^15: exponent 31 decodes as a finite value in the reference but as
                     // inf/nan in IEEE fp16, and P * d could overflow fp16: reported once per segment
                     bad_scale |= (h & 0x7C00u) >= 0x7800u;
-                    if (r < 2) {
+                    if (!IS_V) {
                         const float f = __half2float(__ushort_as_half(h));
-                        asm volatile("st.shared.f32 [%0], %1;" ::"r"(scr + x_dst[r]), "f"(f));
+                        asm volatile("st.shared.f32 [%0], %1;" ::"r"(scr + xkd + rr * ROWSTEP * NBLK * 4), "f"(f));
                     } else {
-                        asm volatile("st.shared.u16 [%0], %1;" ::"r"(scr + x_dst[r]), "h"(h));
+                        asm volatile("st.shared.u16 [%0], %1;" ::"r"(scr + xvd + rr * ROWSTEP * 2), "h"(h));
                     }
-                }
+                });
                 __syncwarp();
 
                 // ---- S = K q~^T ----
                 float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                const uint32_t kr = st + k_off;
-                const float4 dk0 = ld128f<0>(scr + gq * 16), dk1 = ld128f<8 * 16>(scr + gq * 16);
-                const float dka[4] = {dk0.x, dk0.y, dk0.z, dk0.w}, dkb[4] = {dk1.x, dk1.y, dk1.z, dk1.w};
+                float dka[NBLK], dkb[NBLK];
+                static_for<0, NBLK / 4>([&](auto c_c) {
+                    constexpr int c = decltype(c_c)::value;
+                    const float4 x = ld128f<c * 16>(scr + gq * NBLK * 4);
+                    const float4 y = ld128f<8 * NBLK * 4 + c * 16>(scr + gq * NBLK * 4);
+                    dka[4 * c] = x.x; dka[4 * c + 1] = x.y; dka[4 * c + 2] = x.z; dka[4 * c + 3] = x.w;
+                    dkb[4 * c] = y.x; dkb[4 * c + 1] = y.y; dkb[4 * c + 2] = y.z; dkb[4 * c + 3] = y.w;
+                });
                 static_for<0, NBLK>([&](auto blk_c) {
                     constexpr int blk = decltype(blk_c)::value;
                     float acc[4];
                     uint32_t af[4];
-                    uint32_t w0 = ld16<blk * TQ4_BYTES>(kr), w1 = ld16<blk * TQ4_BYTES + KB>(kr);
-                    af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
-                    af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);
-                    af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
-                    af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
-                    mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
-                    w0 = ld16<blk * TQ4_BYTES + 8>(kr);
-                    w1 = ld16<blk * TQ4_BYTES + 8 + KB>(kr);
-                    af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
-                    af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);
-                    af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
-                    af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
-                    mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
+                    if constexpr (KT == 4) {
+                        const uint32_t kr = st + k_off;
+                        uint32_t w0 = ld16<blk * TQ4_BYTES>(kr), w1 = ld16<blk * TQ4_BYTES + KROW8>(kr);
+                        af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
+                        af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);
+                        af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
+                        af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
+                        mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
+                        w0 = ld16<blk * TQ4_BYTES + 8>(kr);
+                        w1 = ld16<blk * TQ4_BYTES + 8 + KROW8>(kr);
+                        af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
+                        af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);
+                        af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
+                        af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
+                        mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
+                    } else {
+                        constexpr int IMM = blk * TQ3_BYTES - 2 * (blk & 1);
+                        const uint32_t kr = st + ((blk & 1) ? k3_off_o : k3_off_e);
+                        const uint32_t sh = (blk & 1) ? k3_sh_o : k3_sh_e;
+                        const uint32_t wg = __funnelshift_r(ld32<IMM>(kr), ld32<IMM + 4>(kr), sh);
+                        const uint32_t wh = __funnelshift_r(ld32<IMM + KROW8>(kr), ld32<IMM + KROW8 + 4>(kr), sh);
+                        af[0] = lut_ld_addr<RES>(tq3_lut_addr<0>(wg, lane4x));
+                        af[1] = lut_ld_addr<RES>(tq3_lut_addr<0>(wh, lane4x));
+                        af[2] = lut_ld_addr<RES>(tq3_lut_addr<1>(wg, lane4x));
+                        af[3] = lut_ld_addr<RES>(tq3_lut_addr<1>(wh, lane4x));
+                        mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
+                        af[0] = lut_ld_addr<RES>(tq3_lut_addr<2>(wg, lane4x));
+                        af[1] = lut_ld_addr<RES>(tq3_lut_addr<2>(wh, lane4x));
+                        af[2] = lut_ld_addr<RES>(tq3_lut_addr<3>(wg, lane4x));
+                        af[3] = lut_ld_addr<RES>(tq3_lut_addr<3>(wh, lane4x));
+                        mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
+                    }
                     sc[0] = fmaf(dka[blk], acc[0], sc[0]);
                     sc[1] = fmaf(dka[blk], acc[1], sc[1]);
                     sc[2] = fmaf(dkb[blk], acc[2], sc[2]);
                     sc[3] = fmaf(dkb[blk], acc[3], sc[3]);
                 });
                 if (valid < ATT_TILE) {
-                    if (2 * gq >= valid) { sc[0] = -INFINITY; sc[1] = -INFINITY; }
-                    if (2 * gq + 1 >= valid) { sc[2] = -INFINITY; sc[3] = -INFINITY; }
+                    if (Cfg::tok_of_row(gq) >= valid) { sc[0] = -INFINITY; sc[1] = -INFINITY; }
+                    if (Cfg::tok_of_row(gq + 8) >= valid) { sc[2] = -INFINITY; sc[3] = -INFINITY; }
                 }
 
                 // ---- online softmax (log2 domain) ----
@@ -499,8 +579,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
                 const uint32_t sdv = scr + ATT_TILE * NBLK * 4 + 4 * tq;
                 static_for<0, NBLK>([&](auto blk_c) {
                     constexpr int blk = decltype(blk_c)::value;
-                    const uint32_t w0 = ld16<blk * TQ4_BYTES>(vr), w1 = ld16<blk * TQ4_BYTES + 2 * VB>(vr);
-                    const uint32_t w2 = ld16<blk * TQ4_BYTES + VB>(vr), w3 = ld16<blk * TQ4_BYTES + 3 * VB>(vr);
+                    const uint32_t w0 = ld16<blk * TQ4_BYTES>(vr), w1 = ld16<blk * TQ4_BYTES + VO1>(vr);
+                    const uint32_t w2 = ld16<blk * TQ4_BYTES + VO8>(vr), w3 = ld16<blk * TQ4_BYTES + VO9>(vr);
                     const uint32_t ra = prmt(w0, w1, 0x5140u), rb = prmt(w2, w3, 0x5140u);
                     const uint32_t ra4 = ra >> 4, rb4 = rb >> 4;
                     const uint32_t xa = (ra & 0x000F000Fu) | (ra4 & 0x00F000F0u);
@@ -535,7 +615,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
         }
         if (__any_sync(0xffffffffu, bad_scale != 0) && lane == 0) atomicExch(a.err, (int)TQ_ERROR_UNSUPPORTED);
 
-        // ---- merge the 16 warps, write the (pair, slot) partial ----
+        // ---- merge the warps, write the (pair, slot) partial ----
 #pragma unroll
         for (int sh = 4; sh < 32; sh <<= 1) {
             l0 += __shfl_xor_sync(0xffffffffu, l0, sh);
@@ -561,14 +641,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const AttnK
         }
         __syncthreads();
         float* dst = a.part + ((size_t)pair * a.slots + slot) * ATT_N * (D + 2);
-        for (int idx = threadIdx.x; idx < ATT_N * (D + 2); idx += ATT_THREADS) {
+        for (int idx = threadIdx.x; idx < ATT_N * (D + 2); idx += THREADS) {
             const int h = idx / (D + 2), c = idx % (D + 2);
             float M = M_FLOOR;
-            for (int w = 0; w < ATT_WARPS; ++w) M = fmaxf(M, red[w * ATT_N * (D + 2) + h * (D + 2)]);
+            for (int w = 0; w < WARPS; ++w) M = fmaxf(M, red[w * ATT_N * (D + 2) + h * (D + 2)]);
             float acc = M;
             if (c > 0) {
                 acc = 0.0f;
-                for (int w = 0; w < ATT_WARPS; ++w)
+                for (int w = 0; w < WARPS; ++w)
                     acc += ex2(red[w * ATT_N * (D + 2) + h * (D + 2)] - M) * red[w * ATT_N * (D + 2) + idx];
             }
             dst[idx] = acc;
@@ -655,29 +735,27 @@ __global__ void __launch_bounds__(128) lse_combine_kernel(const float* __restric
 
 // ── host side ───────────────────────────────────────────────────────────────
 
-template <int D, int KT, int VT>
+template <int D, int KT>
 static size_t decode_smem_bytes() {
-    constexpr int NBLK = D / 32;
-    constexpr int KB = (KT == 4 ? TQ4_BYTES : TQ3_BYTES) * NBLK;
-    constexpr int VB = (VT == 4 ? TQ4_BYTES : TQ3_BYTES) * NBLK;
+    using Cfg = AttnCfg<D, KT>;
     size_t s = LUT_BYTES;
-    const size_t stg = (size_t)ATT_WARPS * ATT_STAGES * ATT_TILE * (KB + VB);
-    const size_t red = (size_t)ATT_WARPS * ATT_N * (D + 2) * 4;   // warp merge scratch reuses the stages
+    const size_t stg = (size_t)Cfg::WARPS * ATT_STAGES * Cfg::STAGE;
+    const size_t red = (size_t)Cfg::WARPS * ATT_N * (D + 2) * 4;   // warp merge scratch reuses the stages
     s += stg > red ? stg : red;
-    s += (size_t)ATT_WARPS * (ATT_TILE * NBLK * 4 + NBLK * ATT_TILE * 2);
-    s += (size_t)ATT_WARPS * ATT_STAGES * 8;
+    s += (size_t)Cfg::WARPS * Cfg::SCR;
+    s += (size_t)Cfg::WARPS * ATT_STAGES * 8;
     s += 16;
     return s;
 }
 
-AttnPlan attn_plan(int B, int Hkv, int64_t cap, int64_t max_len) {
+AttnPlan attn_plan(int B, int Hkv, int D, int64_t cap, int64_t max_len) {
     AttnPlan p;
     const int64_t pairs = (int64_t)B * Hkv;
     const int64_t len = max_len > 0 ? max_len : cap;
     p.lnom = (len + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
     if (p.lnom == 0) p.lnom = ATT_TILE;
     const int64_t total = pairs * p.lnom;
-    const int64_t unit = ATT_WARPS * ATT_TILE;
+    const int64_t unit = (int64_t)att_warps(D) * ATT_TILE;
     const int sms = sm_count();
     int64_t chunk = (total + sms - 1) / sms;
     chunk = (chunk + unit - 1) / unit * unit;
@@ -714,8 +792,11 @@ static int reserved_smem() {
 
 template <typename QT, int D>
 static cudaError_t launch_qprep(const void* q, uint32_t* qfrag, int B, int Hq, int Hkv, int grp, float scale,
-                                int rotate, cudaStream_t st) {
-    attn_qprep_kernel<QT, D><<<B * Hkv, 128, 0, st>>>((const QT*)q, qfrag, Hq, Hkv, grp, scale, rotate);
+                                int rotate, int k_type, cudaStream_t st) {
+    if (k_type == 4)
+        attn_qprep_kernel<QT, D, 4><<<B * Hkv, 128, 0, st>>>((const QT*)q, qfrag, Hq, Hkv, grp, scale, rotate);
+    else
+        attn_qprep_kernel<QT, D, 3><<<B * Hkv, 128, 0, st>>>((const QT*)q, qfrag, Hq, Hkv, grp, scale, rotate);
     return cudaGetLastError();
 }
 
@@ -727,14 +808,19 @@ static cudaError_t launch_combine(const float* part, void* out, float* lse, int 
     return cudaGetLastError();
 }
 
-template <int D, int RES>
+template <int D, int KT, int RES>
 static cudaError_t launch_decode_kernel(const AttnKernelArgs& a, int grid, cudaStream_t st) {
-    const size_t smem = decode_smem_bytes<D, 4, 4>();
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, 4, 4, RES>,
+    const size_t smem = decode_smem_bytes<D, KT>();
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, KT, RES>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    attn_decode_kernel<D, 4, 4, RES><<<grid, ATT_THREADS, smem, st>>>(a);
+    attn_decode_kernel<D, KT, RES><<<grid, AttnCfg<D, KT>::THREADS, smem, st>>>(a);
     return cudaGetLastError();
+}
+
+template <int D, int RES>
+static cudaError_t launch_decode_kt(const AttnKernelArgs& a, int k_type, int grid, cudaStream_t st) {
+    return k_type == 4 ? launch_decode_kernel<D, 4, RES>(a, grid, st) : launch_decode_kernel<D, 3, RES>(a, grid, st);
 }
 
 template <int D>
@@ -749,9 +835,9 @@ static cudaError_t run_decode(const AttnRun& r, const AttnPlan& p, uint8_t* ws, 
     // q~ = FWHT(q) / sqrt(D) * sm_scale * log2(e): the FWHT normalisation folds into the scale
     const float scale = r.sm_scale * LOG2E * (r.rotate_q ? fwht_norm(D) : 1.0f);
     switch (r.q_dtype) {
-        case DT_F32: e = launch_qprep<float, D>(r.q, qfrag, r.B, r.Hq, r.Hkv, r.grp, scale, r.rotate_q, st); break;
-        case DT_F16: e = launch_qprep<__half, D>(r.q, qfrag, r.B, r.Hq, r.Hkv, r.grp, scale, r.rotate_q, st); break;
-        default: e = launch_qprep<__nv_bfloat16, D>(r.q, qfrag, r.B, r.Hq, r.Hkv, r.grp, scale, r.rotate_q, st); break;
+        case DT_F32: e = launch_qprep<float, D>(r.q, qfrag, r.B, r.Hq, r.Hkv, r.grp, scale, r.rotate_q, r.k_type, st); break;
+        case DT_F16: e = launch_qprep<__half, D>(r.q, qfrag, r.B, r.Hq, r.Hkv, r.grp, scale, r.rotate_q, r.k_type, st); break;
+        default: e = launch_qprep<__nv_bfloat16, D>(r.q, qfrag, r.B, r.Hq, r.Hkv, r.grp, scale, r.rotate_q, r.k_type, st); break;
     }
     if (e != cudaSuccess) return e;
     AttnKernelArgs a;
@@ -768,8 +854,8 @@ static cudaError_t run_decode(const AttnRun& r, const AttnPlan& p, uint8_t* ws, 
     a.Hkv = r.Hkv;
     a.slots = p.slots;
     const int res = reserved_smem();
-    if (res == 0) e = launch_decode_kernel<D, 0>(a, p.grid, st);
-    else if (res == 1024) e = launch_decode_kernel<D, 1024>(a, p.grid, st);
+    if (res == 0) e = launch_decode_kt<D, 0>(a, r.k_type, p.grid, st);
+    else if (res == 1024) e = launch_decode_kt<D, 1024>(a, r.k_type, p.grid, st);
     else return cudaErrorNotSupported;
     if (e != cudaSuccess) return e;
     switch (r.out_dtype) {
@@ -780,7 +866,9 @@ static cudaError_t run_decode(const AttnRun& r, const AttnPlan& p, uint8_t* ws, 
 }
 
 cudaError_t launch_decode_attention(const AttnRun& r, const AttnPlan& p, void* workspace, cudaStream_t st) {
+    if (r.v_type != 4 || (r.k_type != 3 && r.k_type != 4)) return cudaErrorInvalidValue;
     if (r.D == 128) return run_decode<128>(r, p, (uint8_t*)workspace, st);
+    if (r.D == 256) return run_decode<256>(r, p, (uint8_t*)workspace, st);
     return cudaErrorInvalidValue;
 }
 

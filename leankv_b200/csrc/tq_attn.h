@@ -9,7 +9,7 @@ namespace tq {
 
 struct AttnPlan {
     int64_t lnom = 0;            // nominal tokens per (sequence, KV head), multiple of 16
-    int64_t chunk = 0;           // tokens per CTA (multiple of 256)
+    int64_t chunk = 0;           // tokens per CTA (multiple of 16 x warps per CTA)
     int grid = 0;                // CTAs
     int slots = 0;               // partial slots per (sequence, KV head)
 };
@@ -30,7 +30,7 @@ struct AttnRun {
     float* lse = nullptr;
 };
 
-AttnPlan attn_plan(int B, int Hkv, int64_t cap, int64_t max_len);
+AttnPlan attn_plan(int B, int Hkv, int D, int64_t cap, int64_t max_len);
 size_t attn_workspace_bytes(int B, int Hkv, int D, const AttnPlan& p);
 cudaError_t launch_decode_attention(const AttnRun& r, const AttnPlan& p, void* workspace, cudaStream_t st);
 cudaError_t launch_lse_combine(const float* o, const float* lse, float* out, float* lse_out, int P, int64_t n, int D,

@@ -17,10 +17,11 @@ static tq_status attn_check(const tq_decode_attention_args* a, AttnRun* r, AttnP
     const int grp = a->n_q_heads / a->n_kv_heads;
     if (grp != 1 && grp != 2 && grp != 4 && grp != 8)
         return set_error(TQ_ERROR_UNSUPPORTED, "GQA group size %d (supported: 1, 2, 4, 8)", grp);
-    if (a->head_dim != 128) return set_error(TQ_ERROR_UNSUPPORTED, "head_dim %d (supported: 128)", a->head_dim);
-    if (a->k_type != TQ_TYPE_TQ4_0 || a->v_type != TQ_TYPE_TQ4_0)
-        return set_error(TQ_ERROR_UNSUPPORTED, "block types K=%d V=%d (supported: TQ4_0/TQ4_0)", (int)a->k_type,
-                         (int)a->v_type);
+    if (a->head_dim != 128 && a->head_dim != 256)
+        return set_error(TQ_ERROR_UNSUPPORTED, "head_dim %d (supported: 128, 256)", a->head_dim);
+    if ((a->k_type != TQ_TYPE_TQ4_0 && a->k_type != TQ_TYPE_TQ3_0) || a->v_type != TQ_TYPE_TQ4_0)
+        return set_error(TQ_ERROR_UNSUPPORTED, "block types K=%d V=%d (supported: K TQ4_0 or TQ3_0, V TQ4_0)",
+                         (int)a->k_type, (int)a->v_type);
     if (!dtype_ok(a->q_dtype) || !dtype_ok(a->out_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "bad dtype");
     if (a->kv_capacity < 0 || (a->kv_capacity & 1)) return set_error(TQ_ERROR_INVALID_VALUE, "kv_capacity must be even");
     if (a->max_kv_len < 0 || a->max_kv_len > a->kv_capacity)
@@ -37,7 +38,7 @@ static tq_status attn_check(const tq_decode_attention_args* a, AttnRun* r, AttnP
     r->sm_scale = a->sm_scale != 0.0f ? a->sm_scale : 1.0f / sqrtf((float)a->head_dim);
     r->rotate_q = a->rotate_q != 0; r->v_rotated = a->v_rotated != 0;
     r->out = a->out; r->out_dtype = a->out_dtype; r->lse = a->lse;
-    *p = attn_plan(a->batch, a->n_kv_heads, a->kv_capacity, a->max_kv_len > 0 ? a->max_kv_len : a->kv_capacity);
+    *p = attn_plan(a->batch, a->n_kv_heads, a->head_dim, a->kv_capacity, a->max_kv_len > 0 ? a->max_kv_len : a->kv_capacity);
     return TQ_SUCCESS;
 }
 

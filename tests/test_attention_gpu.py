@@ -121,8 +121,10 @@ def torch_reference(q, kc, vc, D):
     B, Hkv, T = kc.shape[:3]
     Hq = q.shape[1]
     grp = Hq // Hkv
-    kd = ops.dequantize(kc.reshape(B, Hkv, T * (D // 32), 18), 4).reshape(B, Hkv, T, D)
-    vd = ops.dequantize(vc.reshape(B, Hkv, T * (D // 32), 18), 4).reshape(B, Hkv, T, D)
+    kt = 4 if kc.shape[-1] == 18 else 3
+    vt = 4 if vc.shape[-1] == 18 else 3
+    kd = ops.dequantize(kc.contiguous().reshape(B, Hkv, T * (D // 32), kc.shape[-1]), kt).reshape(B, Hkv, T, D)
+    vd = ops.dequantize(vc.contiguous().reshape(B, Hkv, T * (D // 32), vc.shape[-1]), vt).reshape(B, Hkv, T, D)
     H = torch.tensor([[1.0]], device=DEV)
     while H.shape[0] < D:
         H = torch.cat([torch.cat([H, H], 1), torch.cat([H, -H], 1)], 0)
@@ -179,3 +181,75 @@ def test_split_by_sequence_combine_equals_full(orc):
         lses.append(l.reshape(-1))
     comb = attention.lse_combine(torch.stack(parts), torch.stack(lses)).reshape(full.shape)
     check(comb.cpu().numpy(), full.cpu().numpy())
+
+
+@pytest.mark.parametrize("grp", [1, 2, 4, 8])
+def test_attention_tq3_k_vs_oracle(orc, grp):
+    """Mixed TQ3_0 K / TQ4_0 V caches (the long-context split-sequence layout)."""
+    B, Hkv, T, D = 2, 2, 900, 128
+    kc = make_cache(B, Hkv, T, D, 40 + grp, qtype=3)
+    vc = make_cache(B, Hkv, T, D, 50 + grp)
+    q = torch.randn(B, Hkv * grp, D, generator=torch.Generator().manual_seed(60 + grp)).to(torch.float16)
+    lens = torch.tensor([900, 417], dtype=torch.int32)
+    out, lse = attention.decode_attention(q.to(DEV), kc, vc, kv_len=lens.to(DEV), return_lse=True)
+    ref, lref = orc.decode_attention(q.float().numpy(), kc.cpu().numpy(), 3, vc.cpu().numpy(), 4, Hkv,
+                                     kv_len=lens.numpy(), nthreads=8)
+    rel = check(out.cpu().numpy(), ref, lse.cpu().numpy(), lref)
+    print(f"TQ3 K grp {grp}: rel err {rel:.3g}")
+
+
+@pytest.mark.parametrize("kt", [4, 3])
+@pytest.mark.parametrize("T,lens", [(2, [2, 1]), (34, [0, 33]), (530, [530, 77]), (3000, [2999, 1500])])
+def test_attention_head_dim_256(orc, kt, T, lens):
+    """head_dim 256 (8 warps per CTA, identity token order), TQ4_0 or TQ3_0 K, ragged lengths."""
+    B, Hkv, D, grp = len(lens), 2, 256, 4
+    kc = make_cache(B, Hkv, T, D, 70 + kt, qtype=kt)
+    vc = make_cache(B, Hkv, T, D, 80 + kt)
+    q = torch.randn(B, Hkv * grp, D, generator=torch.Generator().manual_seed(T)).to(torch.bfloat16)
+    lt = torch.tensor(lens, dtype=torch.int32)
+    out, lse = attention.decode_attention(q.to(DEV), kc, vc, kv_len=lt.to(DEV), return_lse=True)
+    ref, lref = orc.decode_attention(q.float().numpy(), kc.cpu().numpy(), kt, vc.cpu().numpy(), 4, Hkv,
+                                     kv_len=lt.numpy(), nthreads=8)
+    rel = check(out.cpu().numpy(), ref, lse.cpu().numpy(), lref)
+    print(f"D256 K TQ{kt} T {T}: rel err {rel:.3g}")
+
+
+def test_attention_tq3_k_rotation_flags(orc):
+    B, Hkv, T, D, grp = 1, 2, 300, 128, 8
+    kc = make_cache(B, Hkv, T, D, 91, qtype=3)
+    vc = make_cache(B, Hkv, T, D, 92)
+    q = torch.randn(B, Hkv * grp, D, generator=torch.Generator().manual_seed(93))
+    out = attention.decode_attention(q.to(DEV), kc, vc, rotate_q=False, v_rotated=False)
+    ref, _ = orc.decode_attention(q.numpy(), kc.cpu().numpy(), 3, vc.cpu().numpy(), 4, Hkv,
+                                  rotate_q=False, v_rotated=False, nthreads=4)
+    check(out.cpu().numpy(), ref)
+
+
+def test_c4_shape_tq3k_long_context(orc):
+    """64 query / 8 KV heads, head_dim 128, context 131072, TQ3_0 K / TQ4_0 V (batch 2 of the 64)."""
+    B, Hq, Hkv, T, D = 2, 64, 8, 131072, 128
+    g = torch.Generator(device=DEV).manual_seed(4)
+    kc = ops.quantize(torch.randn(B, Hkv, T, D, device=DEV, generator=g), 3, fwht_head_dim=D)
+    vc = ops.quantize(torch.randn(B, Hkv, T, D, device=DEV, generator=g), 4, fwht_head_dim=D)
+    q = torch.randn(B, Hq, D, device=DEV, generator=g).half()
+    lens = torch.tensor([T, T - 12345], dtype=torch.int32, device=DEV)
+    out, lse = attention.decode_attention(q, kc, vc, kv_len=lens, return_lse=True)
+    for b in range(B):
+        n = int(lens[b])
+        ref, lref = torch_reference(q[b:b + 1], kc[b:b + 1, :, :n], vc[b:b + 1, :, :n], D)
+        rel = check(out[b:b + 1].cpu().numpy(), ref.cpu().numpy(), lse[b:b + 1].cpu().numpy(), lref.cpu().numpy())
+        print(f"C4 shape seq {b} (len {n}) vs torch fp32: rel err {rel:.3g}")
+
+
+def test_c5_shape_head_dim_256(orc):
+    """8 KV heads, head_dim 256, context 16384 + 1, TQ4_0 K/V (one layer, batch 4 of the 32)."""
+    B, Hq, Hkv, T, D = 4, 32, 8, 16385, 256
+    g = torch.Generator(device=DEV).manual_seed(5)
+    kc = ops.quantize(torch.randn(B, Hkv, T + 1, D, device=DEV, generator=g), 4, fwht_head_dim=D)
+    vc = ops.quantize(torch.randn(B, Hkv, T + 1, D, device=DEV, generator=g), 4, fwht_head_dim=D)
+    q = torch.randn(B, Hq, D, device=DEV, generator=g).to(torch.bfloat16)
+    lens = torch.full((B,), T, dtype=torch.int32, device=DEV)
+    out, lse = attention.decode_attention(q, kc, vc, kv_len=lens, max_kv_len=T, return_lse=True)
+    ref, lref = torch_reference(q, kc[:, :, :T], vc[:, :, :T], D)
+    rel = check(out.cpu().numpy(), ref.cpu().numpy(), lse.cpu().numpy(), lref.cpu().numpy())
+    print(f"C5 shape vs torch fp32: rel err {rel:.3g}")

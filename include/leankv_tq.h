@@ -117,6 +117,26 @@ tq_status tq_dequantize_cuda(tq_type type, const void *x, void *y, tq_dtype y_dt
 /* In-place hadamard_transform_row on n float32 values (head_dim a power of two <= 32768). */
 tq_status tq_hadamard_cuda(float *x, int64_t n, int head_dim, void *stream);
 
+/*
+ * Quantize-on-write into a KV cache: [FWHT] + quantize n_new new head rows per
+ * (sequence, KV head) straight into their token slots.  No counterpart in the
+ * reference C; it is hadamard_transform_row + quantize_row_tq*_0 placed the way
+ * the prototype's LeanKVCache.update appends tokens
+ * (prototype/turboquant/kv_cache.py:109-150).
+ *   src   device [batch][n_kv_heads][n_new][head_dim] of src_dtype
+ *   cache device [batch][n_kv_heads][capacity][head_dim/32] blocks of `type`
+ *   row t of (b, h) goes to token slot pos[b] + t; pos is a device int32 [batch]
+ *   array, or NULL for slot t (a prefill from slot 0).
+ * rotate != 0 applies the head_dim Hadamard rotation first (the layout the decode
+ * attention reads); opt_passes as for tq_quantize_cuda.  head_dim: power of two,
+ * 32..1024.  Rows whose slot is outside [0, capacity) are not written; when
+ * overflow is not NULL their number is added to the device int32 *overflow.
+ * The blocks written are bit-identical to tq_quantize_cuda on the same rows.
+ */
+tq_status tq_kv_append_cuda(tq_type type, const void *src, tq_dtype src_dtype, void *cache, int batch,
+                            int n_kv_heads, int head_dim, int64_t capacity, int64_t n_new, const int32_t *pos,
+                            int rotate, int opt_passes, int32_t *overflow, void *stream);
+
 /* ── 3. host-pointer API (synchronous) ───────────────────────────────────── */
 
 tq_status tq_quantize_host(tq_type type, const void *x, tq_dtype x_dtype, void *y, int64_t k,
@@ -138,9 +158,12 @@ tq_status tq_hadamard_host(float *x, int64_t n, int head_dim);
  * (or block_tq3_0), i.e. every token's head row is head_dim/32 consecutive blocks.
  * q / out: [batch][n_q_heads][head_dim].  lse (optional): [batch][n_q_heads],
  * natural log of sum_t exp(s_t); -inf and a zero output for kv_len == 0.
- * Requirements: head_dim 128; n_q_heads / n_kv_heads in {1, 2, 4, 8}; kv_capacity
- * even; cache pointers 16-byte aligned.  Supported block types: TQ4_0 K and V.
- * Work memory: tq_decode_attention_workspace_size() bytes of device memory.
+ * Requirements: head_dim 128 or 256; n_q_heads / n_kv_heads in {1, 2, 4, 8};
+ * kv_capacity even; cache pointers 16-byte aligned.  Block types: K TQ4_0 or
+ * TQ3_0, V TQ4_0.  Work memory: tq_decode_attention_workspace_size() bytes of
+ * device memory; its first int32 receives the kernel-side status (TQ_SUCCESS,
+ * TQ_ERROR_TIMEOUT for a bulk copy that never completed, TQ_ERROR_UNSUPPORTED
+ * for a block scale of magnitude >= 2^15) once the stream has run the call.
  */
 typedef struct {
     int batch, n_q_heads, n_kv_heads, head_dim;
@@ -186,6 +209,13 @@ tq_status tq_decode_attention_static_cuda(const tq_decode_attention_args *a, voi
  * the split-by-sequence combine of the multi-GPU path (new) */
 tq_status tq_lse_combine_cuda(int n_parts, int64_t n_rows, int head_dim, const float *o, const float *lse,
                               float *out, float *lse_out, void *stream);
+/* The same merge with parts at arbitrary strides (in floats) and the output in
+ * out_dtype: part p's rows are o + p * o_part_stride ([n_rows][head_dim]) and
+ * lse + p * lse_part_stride ([n_rows]).  This reads the partials of all ranks
+ * straight out of one all-gathered buffer that packs [o | lse] per rank. */
+tq_status tq_lse_merge_cuda(int n_parts, int64_t n_rows, int head_dim, const float *o, int64_t o_part_stride,
+                            const float *lse, int64_t lse_part_stride, void *out, tq_dtype out_dtype,
+                            float *lse_out, void *stream);
 
 #ifdef __cplusplus
 }

@@ -65,6 +65,9 @@ SIGNATURES = {
     "tq_decode_attention_cuda": (_i32, [_v, _v]),
     "tq_decode_attention_static_cuda": (_i32, [_v, _v]),
     "tq_lse_combine_cuda": (_i32, [_i32, _i64, _i32, _v, _v, _v, _v, _v]),
+    "tq_lse_merge_cuda": (_i32, [_i32, _i64, _i32, _v, _i64, _v, _i64, _v, _i32, _v, _v]),
+    # KV-cache append
+    "tq_kv_append_cuda": (_i32, [_i32, _v, _i32, _v, _i32, _i32, _i32, _i64, _i64, _v, _i32, _i32, _v, _v]),
 }
 
 

@@ -82,12 +82,13 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
                      kv_len: torch.Tensor | None = None, max_kv_len: int | None = None,
                      sm_scale: float | None = None, rotate_q: bool = True, v_rotated: bool = True,
                      out_dtype: torch.dtype = torch.float32, return_lse: bool = False,
-                     out: torch.Tensor | None = None):
+                     out: torch.Tensor | None = None, lse_out: torch.Tensor | None = None):
     """softmax(q~ K^T * sm_scale) V over packed caches; q [B, Hq, D] -> out [B, Hq, D].
 
     kv_len: int32 CUDA tensor [B] of valid tokens (default: the whole capacity);
     max_kv_len: host-side upper bound of kv_len used to plan the split-KV work
-    (default: the capacity).
+    (default: the capacity).  out / lse_out: preallocated contiguous [B, Hq, D]
+    and float32 [B, Hq] destinations (lse_out implies the lse is written).
     """
     _need_cuda(q, k_cache, v_cache)
     if q.dim() != 3 or not q.is_contiguous():
@@ -104,7 +105,13 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     B, Hq, D = q.shape
     if out is None:
         out = torch.empty((B, Hq, D), dtype=out_dtype, device=q.device)
-    lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device) if return_lse else None
+    if lse_out is not None:
+        _need_cuda(lse_out)
+        if lse_out.dtype != torch.float32 or lse_out.numel() != B * Hq or not lse_out.is_contiguous():
+            raise ValueError("lse_out must be a contiguous float32 [B, Hq] tensor")
+        lse = lse_out
+    else:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device) if return_lse else None
     k_type = 4 if k_cache.shape[-1] == 18 else 3
     v_type = 4 if v_cache.shape[-1] == 18 else 3
     a = make_args(q, k_cache, v_cache, kv_len, max_kv_len or 0, sm_scale or 0.0, rotate_q, v_rotated, out, lse,
@@ -118,6 +125,42 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     L.check(lib.tq_decode_attention_cuda(C.byref(a), _stream(q)))
     return (out, lse) if return_lse else out
+
+
+def last_status(device: torch.device | str | int | None = None) -> int:
+    """Kernel-side status of the last decode_attention on `device` (synchronizes its stream).
+
+    0 (TQ_SUCCESS), 7 (TQ_ERROR_TIMEOUT: a bulk copy never completed) or 2
+    (TQ_ERROR_UNSUPPORTED: a block scale of magnitude >= 2^15).
+    """
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    ws = _workspaces.get((dev.type, dev.index))
+    if ws is None:
+        return 0
+    return int(ws[:4].view(torch.int32).item())
+
+
+def merge_partials(parts: torch.Tensor, n_parts: int, n_rows: int, head_dim: int, out: torch.Tensor,
+                   lse_out: torch.Tensor | None = None) -> torch.Tensor:
+    """Log-sum-exp merge of partials packed per part as [o (n_rows*head_dim) | lse (n_rows)] floats.
+
+    parts: contiguous float32 [n_parts * n_rows * (head_dim + 1)] (e.g. the output of
+    an all_gather of every rank's packed partial); out: contiguous [n_rows, head_dim]
+    of float32/float16/bfloat16 (written); lse_out: optional float32 [n_rows].
+    """
+    _need_cuda(parts, out)
+    stride = n_rows * (head_dim + 1)
+    if parts.dtype != torch.float32 or not parts.is_contiguous() or parts.numel() < n_parts * stride:
+        raise ValueError("parts must be a contiguous float32 buffer of n_parts packed partials")
+    if out.dtype not in _DTYPES or not out.is_contiguous() or out.numel() != n_rows * head_dim:
+        raise ValueError("out must be a contiguous [n_rows, head_dim] tensor")
+    base = parts.data_ptr()
+    L.check(_bind().tq_lse_merge_cuda(n_parts, n_rows, head_dim, base, stride, base + 4 * n_rows * head_dim, stride,
+                                      out.data_ptr(), _DTYPES[out.dtype],
+                                      lse_out.data_ptr() if lse_out is not None else None, _stream(parts)))
+    return out
 
 
 def lse_combine(o: torch.Tensor, lse: torch.Tensor, return_lse: bool = False):

@@ -709,26 +709,29 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restri
     if (lse && threadIdx.x == 0) lse[bh] = empty ? -INFINITY : (M + __log2f(L)) * 0.6931471805599453f;
 }
 
-// log-sum-exp merge of P partial results (natural-log lse), e.g. from several ranks
-__global__ void __launch_bounds__(128) lse_combine_kernel(const float* __restrict__ o, const float* __restrict__ lse,
-                                                          float* __restrict__ out, float* __restrict__ lse_out,
-                                                          int P, int64_t n, int D) {
+// log-sum-exp merge of P partial results (natural-log lse), e.g. from several ranks;
+// part p at o + p * o_stride, lse + p * lse_stride
+template <typename OT>
+__global__ void __launch_bounds__(128) lse_combine_kernel(const float* __restrict__ o, int64_t o_stride,
+                                                          const float* __restrict__ lse, int64_t lse_stride,
+                                                          OT* __restrict__ out, float* __restrict__ lse_out, int P,
+                                                          int64_t n, int D) {
     const int64_t i = blockIdx.x;
     float M = -INFINITY;
-    for (int p = 0; p < P; ++p) M = fmaxf(M, lse[(int64_t)p * n + i]);
+    for (int p = 0; p < P; ++p) M = fmaxf(M, lse[(int64_t)p * lse_stride + i]);
     float W = 0.0f;
     for (int p = 0; p < P; ++p) {
-        const float l = lse[(int64_t)p * n + i];
+        const float l = lse[(int64_t)p * lse_stride + i];
         if (l != -INFINITY) W += __expf(l - M);
     }
     for (int e = threadIdx.x; e < D; e += 128) {
         float acc = 0.0f;
         if (M != -INFINITY)
             for (int p = 0; p < P; ++p) {
-                const float l = lse[(int64_t)p * n + i];
-                if (l != -INFINITY) acc += __expf(l - M) * o[((int64_t)p * n + i) * D + e];
+                const float l = lse[(int64_t)p * lse_stride + i];
+                if (l != -INFINITY) acc += __expf(l - M) * o[(int64_t)p * o_stride + i * D + e];
             }
-        out[i * D + e] = M == -INFINITY ? 0.0f : acc / W;
+        store_out<OT>(out + i * D + e, M == -INFINITY ? 0.0f : acc / W);
     }
     if (lse_out && threadIdx.x == 0) lse_out[i] = M == -INFINITY ? -INFINITY : M + __logf(W);
 }
@@ -872,11 +875,28 @@ cudaError_t launch_decode_attention(const AttnRun& r, const AttnPlan& p, void* w
     return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_lse_combine(const float* o, const float* lse, float* out, float* lse_out, int P, int64_t n, int D,
-                               cudaStream_t st) {
-    if (n <= 0) return cudaSuccess;
-    lse_combine_kernel<<<(unsigned)n, 128, 0, st>>>(o, lse, out, lse_out, P, n, D);
-    return cudaGetLastError();
+cudaError_t launch_lse_combine(const float* o, int64_t o_stride, const float* lse, int64_t lse_stride, void* out,
+                               int out_dtype, float* lse_out, int P, int64_t n, int D, cudaStream_t st) {
+    for (int64_t r0 = 0; r0 < n; r0 += 1 << 30) {   // grid.x limit
+        const int64_t nr = n - r0 < (1 << 30) ? n - r0 : (1 << 30);
+        const float* oo = o + r0 * D;
+        const float* ll = lse + r0;
+        float* lo = lse_out ? lse_out + r0 : nullptr;
+        switch (out_dtype) {
+            case DT_F32:
+                lse_combine_kernel<float><<<(unsigned)nr, 128, 0, st>>>(oo, o_stride, ll, lse_stride, (float*)out + r0 * D, lo, P, nr, D);
+                break;
+            case DT_F16:
+                lse_combine_kernel<__half><<<(unsigned)nr, 128, 0, st>>>(oo, o_stride, ll, lse_stride, (__half*)out + r0 * D, lo, P, nr, D);
+                break;
+            default:
+                lse_combine_kernel<__nv_bfloat16><<<(unsigned)nr, 128, 0, st>>>(oo, o_stride, ll, lse_stride, (__nv_bfloat16*)out + r0 * D, lo, P, nr, D);
+                break;
+        }
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 }  // namespace tq

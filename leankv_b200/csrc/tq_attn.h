@@ -33,7 +33,7 @@ struct AttnRun {
 AttnPlan attn_plan(int B, int Hkv, int D, int64_t cap, int64_t max_len);
 size_t attn_workspace_bytes(int B, int Hkv, int D, const AttnPlan& p);
 cudaError_t launch_decode_attention(const AttnRun& r, const AttnPlan& p, void* workspace, cudaStream_t st);
-cudaError_t launch_lse_combine(const float* o, const float* lse, float* out, float* lse_out, int P, int64_t n, int D,
-                               cudaStream_t st);
+cudaError_t launch_lse_combine(const float* o, int64_t o_stride, const float* lse, int64_t lse_stride, void* out,
+                               int out_dtype, float* lse_out, int P, int64_t n, int D, cudaStream_t st);
 
 }  // namespace tq

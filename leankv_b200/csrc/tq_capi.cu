@@ -176,6 +176,37 @@ extern "C" tq_status tq_quantize_cuda(tq_type type, const void* x, tq_dtype x_dt
                        "quantize kernel launch");
 }
 
+extern "C" tq_status tq_kv_append_cuda(tq_type type, const void* src, tq_dtype src_dtype, void* cache, int batch,
+                                       int n_kv_heads, int head_dim, int64_t capacity, int64_t n_new,
+                                       const int32_t* pos, int rotate, int opt_passes, int32_t* overflow,
+                                       void* stream) {
+    g_err[0] = 0;
+    if (!type_ok(type)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown block type %d", (int)type);
+    if (!dtype_ok(src_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown input dtype %d", (int)src_dtype);
+    if (batch < 0 || n_kv_heads <= 0 || capacity < 0 || n_new < 0)
+        return set_error(TQ_ERROR_INVALID_VALUE, "bad batch / head / capacity / row counts");
+    const int l2 = log2_pow2(head_dim);
+    if (l2 < 5 || l2 > 10) return set_error(TQ_ERROR_UNSUPPORTED, "head_dim=%d (supported: powers of two 32..1024)", head_dim);
+    if (opt_passes < 0 || opt_passes > 64) return set_error(TQ_ERROR_INVALID_VALUE, "opt_passes=%d out of [0, 64]", opt_passes);
+    if (opt_passes > 0 && type != TQ_TYPE_TQ3_0) return set_error(TQ_ERROR_UNSUPPORTED, "optimal rounding is defined for TQ3_0 only");
+    const int64_t rows = (int64_t)batch * n_kv_heads * n_new;
+    if (rows == 0 || capacity == 0) return TQ_SUCCESS;
+    if (!src || !cache) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    if (((uintptr_t)src) % dtype_bytes(src_dtype)) return set_error(TQ_ERROR_MISALIGNED, "src not aligned to its element size");
+    if (((uintptr_t)cache) & 15) return set_error(TQ_ERROR_MISALIGNED, "cache must be 16-byte aligned");
+    RowMap map;
+    map.cap = capacity;
+    map.n_new = n_new;
+    map.hkv = n_kv_heads;
+    map.nblk = head_dim / QK;
+    map.pos = pos;
+    map.overflow = overflow;
+    return cuda_status(launch_quantize((int)type, (int)src_dtype, src, cache, rows * (head_dim / QK),
+                                       rotate ? l2 : -1, rotate ? fwht_norm(head_dim) : 1.0f, opt_passes,
+                                       (cudaStream_t)stream, map),
+                       "kv append kernel launch");
+}
+
 extern "C" tq_status tq_dequantize_cuda(tq_type type, const void* x, void* y, tq_dtype y_dtype, int64_t k,
                                         void* stream) {
     g_err[0] = 0;

@@ -62,13 +62,24 @@ extern "C" tq_status tq_decode_attention_cuda(const tq_decode_attention_args* a,
     return cuda_status(launch_decode_attention(r, p, a->workspace, (cudaStream_t)stream), "decode attention launch");
 }
 
-extern "C" tq_status tq_lse_combine_cuda(int n_parts, int64_t n_rows, int head_dim, const float* o, const float* lse,
-                                         float* out, float* lse_out, void* stream) {
+extern "C" tq_status tq_lse_merge_cuda(int n_parts, int64_t n_rows, int head_dim, const float* o,
+                                       int64_t o_part_stride, const float* lse, int64_t lse_part_stride, void* out,
+                                       tq_dtype out_dtype, float* lse_out, void* stream) {
     if (n_parts <= 0 || n_rows < 0 || head_dim <= 0) return set_error(TQ_ERROR_INVALID_VALUE, "bad sizes");
+    if (!dtype_ok(out_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "bad output dtype");
+    if (o_part_stride < 0 || lse_part_stride < 0) return set_error(TQ_ERROR_INVALID_VALUE, "negative part strides");
     if (n_rows == 0) return TQ_SUCCESS;
     if (!o || !lse || !out) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
-    return cuda_status(launch_lse_combine(o, lse, out, lse_out, n_parts, n_rows, head_dim, (cudaStream_t)stream),
-                       "lse combine launch");
+    if (((uintptr_t)out) % dtype_bytes(out_dtype)) return set_error(TQ_ERROR_MISALIGNED, "out not aligned to its element size");
+    return cuda_status(launch_lse_combine(o, o_part_stride, lse, lse_part_stride, out, (int)out_dtype, lse_out, n_parts,
+                                          n_rows, head_dim, (cudaStream_t)stream),
+                       "lse merge launch");
+}
+
+extern "C" tq_status tq_lse_combine_cuda(int n_parts, int64_t n_rows, int head_dim, const float* o, const float* lse,
+                                         float* out, float* lse_out, void* stream) {
+    return tq_lse_merge_cuda(n_parts, n_rows, head_dim, o, n_rows * head_dim, lse, n_rows, out, TQ_DTYPE_F32, lse_out,
+                             stream);
 }
 
 // ── fixed-scratch variant ────────────────────────────────────────────────────

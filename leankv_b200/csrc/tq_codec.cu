@@ -193,6 +193,42 @@ __device__ __forceinline__ void store_staged(uint8_t* __restrict__ dst, const ui
     }
 }
 
+// Head rows of a tile written into a KV cache: head row R of the input (R =
+// s * n_new + t, s = sequence * Hkv + head) goes to token slot pos[sequence] + t
+// of s in a [s][cap][row_bytes] cache.  dst[] holds each row's byte offset
+// (-1: slot outside the cache, not written).  Copies use the widest word that
+// divides the row size (rows and the cache start are 16-byte aligned otherwise).
+template <typename W>
+__device__ __forceinline__ void copy_rows(uint8_t* __restrict__ y, const uint8_t* __restrict__ smem,
+                                          const int64_t* __restrict__ dst, int nr, int row_bytes) {
+    const int wpr = row_bytes / (int)sizeof(W);
+    for (int c = threadIdx.x; c < nr * wpr; c += CODEC_THREADS) {
+        const int r = c / wpr, w = c - r * wpr;
+        const int64_t off = dst[r];
+        if (off >= 0)
+            reinterpret_cast<W*>(y + off)[w] = reinterpret_cast<const W*>(smem + r * row_bytes)[w];
+    }
+}
+
+__device__ __forceinline__ void store_mapped(uint8_t* __restrict__ y, const uint8_t* __restrict__ smem,
+                                             int64_t* __restrict__ s_dst, int64_t b0, int nrows, int bb,
+                                             const RowMap& map) {
+    const int nb = map.nblk, row_bytes = nb * bb, nr = nrows / nb;
+    if (threadIdx.x < nr) {
+        const int64_t R = b0 / nb + threadIdx.x;
+        const int64_t sh = R / map.n_new, t = R - sh * map.n_new;
+        const int64_t slot = (map.pos ? (int64_t)map.pos[sh / map.hkv] : 0) + t;
+        int64_t off = -1;
+        if (slot >= 0 && slot < map.cap) off = (sh * map.cap + slot) * row_bytes;
+        else if (map.overflow) atomicAdd(map.overflow, 1);
+        s_dst[threadIdx.x] = off;
+    }
+    __syncthreads();
+    if ((row_bytes & 7) == 0) copy_rows<uint2>(y, smem, s_dst, nr, row_bytes);
+    else if ((row_bytes & 3) == 0) copy_rows<uint32_t>(y, smem, s_dst, nr, row_bytes);
+    else copy_rows<uint16_t>(y, smem, s_dst, nr, row_bytes);
+}
+
 // ── TQ3 optimal rounding (scripts/tq3_rounding.py:74-125) ───────────────────
 // Coordinate descent over adjacent levels with a least-squares scale.  For an
 // assignment with C = sum x*L and A = sum L^2 the least-squares block MSE is
@@ -259,13 +295,14 @@ __device__ __forceinline__ double tq3_opt_refine(const float (&v)[QK], uint32_t 
 template <int QT, typename IN, int MODE>
 __global__ void __launch_bounds__(CODEC_THREADS)
 quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nblocks,
-                int log2_hd, float norm, int n_passes, int x_vec, int y_vec) {
+                int log2_hd, float norm, int n_passes, int x_vec, int y_vec, const RowMap map) {
     constexpr int EB = ElemBits<IN>::bytes;
     constexpr int ROW_BYTES = QK * EB;
     constexpr int BB = QT == 4 ? TQ4_BYTES : TQ3_BYTES;
     __shared__ __align__(16) uint8_t s_in[CODEC_THREADS * ROW_BYTES];
     __shared__ __align__(16) uint8_t s_out[CODEC_THREADS * BB];
     __shared__ Tq3OptTables s_tbl;
+    __shared__ int64_t s_dst[CODEC_THREADS];   // row-mapped output: byte offset of each head row
 
     if (MODE == 1 && threadIdx.x < 8) {
         const int i = threadIdx.x;
@@ -332,7 +369,8 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
             if (threadIdx.x < nrows) stage_block<3>(s_out, threadIdx.x * BB, dh, w);
         }
         __syncthreads();
-        store_staged(y + b0 * BB, s_out, nrows * BB, y_vec != 0);
+        if (map.cap == 0) store_staged(y + b0 * BB, s_out, nrows * BB, y_vec != 0);
+        else store_mapped(y, s_out, s_dst, b0, nrows, BB, map);
     }
 }
 
@@ -483,33 +521,33 @@ static int codec_grid(int64_t ntiles, int per_sm) {
 
 template <int QT, typename IN>
 static cudaError_t launch_quant_t(const void* x, void* y, int64_t nblocks, int log2_hd, float norm,
-                                  int n_passes, cudaStream_t st) {
+                                  int n_passes, const RowMap& map, cudaStream_t st) {
     const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
     const int grid = codec_grid(ntiles, 16);
     const int xv = ((uintptr_t)x & 15) == 0, yv = ((uintptr_t)y & 15) == 0;
     if (QT == 3 && n_passes > 0)
         quantize_kernel<QT, IN, 1><<<grid, CODEC_THREADS, 0, st>>>((const IN*)x, (uint8_t*)y, nblocks, log2_hd,
-                                                                   norm, n_passes, xv, yv);
+                                                                   norm, n_passes, xv, yv, map);
     else
         quantize_kernel<QT, IN, 0><<<grid, CODEC_THREADS, 0, st>>>((const IN*)x, (uint8_t*)y, nblocks, log2_hd,
-                                                                   norm, 0, xv, yv);
+                                                                   norm, 0, xv, yv, map);
     return cudaGetLastError();
 }
 
 cudaError_t launch_quantize(int qtype, int in_dtype, const void* x, void* y, int64_t nblocks, int log2_hd,
-                            float norm, int n_passes, cudaStream_t st) {
+                            float norm, int n_passes, cudaStream_t st, const RowMap& map) {
     if (nblocks <= 0) return cudaSuccess;
     if (qtype == 4) {
         switch (in_dtype) {
-            case DT_F32: return launch_quant_t<4, float>(x, y, nblocks, log2_hd, norm, 0, st);
-            case DT_F16: return launch_quant_t<4, __half>(x, y, nblocks, log2_hd, norm, 0, st);
-            default: return launch_quant_t<4, __nv_bfloat16>(x, y, nblocks, log2_hd, norm, 0, st);
+            case DT_F32: return launch_quant_t<4, float>(x, y, nblocks, log2_hd, norm, 0, map, st);
+            case DT_F16: return launch_quant_t<4, __half>(x, y, nblocks, log2_hd, norm, 0, map, st);
+            default: return launch_quant_t<4, __nv_bfloat16>(x, y, nblocks, log2_hd, norm, 0, map, st);
         }
     }
     switch (in_dtype) {
-        case DT_F32: return launch_quant_t<3, float>(x, y, nblocks, log2_hd, norm, n_passes, st);
-        case DT_F16: return launch_quant_t<3, __half>(x, y, nblocks, log2_hd, norm, n_passes, st);
-        default: return launch_quant_t<3, __nv_bfloat16>(x, y, nblocks, log2_hd, norm, n_passes, st);
+        case DT_F32: return launch_quant_t<3, float>(x, y, nblocks, log2_hd, norm, n_passes, map, st);
+        case DT_F16: return launch_quant_t<3, __half>(x, y, nblocks, log2_hd, norm, n_passes, map, st);
+        default: return launch_quant_t<3, __nv_bfloat16>(x, y, nblocks, log2_hd, norm, n_passes, map, st);
     }
 }
 

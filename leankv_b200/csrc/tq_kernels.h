@@ -8,10 +8,23 @@ namespace tq {
 
 int sm_count();
 
+// Placement of quantized head rows in a KV cache (cap == 0: contiguous output).
+// Input head row R = s * n_new + t (s = sequence * hkv + head) is written to token
+// slot pos[sequence] + t (pos null: slot t) of s in a [s][cap][nblk blocks] cache;
+// rows whose slot is outside [0, cap) are skipped and counted in *overflow.
+struct RowMap {
+    int64_t cap = 0;
+    int64_t n_new = 1;
+    int hkv = 1;
+    int nblk = 1;
+    const int32_t* pos = nullptr;
+    int* overflow = nullptr;
+};
+
 // [FWHT over heads of 2^log2_hd elements when log2_hd >= 0] + quantize nblocks blocks.
 // qtype 3 or 4; in_dtype DT_F32/DT_F16/DT_BF16; n_passes > 0 selects TQ3 optimal rounding.
 cudaError_t launch_quantize(int qtype, int in_dtype, const void* x, void* y, int64_t nblocks, int log2_hd,
-                            float norm, int n_passes, cudaStream_t st);
+                            float norm, int n_passes, cudaStream_t st, const RowMap& map = RowMap());
 // in-place FWHT of nblocks 32-element rows (heads of 2^log2_hd <= 1024 elements)
 cudaError_t launch_fwht(float* x, int64_t nblocks, int log2_hd, float norm, cudaStream_t st);
 // FWHT of a tail shorter than 32 elements (heads smaller than 32)

@@ -1,0 +1,116 @@
+"""Multi-GPU partitioning of the TurboQuant decode path (one process per GPU).
+
+The decode attention divides two ways:
+
+* By (sequence, KV head).  Each rank owns whole contexts, so ranks never
+  exchange data: ``batch_shard`` gives the rank's sequence range.  This covers
+  the codec and short or medium contexts (the streaming append + decode path).
+* By token position, for long contexts.  Every rank holds one contiguous token
+  range of every (sequence, KV head) context (``token_shard``).  It computes
+  attention over that range together with its log-sum-exp, and the partials are
+  merged exactly:
+
+      M = max_r lse_r,   O = sum_r e^{lse_r - M} O_r / sum_r e^{lse_r - M},
+      lse = M + log sum_r e^{lse_r - M}
+
+  The single exchange is one all_gather of every rank's packed [O_r | lse_r]
+  (batch * n_q_heads * (head_dim + 1) float32 values) over the process group,
+  which is NCCL over NVLink on a B200 node.  Each rank then merges the P partials
+  itself (tq_lse_merge_cuda), so every rank ends up holding the full output.
+
+The output rotation (FWHT) is linear and is applied inside each rank's partial;
+the merge is a convex combination, so it commutes with the rotation.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+from . import attention
+
+
+def batch_shard(batch: int, rank: int, world: int) -> tuple[int, int]:
+    """[start, stop) of the sequences owned by `rank` (contiguous, sizes differ by at most one)."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("bad rank / world size")
+    base, extra = divmod(batch, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def token_shard(context: int, rank: int, world: int) -> tuple[int, int]:
+    """[start, stop) of the token positions held by `rank` for a context of `context` tokens.
+
+    Ranges are contiguous, in rank order, and start on even positions (cache
+    capacities stay even, as the decode attention requires); trailing ranks may
+    get fewer tokens, or none, when the context is short.
+    """
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("bad rank / world size")
+    per = -(-context // world)
+    per += per & 1
+    start = min(rank * per, context)
+    return start, min(start + per, context)
+
+
+def local_lengths(kv_len: torch.Tensor, start: int, stop: int) -> torch.Tensor:
+    """Valid tokens of each sequence inside the shard [start, stop): clamp(kv_len - start, 0, stop - start)."""
+    return (kv_len.to(torch.int64) - start).clamp_(0, stop - start).to(torch.int32)
+
+
+class SplitSequenceAttention:
+    """Decode attention over contexts split across ranks by token position.
+
+    Call it on every rank of `group` with the same query and that rank's shard of
+    the caches (``token_shard``); all ranks return the merged output.  Buffers for
+    the exchange are allocated once per shape and reused, so steps issue no
+    allocation.
+
+    ``attend(q, k, v, kv_len, max_kv_len, o_out, lse_out)`` and
+    ``merge(parts, n_parts, n_rows, head_dim, out)`` default to the CUDA
+    kernels; they are parameters so that the exchange logic can run on CPU ranks
+    (gloo) with CPU stand-ins.
+    """
+
+    def __init__(self, group=None, attend: Callable | None = None, merge: Callable | None = None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        self._attend = attend or self._cuda_attend
+        self._merge = merge or attention.merge_partials
+        self._bufs: dict = {}
+
+    @staticmethod
+    def _cuda_attend(q, k, v, kv_len, max_kv_len, o_out, lse_out, **kw):
+        attention.decode_attention(q, k, v, kv_len=kv_len, max_kv_len=max_kv_len, out=o_out, lse_out=lse_out,
+                                   return_lse=True, **kw)
+
+    def _buffers(self, n_rows: int, head_dim: int, device):
+        key = (n_rows, head_dim, str(device))
+        b = self._bufs.get(key)
+        if b is None:
+            per = n_rows * (head_dim + 1)
+            send = torch.empty(per, dtype=torch.float32, device=device)
+            recv = torch.empty(self.world * per, dtype=torch.float32, device=device)
+            b = self._bufs[key] = (send, recv)
+        return b
+
+    def __call__(self, q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,
+                 kv_len_local: torch.Tensor | None = None, max_kv_len: int | None = None,
+                 out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float32, **kw) -> torch.Tensor:
+        B, Hq, D = q.shape
+        n = B * Hq
+        send, recv = self._buffers(n, D, q.device)
+        o_local = send[: n * D].view(B, Hq, D)
+        lse_local = send[n * D:].view(B, Hq)
+        self._attend(q, k_shard, v_shard, kv_len_local, max_kv_len, o_local, lse_local, **kw)
+        if out is None:
+            out = torch.empty((B, Hq, D), dtype=out_dtype, device=q.device)
+        if self.world == 1:
+            self._merge(send, 1, n, D, out.view(n, D))
+            return out
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+        self._merge(recv, self.world, n, D, out.view(n, D))
+        return out

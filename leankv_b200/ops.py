@@ -97,3 +97,40 @@ def hadamard_(x: torch.Tensor, head_dim: int) -> torch.Tensor:
         raise ValueError("x must be a contiguous float32 tensor")
     L.check(L.load().tq_hadamard_cuda(x.data_ptr(), x.numel(), int(head_dim), _stream(x)))
     return x
+
+
+def kv_append(src: torch.Tensor, cache: torch.Tensor, pos: torch.Tensor | None = None, qtype=None,
+              rotate: bool = True, opt_passes: int = 0, overflow: torch.Tensor | None = None) -> torch.Tensor:
+    """Quantize-on-write of new head rows into a packed KV cache (tq_kv_append_cuda).
+
+    src [batch, n_kv_heads, n_new, head_dim] (f32/f16/bf16); cache uint8
+    [batch, n_kv_heads, capacity, head_dim/32, block_bytes]; row t of (b, h) lands
+    in token slot pos[b] + t (pos: int32 CUDA tensor [batch], None = slot t).
+    rotate applies the head_dim Hadamard rotation first.  Slots outside the
+    capacity are skipped and counted into overflow (int32 CUDA tensor [1]) when
+    given.  Returns cache.
+    """
+    _need_cuda(src, cache)
+    if src.dim() != 4 or not src.is_contiguous() or src.dtype not in _DTYPES:
+        raise ValueError("src must be a contiguous f32/f16/bf16 [batch, n_kv_heads, n_new, head_dim] tensor")
+    if cache.dim() != 5 or cache.dtype != torch.uint8 or not cache.is_contiguous():
+        raise ValueError("cache must be a contiguous uint8 [batch, n_kv_heads, capacity, head_dim/32, bytes] tensor")
+    B, H, n_new, D = src.shape
+    if qtype is None:
+        qtype = TQ4_0 if cache.shape[-1] == BLOCK_BYTES[TQ4_0] else TQ3_0
+    q = _qtype(qtype)
+    if cache.shape[0] != B or cache.shape[1] != H or cache.shape[3] * QK != D or cache.shape[4] != BLOCK_BYTES[q]:
+        raise ValueError(f"cache shape {tuple(cache.shape)} does not match src {tuple(src.shape)} / type {q}")
+    if pos is not None:
+        _need_cuda(pos)
+        if pos.dtype != torch.int32 or pos.numel() != B or not pos.is_contiguous():
+            raise ValueError("pos must be a contiguous int32 [batch] tensor")
+    if overflow is not None:
+        _need_cuda(overflow)
+        if overflow.dtype != torch.int32:
+            raise ValueError("overflow must be an int32 tensor")
+    L.check(L.load().tq_kv_append_cuda(q, src.data_ptr(), _DTYPES[src.dtype], cache.data_ptr(), B, H, D,
+                                       cache.shape[2], n_new, pos.data_ptr() if pos is not None else None,
+                                       int(rotate), int(opt_passes),
+                                       overflow.data_ptr() if overflow is not None else None, _stream(src)))
+    return cache

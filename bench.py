@@ -242,38 +242,84 @@ class Codec:
         return sample_bytes / dt / 1e9, tokens
 
 
-class Attn:
-    """Fused TQ4/TQ4 decode attention, B16 Hq32 Hkv8 D128 ctx 32768 (3 launches per step)."""
+def _outlier_rows(g, shape, hd):
+    """N(0,1) rows with 4 outlier channels per KV head scaled x20 (the C1 generator); shape [..., H, T, hd]."""
+    import torch
+    x = torch.randn(*shape, generator=g, device="cuda")
+    H = shape[-3]
+    for h in range(H):
+        ch = torch.randperm(hd, generator=g, device="cuda")[:4]
+        x[..., h, :, ch] *= 20.0
+    return x
 
-    def __init__(self, rank, tokens=None):
+
+class Attn:
+    """Fused decode attention.
+
+    attn (C3): TQ4_0 K/V, B16 Hq32 Hkv8 D128 ctx 32768; ranks split the batch (no collective).
+    c4   (C4): TQ3_0 K / TQ4_0 V, B64 Hq64 Hkv8 D128 ctx 131072; ranks split every context by
+               token position, then one all_gather of the packed (O, lse) partials over NCCL and a
+               log-sum-exp merge on every rank.
+    Both keep the total work fixed as ranks are added ("strong" scaling).
+    """
+
+    def __init__(self, name, rank, ws, tokens=None):
         import torch
-        from leankv_b200 import attention, ops
+        from leankv_b200 import attention, distributed, ops
         self.attention = attention
-        B, Hq, Hkv, D = 16, 32, 8, 128
-        T = tokens or 32768
-        g = torch.Generator(device="cuda").manual_seed(3 + 1000 * rank)
-        kc = torch.empty(B, Hkv, T, D // 32, 18, dtype=torch.uint8, device="cuda")
-        vc = torch.empty_like(kc)
-        for cache in (kc, vc):          # N(0,1) rows, 4 outlier channels per head x20, rotated + quantized
-            for b in range(B):
-                x = torch.randn(Hkv, T, D, generator=g, device="cuda")
-                for h in range(Hkv):
-                    ch = torch.randperm(D, generator=g, device="cuda")[:4]
-                    x[h, :, ch] *= 20.0
-                ops.quantize(x, 4, fwht_head_dim=D, out=cache[b])
+        self.name = name
+        self.ws = ws
+        if name == "attn":
+            B, Hq, Hkv, D, T, kt = 16, 32, 8, 128, tokens or 32768, 4
+            b0, b1 = distributed.batch_shard(B, rank, ws)
+            s0, s1 = 0, T
+        else:
+            B, Hq, Hkv, D, T, kt = 64, 64, 8, 128, tokens or 131072, 3
+            b0, b1 = 0, B
+            s0, s1 = distributed.token_shard(T, rank, ws)
+        Bl, L = b1 - b0, s1 - s0
+        g = torch.Generator(device="cuda").manual_seed((3 if name == "attn" else 4) + 1000 * rank)
+        kb = 18 if kt == 4 else 14
+        kc = torch.empty(Bl, Hkv, L, D // 32, kb, dtype=torch.uint8, device="cuda")
+        vc = torch.empty(Bl, Hkv, L, D // 32, 18, dtype=torch.uint8, device="cuda")
+        for cache, qt in ((kc, kt), (vc, 4)):          # rotated + quantized rows
+            for b in range(Bl):
+                ops.quantize(_outlier_rows(g, (Hkv, L, D), D), qt, fwht_head_dim=D, out=cache[b])
         self.kc, self.vc = kc, vc
-        self.q = torch.randn(B, Hq, D, generator=g, device="cuda").half()
-        self.out = torch.empty(B, Hq, D, dtype=torch.float16, device="cuda")
+        gq = torch.Generator(device="cuda").manual_seed(5)           # the same queries on every rank
+        qfull = torch.randn(B, Hq, D, generator=gq, device="cuda").half()
+        self.q = qfull[b0:b1].contiguous()
+        self.out = torch.empty(Bl, Hq, D, dtype=torch.float16, device="cuda")
+        self.L = L
+        self.split = name == "c4" and ws > 1
+        if self.split:
+            self.att = distributed.SplitSequenceAttention()
+            self.lens = torch.full((Bl,), L, dtype=torch.int32, device="cuda")
         kv_bytes = kc.numel() + vc.numel()
-        self.bytes_per_step = kv_bytes + self.q.numel() * 2 + self.out.numel() * 2
-        self.launches_per_step = 3
-        self.config = {"workload": "fused TQ4_0/TQ4_0 decode attention (FWHT(q), split-KV, LSE combine, FWHT(o))",
-                       "shape": f"B={B} Hq={Hq} Hkv={Hkv} D={D} ctx={T}, fp16 q/out",
-                       "kv_bytes": kv_bytes}
-        self.dtype = "TQ4 blocks -> f16 MMA, f32 accumulate"
+        self.bytes_per_step = kv_bytes + self.q.numel() * 2 + self.out.numel() * 2          # this rank
+        kv_total = B * Hkv * T * (D // 32) * (kb + 18)
+        self.job_bytes = kv_total + B * Hq * D * 2 * 2                                       # all ranks
+        self.launches_per_step = 4 if self.split else 3
+        self.scaling = "strong"
+        self.flush_l2 = False
+        self.l2_note = f"KV {kv_total / 1e9:.2f} GB per step (> L2 126 MB), no flush"
+        if name == "attn":
+            self.config = {"workload": "C3 fused TQ4_0/TQ4_0 decode attention (FWHT(q), split-KV, LSE combine, FWHT(o))",
+                           "shape": f"B={B} Hq={Hq} Hkv={Hkv} D={D} ctx={T}, fp16 q/out", "kv_bytes": kv_total}
+            self.parallelism = f"batch shards x{ws} (sequences {b0}..{b1 - 1} on rank {rank}), no collective"
+        else:
+            self.config = {"workload": "C4 fused TQ3_0-K / TQ4_0-V decode attention, split-KV by sequence",
+                           "shape": f"B={B} Hq={Hq} Hkv={Hkv} D={D} ctx={T}, fp16 q/out", "kv_bytes": kv_total}
+            self.parallelism = (f"token shards x{ws} ({L} tokens per rank); all_gather of packed (O, lse) over NCCL "
+                                "+ LSE merge on every rank" if ws > 1 else "one GPU holds the whole context")
+        self.dtype = "TQ blocks -> f16 MMA, f32 accumulate"
+        self.e2e_path = "leankv_b200 decode attention, q H2D and out D2H from pinned host memory"
 
     def step(self):
-        self.attention.decode_attention(self.q, self.kc, self.vc, out=self.out)
+        if self.split:
+            self.att(self.q, self.kc, self.vc, self.lens, self.L, out=self.out)
+        else:
+            self.attention.decode_attention(self.q, self.kc, self.vc, out=self.out)
 
     def e2e_setup(self):
         self.hq = self.q.cpu().pin_memory()
@@ -282,7 +328,7 @@ class Attn:
     def e2e_step(self):
         import torch
         self.q.copy_(self.hq, non_blocking=True)
-        self.attention.decode_attention(self.q, self.kc, self.vc, out=self.out)
+        self.step()
         self.hout.copy_(self.out, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
@@ -291,31 +337,183 @@ class Attn:
 
     def cpu_run(self, frac, nthreads, impl):
         from oracle import oracle as O
-        n = max(1, self.q.shape[0] // frac)
+        n = 1
         q = self.q[:n].float().cpu().numpy()
         kc, vc = self.kc[:n].cpu().numpy(), self.vc[:n].cpu().numpy()
         t0 = time.perf_counter()
-        O.decode_attention(q, kc, 4, vc, 4, self.kc.shape[1], nthreads=nthreads)
+        O.decode_attention(q, kc, 4 if kc.shape[-1] == 18 else 3, vc, 4, self.kc.shape[1], nthreads=nthreads)
         dt = time.perf_counter() - t0
         return self.bytes_per_step * n / self.q.shape[0] / dt / 1e9, n
 
+    def cpu_sample_note(self, n, nthreads):
+        return (f"{n} of {self.q.shape[0]} sequences, {nthreads} threads; float64 restatement: reference "
+                "dequantize_row_tq*_0 + hadamard_transform + exact softmax (no reference CPU attention exists)")
 
-def make_workload(name, rank, tokens):
-    if name == "attn":
-        return Attn(rank, tokens)
+
+class Stream:
+    """C5 streaming append + decode: 80 layers of a KV cache (8 KV heads, head_dim 256, TQ4_0 K/V).
+
+    Prefill quantizes 16384 bf16 tokens per sequence into every layer (quantize-on-write with the
+    head_dim Hadamard rotation).  A step is one decode step of all 80 layers: append one token's K
+    and V per sequence at its current length, then decode attention (32 query heads, group 4) over
+    the grown context.  The 80-layer step (400 kernel launches) is captured once in a CUDA graph
+    and replayed; the append slots and lengths live on the device and advance inside the graph.
+    Ranks split the batch of 32 ("strong" scaling, no collective).
+    """
+    LAYERS, HKV, HQ, D, BATCH, GROWTH = 80, 8, 32, 256, 32, 256
+
+    def __init__(self, rank, ws, tokens=None, layers=None):
+        import torch
+        from leankv_b200 import attention, distributed, ops
+        self.attention, self.ops = attention, ops
+        self.nl = layers or self.LAYERS
+        b0, b1 = distributed.batch_shard(self.BATCH, rank, ws)
+        B = self.B = b1 - b0
+        H, D, Hq = self.HKV, self.D, self.HQ
+        T0 = tokens or 16384
+        cap = self.cap = T0 + self.GROWTH
+        nb = D // 32
+        self.kc = [torch.empty(B, H, cap, nb, 18, dtype=torch.uint8, device="cuda") for _ in range(self.nl)]
+        self.vc = [torch.empty(B, H, cap, nb, 18, dtype=torch.uint8, device="cuda") for _ in range(self.nl)]
+        g = torch.Generator(device="cuda").manual_seed(5 + 1000 * rank)
+        # prefill: inputs generated on the device layer by layer (bf16), quantize-on-write timed with events
+        chunk = max(1, min(B, (1 << 28) // (H * T0 * D)))
+        pre_ms, pre_bytes = 0.0, 0
+        for l in range(self.nl):
+            for cache in (self.kc[l], self.vc[l]):
+                for c0 in range(0, B, chunk):
+                    c1 = min(B, c0 + chunk)
+                    x = _outlier_rows(g, (c1 - c0, H, T0, D), D).to(torch.bfloat16)
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    ops.kv_append(x, cache[c0:c1])
+                    e1.record()
+                    e1.synchronize()
+                    pre_ms += e0.elapsed_time(e1)
+                    pre_bytes += x.numel() * 2 + x.numel() // 32 * 18
+                    del x
+        self.prefill = {"ms": round(pre_ms, 3), "bytes": pre_bytes, "GB_per_s": round(pre_bytes / pre_ms / 1e6, 1),
+                        "tokens_per_seq": T0, "launches": self.nl * 2 * ((B + chunk - 1) // chunk)}
+        # decode-step inputs for all layers in single buffers (one H2D / D2H each in e2e)
+        self.k_new = torch.randn(self.nl, B, H, 1, D, generator=g, device="cuda").to(torch.bfloat16)
+        self.v_new = torch.randn(self.nl, B, H, 1, D, generator=g, device="cuda").to(torch.bfloat16)
+        self.q = torch.randn(self.nl, B, Hq, D, generator=g, device="cuda").to(torch.bfloat16)
+        self.out = torch.empty(self.nl, B, Hq, D, dtype=torch.bfloat16, device="cuda")
+        self.pos = torch.full((B,), T0, dtype=torch.int32, device="cuda")     # append slot = current length
+        self.len1 = self.pos + 1                                                 # length after the append
+        self.T0 = T0
+        self.steps_done = 0
+        for _ in range(2):                       # eager steps: workspace, kernel attributes, lazy init
+            self._body()
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._body()
+        self.steps_done -= 1                     # capture records the step without running it
+        self.launches_per_step = self.nl * 5
+        per_tok = H * nb * 18 * 2                                       # K + V bytes per token and sequence
+        self._per_tok = per_tok
+        self.scaling = "strong"
+        self.flush_l2 = False
+        self.l2_note = "cache > 10 GB per rank (> L2 126 MB), no flush"
+        self.config = {"workload": "C5 streaming append + decode, 80-layer TQ4_0 KV cache, one CUDA graph per step",
+                       "shape": f"batch {self.BATCH} (x{ws} ranks: {B} each) Hkv={H} Hq={Hq} D={D} prefill {T0} "
+                                f"+ up to {self.GROWTH} appended tokens, bf16 inputs/outputs",
+                       "layers": self.nl, "prefill": self.prefill}
+        self.parallelism = f"batch shards x{ws}, all layers local, no collective"
+        self.dtype = "bf16 -> TQ4 blocks; TQ4 -> f16 MMA, f32 accumulate"
+        self.e2e_path = ("CUDA graph of the 80-layer step; new K/V/q H2D and outputs D2H from pinned host memory "
+                         "(one copy each)")
+        self.job_ranks = ws
+
+    def _body(self):
+        for l in range(self.nl):
+            self.ops.kv_append(self.k_new[l], self.kc[l], self.pos)
+            self.ops.kv_append(self.v_new[l], self.vc[l], self.pos)
+            self.attention.decode_attention(self.q[l], self.kc[l], self.vc[l], kv_len=self.len1,
+                                            max_kv_len=self.cap, out=self.out[l])
+        self.pos += 1
+        self.len1 += 1
+        self.steps_done += 1
+
+    @property
+    def bytes_per_step(self):
+        # K/V read at the mean context of the timed steps + appended rows (bf16 in, blocks out) + q/out
+        ctx = self.T0 + self.steps_done + 1      # the step attends over the appended token too
+        B, H, D, Hq = self.B, self.HKV, self.D, self.HQ
+        per_layer = B * ctx * self._per_tok + 2 * B * H * D * 2 + 2 * B * H * (D // 32) * 18 + 2 * B * Hq * D * 2
+        return per_layer * self.nl
+
+    @property
+    def job_bytes(self):
+        return self.bytes_per_step * self.BATCH // self.B
+
+    def step(self):
+        self.graph.replay()
+        self.steps_done += 1
+
+    def remaining(self):
+        return self.GROWTH - self.steps_done
+
+    def e2e_setup(self):
+        self.hk = self.k_new.cpu().pin_memory()
+        self.hv = self.v_new.cpu().pin_memory()
+        self.hq = self.q.cpu().pin_memory()
+        self.hout = self.out.cpu().pin_memory()
+
+    def e2e_step(self):
+        import torch
+        self.k_new.copy_(self.hk, non_blocking=True)
+        self.v_new.copy_(self.hv, non_blocking=True)
+        self.q.copy_(self.hq, non_blocking=True)
+        self.step()
+        self.hout.copy_(self.out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    def e2e_bytes(self):
+        return (self.hk.numel() + self.hv.numel() + self.hq.numel()) * 2, self.hout.numel() * 2
+
+    def cpu_run(self, frac, nthreads, impl):
+        """One layer of one sequence of the decode step on the host (float64 restatement), scaled per byte."""
+        from oracle import oracle as O
+        ctx = int(self.len1[0].item())
+        kc = self.kc[0][:1, :, :ctx].cpu().numpy()
+        vc = self.vc[0][:1, :, :ctx].cpu().numpy()
+        q = self.q[0][:1].float().cpu().numpy()
+        t0 = time.perf_counter()
+        O.decode_attention(q, kc, 4, vc, 4, self.HKV, nthreads=nthreads)
+        dt = time.perf_counter() - t0
+        return (kc.size + vc.size) / dt / 1e9, 1
+
+    def cpu_sample_note(self, n, nthreads):
+        return (f"attention of 1 layer x 1 sequence at the current context, {nthreads} threads, GB/s of cache read; "
+                "float64 restatement (reference dequantize_row_tq4_0 + hadamard_transform + exact softmax); the "
+                "append's quantize is the reference hadamard_transform_row + quantize_row_tq4_0 (timed in tq4)")
+
+
+def make_workload(name, rank, tokens, ws=1, layers=None):
+    if name in ("attn", "c4"):
+        return Attn(name, rank, ws, tokens)
+    if name == "c5":
+        return Stream(rank, ws, tokens, layers)
     return Codec(name, rank, tokens)
 
 
 def run_ours(args, ws, rank, local):
     import torch
-    wl = make_workload(args.workload, rank, args.tokens)
+    wl = make_workload(args.workload, rank, args.tokens, ws, args.layers)
+    if isinstance(wl, Stream):
+        budget = wl.remaining() - (0 if args.no_e2e else min(args.steps, 20) + 1)
+        if args.warmup + args.steps > budget:
+            raise SystemExit(f"c5: warmup + steps must stay within the {budget} free cache slots")
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
-    flush_l2 = args.workload != "attn"     # the attention step streams 604 MB (> L2) by itself
+    flush_l2 = getattr(wl, "flush_l2", True)
     for _ in range(args.warmup):
         wl.step()
     torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    step_bytes = []
     barrier(ws)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
@@ -323,6 +521,7 @@ def run_ours(args, ws, rank, local):
         for i in range(args.steps):
             if flush_l2:
                 flush.zero_()                  # evict inputs from L2 between steps
+            step_bytes.append(wl.bytes_per_step)
             starts[i].record()
             wl.step()
             ends[i].record()
@@ -332,26 +531,28 @@ def run_ours(args, ws, rank, local):
     per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     ms = statistics.mean(per)
     ms_max = max_over_ranks(ms, ws)
-    value = wl.bytes_per_step * ws / (ms_max * 1e-3) / 1e9
+    rank_bytes = statistics.mean(step_bytes)
+    job_bytes = getattr(wl, "job_bytes", None)
+    job_bytes = job_bytes if job_bytes is not None else rank_bytes * ws
+    value = job_bytes / (ms_max * 1e-3) / 1e9
     peak, peak_kind = hbm_peak()
-    achieved = wl.bytes_per_step / (ms * 1e-3) / 1e9
+    achieved = rank_bytes / (ms * 1e-3) / 1e9
 
-    # e2e through the C ABI (host buffers)
+    # e2e through the public API with host buffers
     e2e = None
     if not args.no_e2e:
         wl.e2e_setup()
         wl.e2e_step()
-        n_e2e = min(args.steps, 50)
+        n_e2e = min(args.steps, 20 if isinstance(wl, Stream) else 50)
         barrier(ws)
         t0 = time.perf_counter()
         for _ in range(n_e2e):
             wl.e2e_step()
         e2e_s = max_over_ranks((time.perf_counter() - t0) / n_e2e, ws)
         h2d, d2h = wl.e2e_bytes()
-        e2e = {"value": round(wl.bytes_per_step * ws / e2e_s / 1e9, 3), "unit": "GB/s",
+        e2e = {"value": round(job_bytes / e2e_s / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "path": ("leankv_b200.attention.decode_attention, q H2D and out D2H from pinned host memory"
-                        if isinstance(wl, Attn) else "tq_quantize_host (C ABI, pinned host buffers)"),
+               "path": getattr(wl, "e2e_path", "tq_quantize_host (C ABI, pinned host buffers)"),
                "steps": n_e2e}
 
     out = None
@@ -359,11 +560,10 @@ def run_ours(args, ws, rank, local):
         cpu = None
         if ws == 1 and not args.no_cpu_baseline:
             n = os.cpu_count() or 1
-            if isinstance(wl, Attn):
+            if isinstance(wl, (Attn, Stream)):
                 v, nseq = wl.cpu_run(16, n, "port")
                 cpu = {"value": round(v, 4), "unit": "GB/s", "cores": n, "kind": "port",
-                       "sample": f"{nseq} of {wl.q.shape[0]} sequences (1/16 of the step), {n} threads; float64 "
-                                 "restatement: reference dequantize_row_tq4_0 + hadamard_transform + exact softmax"}
+                       "sample": wl.cpu_sample_note(nseq, n)}
             else:
                 impl = "port" if wl.passes else "reference"
                 v, tokens = wl.cpu_run(16, n, impl)
@@ -372,21 +572,23 @@ def run_ours(args, ws, rank, local):
                        "sample": f"{tokens} of {wl.x.shape[0]} tokens (1/16 of the workload), {n} threads; "
                                  + ("C restatement of scripts/tq3_rounding.py + reference hadamard_transform_row"
                                     if wl.passes else "reference src/ggml-tq.c hadamard_transform_row + quantize_row")}
+        is_codec = isinstance(wl, Codec)
         out = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_max, 6), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 6), "higher_is_better": True,
+            "scaling": getattr(wl, "scaling", "weak"),
             "vs_baseline": None, "dtype": wl.dtype,
             "data": "synthetic (seeded)",
             "config": {**wl.config,
-                       "parallelism": (f"{ws} independent replicas of the step (batch x KV-head shards), no collective"
-                                       if isinstance(wl, Attn) else f"token-row shards x{ws}, no collective"),
-                       "l2": ("inputs 604 MB > L2 (126 MB), no flush" if isinstance(wl, Attn)
-                              else "flushed (256 MiB write) between timed steps")},
+                       "parallelism": getattr(wl, "parallelism", f"token-row shards x{ws}, no collective"),
+                       "l2": getattr(wl, "l2_note", "flushed (256 MiB write) between timed steps")},
             "us_per_step": round(ms_max * 1e3, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "traffic": profile_traffic(args.workload),
-                         "algorithmic_bytes_per_launch": wl.bytes_per_step},
+                         "algorithmic_bytes_per_launch": int(rank_bytes) if is_codec else None,
+                         "algorithmic_bytes_per_step_per_rank": int(rank_bytes),
+                         "timed": "the kernel" if is_codec else "the whole step on the launching stream"},
             "e2e": e2e,
             "gpu_launches": args.steps * wl.launches_per_step,
             "clocks": clk.summary(),
@@ -455,15 +657,16 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["tq3opt", "tq4", "attn"], default="tq3opt")
+    ap.add_argument("--workload", choices=["tq3opt", "tq4", "attn", "c4", "c5"], default="tq3opt")
+    ap.add_argument("--layers", type=int, default=None, help="c5: override the layer count (profiling runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-API measurement (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the token count (profiling runs)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 3 if args.impl == "reference" else (200 if args.workload == "attn" else 2000)
+        args.steps = 3 if args.impl == "reference" else {"attn": 200, "c4": 50, "c5": 40}.get(args.workload, 2000)
     if args.warmup is None:
-        args.warmup = 3 if args.impl == "reference" else 20
+        args.warmup = 3 if args.impl == "reference" else {"c4": 5, "c5": 5}.get(args.workload, 20)
     args.warmup = max(args.warmup, 3)
 
     if args.impl == "reference":

@@ -814,9 +814,17 @@ static cudaError_t launch_combine(const float* part, void* out, float* lse, int 
 template <int D, int KT, int RES>
 static cudaError_t launch_decode_kernel(const AttnKernelArgs& a, int grid, cudaStream_t st) {
     const size_t smem = decode_smem_bytes<D, KT>();
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, KT, RES>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // the shared-memory opt-in is set once per device, so that later calls (for example
+    // inside a CUDA graph capture) issue only stream work
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        e = cudaFuncSetAttribute(attn_decode_kernel<D, KT, RES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
     attn_decode_kernel<D, KT, RES><<<grid, AttnCfg<D, KT>::THREADS, smem, st>>>(a);
     return cudaGetLastError();
 }

@@ -77,6 +77,33 @@ __device__ __forceinline__ void load_tile(uint8_t* __restrict__ smem, const IN* 
     }
 }
 
+// asynchronous tile load (16-byte aligned input): each thread issues cp.async copies of
+// its chunks straight into the swizzled tile; completion is awaited with cp_async_wait
+template <typename IN>
+__device__ __forceinline__ void load_tile_async(uint8_t* __restrict__ smem, const IN* __restrict__ src, int nrows) {
+    constexpr int ROW_BYTES = QK * ElemBits<IN>::bytes;
+    constexpr int CPR = ROW_BYTES / 16;
+    const char* s8 = reinterpret_cast<const char*>(src);
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem);
+    if (nrows == CODEC_THREADS) {
+#pragma unroll
+        for (int i = 0; i < CPR; ++i) {
+            const int c = threadIdx.x + i * CODEC_THREADS;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sbase + tile_chunk_addr<ROW_BYTES>(c / CPR, c % CPR)),
+                         "l"(s8 + 16 * (size_t)c)
+                         : "memory");
+        }
+    } else {
+        for (int c = threadIdx.x; c < nrows * CPR; c += CODEC_THREADS)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sbase + tile_chunk_addr<ROW_BYTES>(c / CPR, c % CPR)),
+                         "l"(s8 + 16 * (size_t)c)
+                         : "memory");
+    }
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // thread-private read of row r as 32 floats (exact conversion from 16-bit)
 template <typename IN>
 __device__ __forceinline__ void read_row(const uint8_t* __restrict__ smem, int r, float (&v)[QK]) {
@@ -111,17 +138,23 @@ __device__ __forceinline__ void read_row(const uint8_t* __restrict__ smem, int r
 // ── Walsh-Hadamard transform of one head spread over D/32 lanes ─────────────
 // Stage h combines elements j and j+h as (x[j] + x[j+h], x[j] - x[j+h]),
 // h = 1, 2, 4, ... (src/ggml-tq.c:365-374), then scales by norm.
-__device__ __forceinline__ void fwht_block(float (&v)[QK], int log2_hd, float norm) {
+// L2 >= -1 fixes log2(head_dim) at compile time (-1: no rotation), so every stage
+// unrolls without branches; L2 = -2 reads it from log2_hd at run time.
+template <int L2 = -2>
+__device__ __forceinline__ void fwht_block(float (&v)[QK], int log2_hd_rt, float norm) {
+    const int log2_hd = L2 >= -1 ? L2 : log2_hd_rt;
     // Packed fp32x2 adds: every lane of an f32x2 operation is an ordinary
     // round-to-nearest fp32 operation, and a - b is computed as fma(b, -1, a)
     // (b * -1 is exact, one rounding), so the results equal the scalar code.
+    // Register pairs are (v[2i], v[2i+1]) for every packed stage, so no stage needs moves;
+    // h = 1 combines the two halves of a pair and runs as scalar operations.
     const float2 m1 = make_float2(-1.0f, -1.0f);
-    if (log2_hd >= 1) {   // h = 1: pairs (j, j+1); two butterflies per packed op
+    if (log2_hd >= 1) {
 #pragma unroll
-        for (int j = 0; j < QK; j += 4) {
-            const float2 a = make_float2(v[j], v[j + 2]), b = make_float2(v[j + 1], v[j + 3]);
-            const float2 sum = __fadd2_rn(a, b), dif = __ffma2_rn(b, m1, a);
-            v[j] = sum.x; v[j + 2] = sum.y; v[j + 1] = dif.x; v[j + 3] = dif.y;
+        for (int j = 0; j < QK; j += 2) {
+            const float a = v[j], b = v[j + 1];
+            v[j] = __fadd_rn(a, b);
+            v[j + 1] = __fmaf_rn(b, -1.0f, a);
         }
     }
 #pragma unroll
@@ -137,7 +170,8 @@ __device__ __forceinline__ void fwht_block(float (&v)[QK], int log2_hd, float no
             }
         }
     }
-    for (int s = 5; s < log2_hd; ++s) {   // h >= 32: partner lane = lane ^ (h / 32)
+#pragma unroll
+    for (int s = 5; s < (L2 >= -1 ? (L2 > 5 ? L2 : 5) : log2_hd); ++s) {   // h >= 32: partner lane = lane ^ (h / 32)
         const int lane_bit = 1 << (s - 5);
         // lower element: self + partner = fma(self, 1, partner); upper: partner - self = fma(self, -1, partner)
         const float sg = (threadIdx.x & lane_bit) ? -1.0f : 1.0f;
@@ -290,20 +324,91 @@ __device__ __forceinline__ double tq3_opt_refine(const float (&v)[QK], uint32_t 
     return A == 0.0 ? 0.0 : C / A;
 }
 
+// ── nearest level by table ─────────────────────────────────────────────────
+// bin(xn) = round(16 xn + 16) is the low 6 mantissa bits of fma(xn, 16, 1.5 * 2^23 + 16)
+// (one ulp is 1 at that magnitude, and round-to-nearest is monotone in xn).  Each
+// boundary B_k has a bin too; for every bin j the table holds
+//   cnt_j = #{k : bin(B_k) < j}   and   cand_j = the boundary with bin(B_k) = j (else +inf).
+// By monotonicity every xn in bin j lies above the boundaries of lower bins and below
+// those of higher bins, and no bin holds two boundaries (adjacent boundaries are at
+// least 0.0945 = 1.5 bins apart), so #{k : B_k < xn} = cnt_j + [cand_j < xn]: the
+// reference's nearest index for finite xn (clamping xn to [-1, 1] never changes that
+// count).  |xn| <= 1 + 2^-22 keeps j in 0 .. 32 whenever 1/amax is finite; blocks with
+// an infinite 1/amax (amax below 2^-128) take the compare-tree search instead.  A NaN
+// xn is the canonical 0x7FFFFFFF on the GPU and falls in bin 63, whose entry gives the
+// reference's NaN code (TQ3 0, TQ4 15).  Rows are replicated for the 16 lanes of a half
+// warp (8-byte entries: lane l reads banks 2l and 2l + 1), so lookups never conflict.
+constexpr float BIN_MAGIC = 12582928.0f;   // 1.5 * 2^23 + 16
+constexpr float BIN_SCALE = 16.0f;
+constexpr uint32_t BIN_MASK = 0x3Fu;
+constexpr int NEAR_ROWS = 64, NEAR_REP = 16;
+
+template <int QT>
+__device__ __forceinline__ float boundary(int k) {   // B_k of src/ggml-tq.h:103-121, exact fp32
+    if constexpr (QT == 4) {
+        constexpr float P[7] = {TQ4_P0, TQ4_P1, TQ4_P2, TQ4_P3, TQ4_P4, TQ4_P5, TQ4_P6};
+        return k < 7 ? -P[6 - k] : (k == 7 ? 0.0f : P[k - 8]);
+    } else {
+        constexpr float P[3] = {TQ3_P0, TQ3_P1, TQ3_P2};
+        return k < 3 ? -P[2 - k] : (k == 3 ? 0.0f : P[k - 4]);
+    }
+}
+
+template <int QT>
+__device__ void near_table_init(uint2* __restrict__ t) {
+    // one thread per row: count the boundaries of lower bins, find this bin's boundary,
+    // then write the row's 16 replicas
+    constexpr int NB = QT == 4 ? 15 : 7;
+    for (int row = threadIdx.x; row < NEAR_ROWS; row += CODEC_THREADS) {
+        uint32_t cnt = QT == 4 ? 15u : 0u;   // bins past 32: only a NaN reaches them
+        float cand = INFINITY;
+        if (row <= 32) {
+            cnt = 0;
+#pragma unroll
+            for (int k = 0; k < NB; ++k) {
+                const float b = boundary<QT>(k);
+                const int bk = (int)(__float_as_uint(__fmaf_rn(b, BIN_SCALE, BIN_MAGIC)) & BIN_MASK);
+                cnt += bk < row;
+                cand = bk == row ? b : cand;
+            }
+        }
+        const uint4 e = make_uint4(__float_as_uint(cand), cnt, __float_as_uint(cand), cnt);
+#pragma unroll
+        for (int r = 0; r < NEAR_REP / 2; ++r) reinterpret_cast<uint4*>(t + row * NEAR_REP)[r] = e;
+    }
+}
+
+// nearest indices of xn.x, xn.y; tb = shared address of the table + 8 * (lane % 16)
+__device__ __forceinline__ void near_pair(float2 xn, uint32_t tb, uint32_t& i0, uint32_t& i1) {
+    const float2 f = __ffma2_rn(xn, make_float2(BIN_SCALE, BIN_SCALE), make_float2(BIN_MAGIC, BIN_MAGIC));
+    const uint32_t a0 = tb + ((__float_as_uint(f.x) & BIN_MASK) << 7);
+    const uint32_t a1 = tb + ((__float_as_uint(f.y) & BIN_MASK) << 7);
+    uint32_t c0, n0, c1, n1;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(c0), "=r"(n0) : "r"(a0));
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(c1), "=r"(n1) : "r"(a1));
+    asm("{\n\t.reg .pred p;\n\tsetp.gt.f32 p, %1, %2;\n\t@p add.u32 %0, %0, 1;\n\t}" : "+r"(n0) : "f"(xn.x), "f"(__uint_as_float(c0)));
+    asm("{\n\t.reg .pred p;\n\tsetp.gt.f32 p, %1, %2;\n\t@p add.u32 %0, %0, 1;\n\t}" : "+r"(n1) : "f"(xn.y), "f"(__uint_as_float(c1)));
+    i0 = n0;
+    i1 = n1;
+}
+
 // ── quantize ────────────────────────────────────────────────────────────────
 // MODE 0: nearest level (reference).  MODE 1: TQ3 optimal rounding.
-template <int QT, typename IN, int MODE>
-__global__ void __launch_bounds__(CODEC_THREADS)
+template <int QT, typename IN, int MODE, int L2>
+__global__ void __launch_bounds__(CODEC_THREADS, 4)
 quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nblocks,
                 int log2_hd, float norm, int n_passes, int x_vec, int y_vec, const RowMap map) {
     constexpr int EB = ElemBits<IN>::bytes;
     constexpr int ROW_BYTES = QK * EB;
     constexpr int BB = QT == 4 ? TQ4_BYTES : TQ3_BYTES;
-    __shared__ __align__(16) uint8_t s_in[CODEC_THREADS * ROW_BYTES];
+    __shared__ __align__(128) uint8_t s_in2[2][CODEC_THREADS * ROW_BYTES];   // double-buffered input tiles
     __shared__ __align__(16) uint8_t s_out[CODEC_THREADS * BB];
     __shared__ Tq3OptTables s_tbl;
     __shared__ int64_t s_dst[CODEC_THREADS];   // row-mapped output: byte offset of each head row
+    __shared__ __align__(16) uint2 s_near[NEAR_ROWS * NEAR_REP];
 
+    near_table_init<QT>(s_near);
+    const uint32_t near_tb = (uint32_t)__cvta_generic_to_shared(s_near) + 8u * (threadIdx.x & (NEAR_REP - 1));
     if (MODE == 1 && threadIdx.x < 8) {
         const int i = threadIdx.x;
         const double L = tq3_level_f64(i);
@@ -314,31 +419,62 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
     }
 
     const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
-    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    auto rows_of = [&](int64_t t) {
+        const int64_t b = t * CODEC_THREADS;
+        return (int)(nblocks - b < CODEC_THREADS ? nblocks - b : CODEC_THREADS);
+    };
+    // tile i is read from s_in2[i & 1]; tile i + 1 is in flight (cp.async) while tile i computes
+    if (x_vec && (int64_t)blockIdx.x < ntiles)
+        load_tile_async<IN>(s_in2[0], x + (int64_t)blockIdx.x * CODEC_THREADS * QK, rows_of(blockIdx.x));
+    cp_async_commit();
+    int it = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const int64_t b0 = tile * CODEC_THREADS;
-        const int nrows = (int)(nblocks - b0 < CODEC_THREADS ? nblocks - b0 : CODEC_THREADS);
-        __syncthreads();   // previous tile fully consumed (s_in, s_out reusable)
-        load_tile<IN>(s_in, x + b0 * QK, nrows, x_vec != 0);
-        __syncthreads();
+        const int nrows = rows_of(tile);
+        uint8_t* s_in = s_in2[it & 1];
+        if (x_vec) {
+            const int64_t nxt = tile + gridDim.x;
+            if (nxt < ntiles) load_tile_async<IN>(s_in2[(it + 1) & 1], x + nxt * CODEC_THREADS * QK, rows_of(nxt));
+            cp_async_commit();
+            cp_async_wait<1>();   // this thread's copies of the current tile have landed
+        } else {
+            load_tile<IN>(s_in, x + b0 * QK, nrows, false);
+        }
+        __syncthreads();          // every thread's copies have landed
 
         float v[QK];
         read_row<IN>(s_in, threadIdx.x < nrows ? threadIdx.x : 0, v);
-        fwht_block(v, log2_hd, norm);
+        fwht_block<L2>(v, log2_hd, norm);
 
         float amax = 0.0f;
 #pragma unroll
         for (int j = 0; j < QK; ++j) amax = fmaxf(amax, fabsf(v[j]));   // NaN never wins
         const float inv = amax > 0.0f ? 1.0f / amax : 0.0f;
+        const float2 inv2 = make_float2(inv, inv);
+
+        // xn = x * id exactly as the reference (one fp32 multiply per element), then the table
+        uint32_t code[QK];
+#pragma unroll
+        for (int j = 0; j < QK; j += 2)
+            near_pair(__fmul2_rn(make_float2(v[j], v[j + 1]), inv2), near_tb, code[j], code[j + 1]);
+        if (inv == INFINITY) {
+            // amax below 2^-128: xn is +-inf (or NaN for zeros), outside the table's range
+#pragma unroll
+            for (int j = 0; j < QK; ++j) {
+                const float xn = __fmul_rn(v[j], inv);
+                code[j] = (uint32_t)(QT == 4 ? tq4_nearest(xn) : tq3_nearest(xn));
+            }
+        }
 
         uint16_t dh;
         if constexpr (QT == 4) {
             dh = half_trunc(amax);
-            uint32_t w[4] = {0u, 0u, 0u, 0u};
+            uint32_t w[4];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int lo = tq4_nearest(__fmul_rn(v[j], inv));
-                const int hi = tq4_nearest(__fmul_rn(v[j + 16], inv));
-                w[j >> 2] |= (uint32_t)(lo | (hi << 4)) << (8 * (j & 3));
+            for (int k = 0; k < 4; ++k) {   // byte j = code[j] | code[j + 16] << 4
+                const int j = 4 * k;
+                w[k] = code[j] + (code[j + 16] << 4) + (code[j + 1] << 8) + (code[j + 17] << 12) +
+                       (code[j + 2] << 16) + (code[j + 18] << 20) + (code[j + 3] << 24) + (code[j + 19] << 28);
             }
             if (threadIdx.x < nrows) stage_block<4>(s_out, threadIdx.x * BB, dh, w);
         } else {
@@ -346,10 +482,9 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
             uint32_t g[4];
 #pragma unroll
             for (int gi = 0; gi < 4; ++gi) {
-                uint32_t word = 0;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) word |= (uint32_t)tq3_nearest(__fmul_rn(v[8 * gi + i], inv)) << (3 * i);
-                g[gi] = word;
+                const uint32_t* c = code + 8 * gi;
+                g[gi] = c[0] + (c[1] << 3) + (c[2] << 6) + (c[3] << 9) + (c[4] << 12) + (c[5] << 15) + (c[6] << 18) +
+                        (c[7] << 21);
             }
             if constexpr (MODE == 1) {
                 if (amax > 0.0f) {
@@ -368,10 +503,12 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
             const uint32_t w[3] = {g[0] | (g[1] << 24), (g[1] >> 8) | (g[2] << 16), (g[2] >> 16) | (g[3] << 8)};
             if (threadIdx.x < nrows) stage_block<3>(s_out, threadIdx.x * BB, dh, w);
         }
-        __syncthreads();
+        __syncthreads();          // s_out complete; s_in of this tile fully read
         if (map.cap == 0) store_staged(y + b0 * BB, s_out, nrows * BB, y_vec != 0);
         else store_mapped(y, s_out, s_dst, b0, nrows, BB, map);
+        __syncthreads();          // s_out free for the next tile
     }
+    cp_async_wait<0>();
 }
 
 // ── in-place FWHT (hadamard_transform_row) on fp32 ──────────────────────────
@@ -519,18 +656,38 @@ static int codec_grid(int64_t ntiles, int per_sm) {
     return (int)(ntiles < cap ? (ntiles > 0 ? ntiles : 1) : cap);
 }
 
+template <int QT, typename IN, int MODE, int L2>
+static void launch_quant_k(const void* x, void* y, int64_t nblocks, int log2_hd, float norm, int n_passes,
+                           const RowMap& map, int grid, int xv, int yv, cudaStream_t st) {
+    quantize_kernel<QT, IN, MODE, L2><<<grid, CODEC_THREADS, 0, st>>>((const IN*)x, (uint8_t*)y, nblocks, log2_hd,
+                                                                      norm, n_passes, xv, yv, map);
+}
+
+template <int QT, typename IN, int MODE>
+static void launch_quant_l2(const void* x, void* y, int64_t nblocks, int log2_hd, float norm, int n_passes,
+                            const RowMap& map, int grid, int xv, int yv, cudaStream_t st) {
+    // head_dim 128 and 256 (and no rotation) get fully unrolled FWHT stages
+    switch (log2_hd) {
+        case -1: launch_quant_k<QT, IN, MODE, -1>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, st); break;
+        case 7: launch_quant_k<QT, IN, MODE, 7>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, st); break;
+        case 8: launch_quant_k<QT, IN, MODE, 8>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, st); break;
+        default: launch_quant_k<QT, IN, MODE, -2>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, st); break;
+    }
+}
+
 template <int QT, typename IN>
 static cudaError_t launch_quant_t(const void* x, void* y, int64_t nblocks, int log2_hd, float norm,
                                   int n_passes, const RowMap& map, cudaStream_t st) {
     const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
     const int grid = codec_grid(ntiles, 16);
     const int xv = ((uintptr_t)x & 15) == 0, yv = ((uintptr_t)y & 15) == 0;
-    if (QT == 3 && n_passes > 0)
-        quantize_kernel<QT, IN, 1><<<grid, CODEC_THREADS, 0, st>>>((const IN*)x, (uint8_t*)y, nblocks, log2_hd,
-                                                                   norm, n_passes, xv, yv, map);
-    else
-        quantize_kernel<QT, IN, 0><<<grid, CODEC_THREADS, 0, st>>>((const IN*)x, (uint8_t*)y, nblocks, log2_hd,
-                                                                   norm, 0, xv, yv, map);
+    if constexpr (QT == 3) {
+        if (n_passes > 0) {
+            launch_quant_l2<QT, IN, 1>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, st);
+            return cudaGetLastError();
+        }
+    }
+    launch_quant_l2<QT, IN, 0>(x, y, nblocks, log2_hd, norm, 0, map, grid, xv, yv, st);
     return cudaGetLastError();
 }
 

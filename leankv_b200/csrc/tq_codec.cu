@@ -246,7 +246,7 @@ __device__ __forceinline__ void copy_rows(uint8_t* __restrict__ y, const uint8_t
 
 __device__ __forceinline__ void store_mapped(uint8_t* __restrict__ y, const uint8_t* __restrict__ smem,
                                              int64_t* __restrict__ s_dst, int64_t b0, int nrows, int bb,
-                                             const RowMap& map) {
+                                             const RowMap& map, bool y_vec) {
     const int nb = map.nblk, row_bytes = nb * bb, nr = nrows / nb;
     if (threadIdx.x < nr) {
         const int64_t R = b0 / nb + threadIdx.x;
@@ -256,11 +256,24 @@ __device__ __forceinline__ void store_mapped(uint8_t* __restrict__ y, const uint
         if (slot >= 0 && slot < map.cap) off = (sh * map.cap + slot) * row_bytes;
         else if (map.overflow) atomicAdd(map.overflow, 1);
         s_dst[threadIdx.x] = off;
+        if (threadIdx.x == 0) {
+            // the whole tile lands in consecutive slots of one (sequence, head) when its last
+            // row belongs to the same (sequence, head) and still fits
+            const int64_t R1 = R + nr - 1, sh1 = R1 / map.n_new;
+            s_dst[CODEC_THREADS] = (off >= 0 && sh1 == sh && slot + (nr - 1) < map.cap) ? 1 : 0;
+        }
     }
     __syncthreads();
-    if ((row_bytes & 7) == 0) copy_rows<uint2>(y, smem, s_dst, nr, row_bytes);
-    else if ((row_bytes & 3) == 0) copy_rows<uint32_t>(y, smem, s_dst, nr, row_bytes);
-    else copy_rows<uint16_t>(y, smem, s_dst, nr, row_bytes);
+    if (s_dst[CODEC_THREADS]) {
+        uint8_t* dst = y + s_dst[0];
+        store_staged(dst, smem, nrows * bb, y_vec && (((uintptr_t)dst) & 15) == 0);
+    } else if ((row_bytes & 7) == 0) {
+        copy_rows<uint2>(y, smem, s_dst, nr, row_bytes);
+    } else if ((row_bytes & 3) == 0) {
+        copy_rows<uint32_t>(y, smem, s_dst, nr, row_bytes);
+    } else {
+        copy_rows<uint16_t>(y, smem, s_dst, nr, row_bytes);
+    }
 }
 
 // ── TQ3 optimal rounding (scripts/tq3_rounding.py:74-125) ───────────────────
@@ -272,8 +285,12 @@ __device__ __forceinline__ void store_mapped(uint8_t* __restrict__ y, const uint
 // (that is C'^2 * A > C^2 * A' with C' = C + p, A' = A + dLL).  The levels are
 // the float64 decimals of the Python prototype.
 //
+// Per code i: {dL down, dLL down} and {dL up, dLL up} (a missing neighbour holds zeros and is
+// never accepted), replicated 8 times as rep[(2 i + half) * 8 + lane % 8]: a 16-byte load is
+// served a quarter warp (8 lanes) at a time, and those 8 lanes read 8 different 16-byte slots,
+// so the lane-dependent lookups are free of bank conflicts.
 struct Tq3OptTables {
-    double4 mv64[8];   // per code: {dL down, dLL down, dL up, dLL up} (missing neighbour: zeros, never accepted)
+    double2 rep[8 * 2 * 8];
     double lv[8];      // float64 levels
 };
 
@@ -287,6 +304,7 @@ __device__ __forceinline__ uint32_t code_of(const uint32_t (&g)[4], int j) {   /
 // accepts the first strict improvement.
 __device__ __forceinline__ double tq3_opt_refine(const float (&v)[QK], uint32_t (&g)[4], int n_passes,
                                                  const Tq3OptTables* __restrict__ t) {
+    const int lane8 = threadIdx.x & 7;
     int idx[QK];
 #pragma unroll
     for (int j = 0; j < QK; ++j) idx[j] = (int)code_of(g, j);
@@ -303,7 +321,8 @@ __device__ __forceinline__ double tq3_opt_refine(const float (&v)[QK], uint32_t 
 #pragma unroll
         for (int j = 0; j < QK; ++j) {
             const int i = idx[j];
-            const double4 e = t->mv64[i];   // dL down, dLL down, dL up, dLL up
+            const double2 ed = t->rep[(2 * i) * 8 + lane8], eu = t->rep[(2 * i + 1) * 8 + lane8];
+            const double4 e = make_double4(ed.x, ed.y, eu.x, eu.y);   // dL down, dLL down, dL up, dLL up
             const double xd = (double)v[j];
             const double Cd = fma(xd, e.x, C), Ad = A + e.y;
             const double Cu = fma(xd, e.z, C), Au = A + e.w;
@@ -401,21 +420,23 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
     constexpr int EB = ElemBits<IN>::bytes;
     constexpr int ROW_BYTES = QK * EB;
     constexpr int BB = QT == 4 ? TQ4_BYTES : TQ3_BYTES;
-    __shared__ __align__(128) uint8_t s_in2[2][CODEC_THREADS * ROW_BYTES];   // double-buffered input tiles
+    constexpr int NBUF = 2;   // double-buffered input tiles
+    __shared__ __align__(128) uint8_t s_in2[NBUF][CODEC_THREADS * ROW_BYTES];
     __shared__ __align__(16) uint8_t s_out[CODEC_THREADS * BB];
     __shared__ Tq3OptTables s_tbl;
-    __shared__ int64_t s_dst[CODEC_THREADS];   // row-mapped output: byte offset of each head row
+    __shared__ int64_t s_dst[CODEC_THREADS + 1];   // row-mapped output: byte offset of each head row | contiguous flag
     __shared__ __align__(16) uint2 s_near[NEAR_ROWS * NEAR_REP];
 
     near_table_init<QT>(s_near);
     const uint32_t near_tb = (uint32_t)__cvta_generic_to_shared(s_near) + 8u * (threadIdx.x & (NEAR_REP - 1));
-    if (MODE == 1 && threadIdx.x < 8) {
-        const int i = threadIdx.x;
-        const double L = tq3_level_f64(i);
-        const double Ld = i > 0 ? tq3_level_f64(i - 1) : L;
-        const double Lu = i < 7 ? tq3_level_f64(i + 1) : L;
-        s_tbl.lv[i] = L;
-        s_tbl.mv64[i] = make_double4(Ld - L, Ld * Ld - L * L, Lu - L, Lu * Lu - L * L);
+    if (MODE == 1) {
+        for (int e = threadIdx.x; e < 8 * 2 * 8; e += CODEC_THREADS) {
+            const int i = e >> 4, up = (e >> 3) & 1;
+            const double L = tq3_level_f64(i);
+            const double Ln = up ? (i < 7 ? tq3_level_f64(i + 1) : L) : (i > 0 ? tq3_level_f64(i - 1) : L);
+            s_tbl.rep[e] = make_double2(Ln - L, Ln * Ln - L * L);
+            if (e < 8) s_tbl.lv[e] = tq3_level_f64(e);
+        }
     }
 
     const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
@@ -424,21 +445,22 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
         return (int)(nblocks - b < CODEC_THREADS ? nblocks - b : CODEC_THREADS);
     };
     // tile i is read from s_in2[i & 1]; tile i + 1 is in flight (cp.async) while tile i computes
-    if (x_vec && (int64_t)blockIdx.x < ntiles)
+    const bool async_tiles = NBUF == 2 && x_vec;
+    if (async_tiles && (int64_t)blockIdx.x < ntiles)
         load_tile_async<IN>(s_in2[0], x + (int64_t)blockIdx.x * CODEC_THREADS * QK, rows_of(blockIdx.x));
     cp_async_commit();
     int it = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const int64_t b0 = tile * CODEC_THREADS;
         const int nrows = rows_of(tile);
-        uint8_t* s_in = s_in2[it & 1];
-        if (x_vec) {
+        uint8_t* s_in = s_in2[it % NBUF];
+        if (async_tiles) {
             const int64_t nxt = tile + gridDim.x;
-            if (nxt < ntiles) load_tile_async<IN>(s_in2[(it + 1) & 1], x + nxt * CODEC_THREADS * QK, rows_of(nxt));
+            if (nxt < ntiles) load_tile_async<IN>(s_in2[(it + 1) % NBUF], x + nxt * CODEC_THREADS * QK, rows_of(nxt));
             cp_async_commit();
             cp_async_wait<1>();   // this thread's copies of the current tile have landed
         } else {
-            load_tile<IN>(s_in, x + b0 * QK, nrows, false);
+            load_tile<IN>(s_in, x + b0 * QK, nrows, x_vec != 0);
         }
         __syncthreads();          // every thread's copies have landed
 
@@ -505,7 +527,7 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
         }
         __syncthreads();          // s_out complete; s_in of this tile fully read
         if (map.cap == 0) store_staged(y + b0 * BB, s_out, nrows * BB, y_vec != 0);
-        else store_mapped(y, s_out, s_dst, b0, nrows, BB, map);
+        else store_mapped(y, s_out, s_dst, b0, nrows, BB, map, y_vec != 0);
         __syncthreads();          // s_out free for the next tile
     }
     cp_async_wait<0>();

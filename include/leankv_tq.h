@@ -144,6 +144,26 @@ tq_status tq_quantize_host(tq_type type, const void *x, tq_dtype x_dtype, void *
 tq_status tq_dequantize_host(tq_type type, const void *x, void *y, tq_dtype y_dtype, int64_t k);
 tq_status tq_hadamard_host(float *x, int64_t n, int head_dim);
 
+/* ── prototype vector codec (prototype/turboquant, no C counterpart) ─────────
+ *
+ * The Python prototype's per-vector TurboQuant (prototype/turboquant/quantizer.py:103-221,
+ * qjl_residual.py:44-110, lloyd_max.py:208-236) on the GPU, one warp per vector:
+ *   xr = Hadamard(x * signs) when rotate (signs: float[dim] of +-1, or NULL), or the caller's
+ *        pre-rotated x_rotated (dense rotation matrices are applied by the caller);
+ *   scale = ||x||_2 per vector (group == dim or 0) or max |xr| per group of `group` elements;
+ *   xn = xr / (scale + 1e-10);  indices = #{b : boundaries[b] < xn}  (torch.bucketize);
+ *   with qjl_signs: r = xn - levels[idx], bit (r >= 0) packed 8 per byte (bit i of byte j =
+ *   element 8j + i) and qjl_mean_abs = mean |r| per vector.
+ * Decode: y = (levels[idx] + (2 bit - 1) * mean_abs) * scale, then, when inv_rotate,
+ * y = Hadamard(y) * signs.  dim: 32, 64, 128 or 256; 2..16 levels; device pointers. */
+tq_status tq_proto_encode_cuda(const void *x, tq_dtype x_dtype, const float *x_rotated, int64_t rows, int dim,
+                               int rotate, const float *signs, int group, int n_levels, const float *levels,
+                               const float *boundaries, uint8_t *indices, float *scales, uint8_t *qjl_signs,
+                               float *qjl_mean_abs, void *stream);
+tq_status tq_proto_decode_cuda(const uint8_t *indices, const float *scales, int64_t rows, int dim, int group,
+                               const uint8_t *qjl_signs, const float *qjl_mean_abs, int n_levels,
+                               const float *levels, int inv_rotate, const float *signs, float *y, void *stream);
+
 /* ── fused decode attention over packed K/V blocks ──────────────────────────
  *
  * For each sequence b and query head h (GQA: KV head h / (n_q_heads / n_kv_heads)):

@@ -66,6 +66,9 @@ SIGNATURES = {
     "tq_decode_attention_static_cuda": (_i32, [_v, _v]),
     "tq_lse_combine_cuda": (_i32, [_i32, _i64, _i32, _v, _v, _v, _v, _v]),
     "tq_lse_merge_cuda": (_i32, [_i32, _i64, _i32, _v, _i64, _v, _i64, _v, _i32, _v, _v]),
+    # prototype vector codec (levels / boundaries are host float arrays)
+    "tq_proto_encode_cuda": (_i32, [_v, _i32, _v, _i64, _i32, _i32, _v, _i32, _i32, _v, _v, _v, _v, _v, _v, _v]),
+    "tq_proto_decode_cuda": (_i32, [_v, _v, _i64, _i32, _i32, _v, _v, _i32, _v, _i32, _v, _v, _v]),
     # KV-cache append
     "tq_kv_append_cuda": (_i32, [_i32, _v, _i32, _v, _i32, _i32, _i32, _i64, _i64, _v, _i32, _i32, _v, _v]),
 }

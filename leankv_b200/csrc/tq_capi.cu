@@ -147,6 +147,10 @@ extern "C" const char* tq_status_string(tq_status s) {
 }
 
 extern "C" const char* tq_last_error_string(void) { return g_err; }
+
+namespace tq {
+void clear_error() { g_err[0] = 0; }
+}  // namespace tq
 extern "C" int tq_abi_version(void) { return LEANKV_TQ_ABI_VERSION; }
 
 // ── device-pointer API ────────────────────────────────────────────────────────

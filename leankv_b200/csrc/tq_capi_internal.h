@@ -10,6 +10,7 @@
 namespace tq {
 
 tq_status set_error(tq_status s, const char* fmt, ...);
+void clear_error();   // empty the calling thread's last-error message
 tq_status cuda_status(cudaError_t e, const char* what);
 int log2_pow2(int64_t v);
 float fwht_norm(int d);

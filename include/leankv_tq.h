@@ -40,8 +40,13 @@ extern "C" {
 /* ── block formats: byte-identical to src/ggml-tq.h:125-141 ────────────── */
 
 #ifndef GGML_TQ_H  /* the reference header defines the same layouts */
+#define QK_TQ2 32
 #define QK_TQ3 32
 #define QK_TQ4 32
+typedef struct {
+    uint16_t d;
+    uint8_t  qs[8];      /* byte i = code 4i | 4i+1 << 2 | 4i+2 << 4 | 4i+3 << 6, src/ggml-tq.c:78-96 */
+} block_tq2_0;           /* 10 bytes */
 typedef struct {
     uint16_t d;          /* fp16 scale (truncating fp32->fp16, src/ggml-tq.h:39-48) */
     uint8_t  qs[12];     /* 4 groups x 8 codes x 3 bits, src/ggml-tq.c:26-55 */
@@ -74,6 +79,19 @@ void quantize_row_tq3_0_opt(const float * TQ_RESTRICT x, block_tq3_0 * TQ_RESTRI
 void hadamard_transform(float * x, int d);
 /* replaces hadamard_transform_row, src/ggml-tq.c:398-404 */
 void hadamard_transform_row(float * x, int n, int head_dim);
+/* replace the TQ2_0 entry points, src/ggml-tq.c:158-212 */
+void quantize_row_tq2_0_ref(const float * TQ_RESTRICT x, block_tq2_0 * TQ_RESTRICT y, int64_t k);
+void dequantize_row_tq2_0(const block_tq2_0 * TQ_RESTRICT x, float * TQ_RESTRICT y, int64_t k);
+void quantize_row_tq2_0(const float * TQ_RESTRICT x, void * TQ_RESTRICT y, int64_t k);
+/* replace the tier migrations, src/ggml-tq.c:329-357 (dequantize, then quantize_row_*_ref) */
+void requantize_tq4_to_tq3(const block_tq4_0 * TQ_RESTRICT src, block_tq3_0 * TQ_RESTRICT dst, int64_t k);
+void requantize_tq3_to_tq2(const block_tq3_0 * TQ_RESTRICT src, block_tq2_0 * TQ_RESTRICT dst, int64_t k);
+void requantize_tq4_to_tq2(const block_tq4_0 * TQ_RESTRICT src, block_tq2_0 * TQ_RESTRICT dst, int64_t k);
+/* replace randomized_hadamard_transform(_row), src/ggml-tq.c:383-396 and :406-412: signs from
+ * the LCG s = s * 1664525 + 1013904223 (negate where bit 31 is set), then the Hadamard transform;
+ * chunk h of a row uses seed + h.  d / head_dim: powers of two from 32 to 1024. */
+void randomized_hadamard_transform(float * x, int d, uint32_t seed);
+void randomized_hadamard_transform_row(float * x, int n, int head_dim, uint32_t seed);
 
 /* ── status, types ───────────────────────────────────────────────────────── */
 
@@ -89,7 +107,7 @@ typedef enum {
 } tq_status;
 
 typedef enum { TQ_DTYPE_F32 = 0, TQ_DTYPE_F16 = 1, TQ_DTYPE_BF16 = 2 } tq_dtype;
-typedef enum { TQ_TYPE_TQ3_0 = 3, TQ_TYPE_TQ4_0 = 4 } tq_type;
+typedef enum { TQ_TYPE_TQ2_0 = 2, TQ_TYPE_TQ3_0 = 3, TQ_TYPE_TQ4_0 = 4 } tq_type;
 
 const char *tq_status_string(tq_status s);
 /* message of the last failure on the calling thread ("" if none) */
@@ -116,6 +134,18 @@ tq_status tq_quantize_cuda(tq_type type, const void *x, tq_dtype x_dtype, void *
 tq_status tq_dequantize_cuda(tq_type type, const void *x, void *y, tq_dtype y_dtype, int64_t k, void *stream);
 /* In-place hadamard_transform_row on n float32 values (head_dim a power of two <= 32768). */
 tq_status tq_hadamard_cuda(float *x, int64_t n, int head_dim, void *stream);
+/* In-place randomized_hadamard_transform_row(row, row_len, head_dim, seed) on every row of
+ * row_len elements of x (n a multiple of row_len, row_len of head_dim; head_dim a power of two,
+ * 32..1024). */
+tq_status tq_hadamard_randomized_cuda(float *x, int64_t n, int row_len, int head_dim, uint32_t seed, void *stream);
+/* randomized_hadamard_transform_row + quantize_row_*_ref fused: every row of row_len elements is
+ * rotated with the seeded sign diagonal and Hadamard transform of each head_dim chunk, then
+ * quantized (opt_passes as for tq_quantize_cuda). */
+tq_status tq_quantize_randomized_cuda(tq_type type, const void *x, tq_dtype x_dtype, void *y, int64_t k, int row_len,
+                                      int head_dim, uint32_t seed, int opt_passes, void *stream);
+/* Requantize k elements from src_type blocks to dst_type blocks in one pass (each block is
+ * dequantized to float32 and quantized again, as requantize_tq4_to_tq3 and friends do). */
+tq_status tq_requantize_cuda(tq_type src_type, const void *src, tq_type dst_type, void *dst, int64_t k, void *stream);
 
 /*
  * Quantize-on-write into a KV cache: [FWHT] + quantize n_new new head rows per
@@ -143,6 +173,8 @@ tq_status tq_quantize_host(tq_type type, const void *x, tq_dtype x_dtype, void *
                            int fwht_head_dim, int opt_passes);
 tq_status tq_dequantize_host(tq_type type, const void *x, void *y, tq_dtype y_dtype, int64_t k);
 tq_status tq_hadamard_host(float *x, int64_t n, int head_dim);
+tq_status tq_hadamard_randomized_host(float *x, int64_t n, int row_len, int head_dim, uint32_t seed);
+tq_status tq_requantize_host(tq_type src_type, const void *src, tq_type dst_type, void *dst, int64_t k);
 
 /* ── prototype vector codec (prototype/turboquant, no C counterpart) ─────────
  *

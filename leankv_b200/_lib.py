@@ -19,8 +19,8 @@ STATUS_NAMES = {0: "TQ_SUCCESS", 1: "TQ_ERROR_INVALID_VALUE", 2: "TQ_ERROR_UNSUP
                 4: "TQ_ERROR_CUDA", 5: "TQ_ERROR_OUT_OF_MEMORY", 6: "TQ_ERROR_NO_DEVICE", 7: "TQ_ERROR_TIMEOUT"}
 # tq_dtype / tq_type
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
-TYPE_TQ3_0, TYPE_TQ4_0 = 3, 4
-BLOCK_BYTES = {TYPE_TQ3_0: 14, TYPE_TQ4_0: 18}
+TYPE_TQ2_0, TYPE_TQ3_0, TYPE_TQ4_0 = 2, 3, 4
+BLOCK_BYTES = {TYPE_TQ2_0: 10, TYPE_TQ3_0: 14, TYPE_TQ4_0: 18}
 QK = 32
 
 
@@ -48,6 +48,14 @@ SIGNATURES = {
     "dequantize_row_tq4_0": (None, [_v, _v, _i64]),
     "hadamard_transform": (None, [_v, _i32]),
     "hadamard_transform_row": (None, [_v, _i32, _i32]),
+    "quantize_row_tq2_0_ref": (None, [_v, _v, _i64]),
+    "quantize_row_tq2_0": (None, [_v, _v, _i64]),
+    "dequantize_row_tq2_0": (None, [_v, _v, _i64]),
+    "requantize_tq4_to_tq3": (None, [_v, _v, _i64]),
+    "requantize_tq3_to_tq2": (None, [_v, _v, _i64]),
+    "requantize_tq4_to_tq2": (None, [_v, _v, _i64]),
+    "randomized_hadamard_transform": (None, [_v, _i32, C.c_uint32]),
+    "randomized_hadamard_transform_row": (None, [_v, _i32, _i32, C.c_uint32]),
     # status
     "tq_status_string": (C.c_char_p, [_i32]),
     "tq_last_error_string": (C.c_char_p, []),
@@ -56,10 +64,15 @@ SIGNATURES = {
     "tq_quantize_cuda": (_i32, [_i32, _v, _i32, _v, _i64, _i32, _i32, _v]),
     "tq_dequantize_cuda": (_i32, [_i32, _v, _v, _i32, _i64, _v]),
     "tq_hadamard_cuda": (_i32, [_v, _i64, _i32, _v]),
+    "tq_hadamard_randomized_cuda": (_i32, [_v, _i64, _i32, _i32, C.c_uint32, _v]),
+    "tq_quantize_randomized_cuda": (_i32, [_i32, _v, _i32, _v, _i64, _i32, _i32, C.c_uint32, _i32, _v]),
+    "tq_requantize_cuda": (_i32, [_i32, _v, _i32, _v, _i64, _v]),
     # host API
     "tq_quantize_host": (_i32, [_i32, _v, _i32, _v, _i64, _i32, _i32]),
     "tq_dequantize_host": (_i32, [_i32, _v, _v, _i32, _i64]),
     "tq_hadamard_host": (_i32, [_v, _i64, _i32]),
+    "tq_hadamard_randomized_host": (_i32, [_v, _i64, _i32, _i32, C.c_uint32]),
+    "tq_requantize_host": (_i32, [_i32, _v, _i32, _v, _i64]),
     # decode attention (argument block pointer; leankv_b200.attention binds the struct type)
     "tq_decode_attention_workspace_size": (C.c_size_t, [_v]),
     "tq_decode_attention_cuda": (_i32, [_v, _v]),

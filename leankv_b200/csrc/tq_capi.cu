@@ -48,10 +48,10 @@ int log2_pow2(int64_t v) {
 // 1/sqrt(d) with the reference's float expression (src/ggml-tq.c:377)
 float fwht_norm(int d) { return 1.0f / sqrtf((float)d); }
 
-size_t block_bytes(int type) { return type == TQ_TYPE_TQ4_0 ? TQ4_BYTES : TQ3_BYTES; }
+size_t block_bytes(int type) { return type == TQ_TYPE_TQ4_0 ? TQ4_BYTES : type == TQ_TYPE_TQ3_0 ? TQ3_BYTES : TQ2_BYTES; }
 size_t dtype_bytes(int dt) { return dt == TQ_DTYPE_F32 ? 4 : 2; }
 bool dtype_ok(int dt) { return dt == TQ_DTYPE_F32 || dt == TQ_DTYPE_F16 || dt == TQ_DTYPE_BF16; }
-bool type_ok(int t) { return t == TQ_TYPE_TQ3_0 || t == TQ_TYPE_TQ4_0; }
+bool type_ok(int t) { return t == TQ_TYPE_TQ2_0 || t == TQ_TYPE_TQ3_0 || t == TQ_TYPE_TQ4_0; }
 
 // ── host-API contexts: one stream + grow-only device buffer each ───────────
 struct HostCtx {
@@ -243,6 +243,52 @@ extern "C" tq_status tq_hadamard_cuda(float* x, int64_t n, int head_dim, void* s
     return cuda_status(launch_fwht_tail(x + bulk, (int)(n - bulk), l2, norm, st), "fwht tail launch");
 }
 
+extern "C" tq_status tq_hadamard_randomized_cuda(float* x, int64_t n, int row_len, int head_dim, uint32_t seed,
+                                                 void* stream) {
+    clear_error();
+    const int l2 = log2_pow2(head_dim);
+    if (l2 < 0) return set_error(TQ_ERROR_INVALID_VALUE, "head_dim=%d is not a power of two", head_dim);
+    if (l2 < 5 || l2 > 10) return set_error(TQ_ERROR_UNSUPPORTED, "randomized Hadamard needs head_dim in 32..1024 (got %d)", head_dim);
+    if (row_len <= 0 || row_len % head_dim) return set_error(TQ_ERROR_INVALID_VALUE, "row_len is not a multiple of head_dim");
+    if (n < 0 || n % row_len) return set_error(TQ_ERROR_INVALID_VALUE, "n is not a multiple of row_len");
+    if (n == 0) return TQ_SUCCESS;
+    if (!x) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    return cuda_status(launch_fwht(x, n / QK, l2, fwht_norm(head_dim), (cudaStream_t)stream, seed, row_len / head_dim),
+                       "randomized fwht kernel launch");
+}
+
+extern "C" tq_status tq_quantize_randomized_cuda(tq_type type, const void* x, tq_dtype x_dtype, void* y, int64_t k,
+                                                 int row_len, int head_dim, uint32_t seed, int opt_passes,
+                                                 void* stream) {
+    clear_error();
+    if (!type_ok(type)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown block type %d", (int)type);
+    if (!dtype_ok(x_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown input dtype %d", (int)x_dtype);
+    const int l2 = log2_pow2(head_dim);
+    if (l2 < 5 || l2 > 10) return set_error(TQ_ERROR_UNSUPPORTED, "randomized Hadamard needs head_dim in 32..1024 (got %d)", head_dim);
+    if (row_len <= 0 || row_len % head_dim) return set_error(TQ_ERROR_INVALID_VALUE, "row_len is not a multiple of head_dim");
+    if (k < 0 || k % row_len) return set_error(TQ_ERROR_INVALID_VALUE, "k is not a multiple of row_len");
+    if (opt_passes < 0 || opt_passes > 64) return set_error(TQ_ERROR_INVALID_VALUE, "opt_passes=%d out of [0, 64]", opt_passes);
+    if (opt_passes > 0 && type != TQ_TYPE_TQ3_0) return set_error(TQ_ERROR_UNSUPPORTED, "optimal rounding is defined for TQ3_0 only");
+    if (k == 0) return TQ_SUCCESS;
+    if (!x || !y) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    if (((uintptr_t)x) % dtype_bytes(x_dtype)) return set_error(TQ_ERROR_MISALIGNED, "x not aligned to its element size");
+    return cuda_status(launch_quantize((int)type, (int)x_dtype, x, y, k / QK, l2, fwht_norm(head_dim), opt_passes,
+                                       (cudaStream_t)stream, RowMap(), seed, row_len / head_dim),
+                       "quantize kernel launch");
+}
+
+extern "C" tq_status tq_requantize_cuda(tq_type src_type, const void* src, tq_type dst_type, void* dst, int64_t k,
+                                        void* stream) {
+    clear_error();
+    if (!type_ok(src_type) || !type_ok(dst_type)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown block type");
+    if (k < 0 || k % QK != 0) return set_error(TQ_ERROR_INVALID_VALUE, "k=%lld is not a multiple of 32", (long long)k);
+    if (k == 0) return TQ_SUCCESS;
+    if (!src || !dst) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    if ((((uintptr_t)src) | ((uintptr_t)dst)) & 1) return set_error(TQ_ERROR_MISALIGNED, "blocks must be 2-byte aligned (fp16 scale)");
+    return cuda_status(launch_requantize((int)src_type, src, (int)dst_type, dst, k / QK, (cudaStream_t)stream),
+                       "requantize kernel launch");
+}
+
 // ── host-pointer API ──────────────────────────────────────────────────────────
 
 extern "C" tq_status tq_quantize_host(tq_type type, const void* x, tq_dtype x_dtype, void* y, int64_t k,
@@ -330,6 +376,62 @@ extern "C" tq_status tq_hadamard_host(float* x, int64_t n, int head_dim) {
     return cuda_status(cudaStreamSynchronize(g.c->st), "cudaStreamSynchronize");
 }
 
+extern "C" tq_status tq_hadamard_randomized_host(float* x, int64_t n, int row_len, int head_dim, uint32_t seed) {
+    clear_error();
+    const int l2 = log2_pow2(head_dim);
+    if (l2 < 5 || l2 > 10) return set_error(TQ_ERROR_UNSUPPORTED, "randomized Hadamard needs head_dim in 32..1024 (got %d)", head_dim);
+    if (row_len <= 0 || row_len % head_dim) return set_error(TQ_ERROR_INVALID_VALUE, "row_len is not a multiple of head_dim");
+    if (n < 0 || n % row_len) return set_error(TQ_ERROR_INVALID_VALUE, "n is not a multiple of row_len");
+    if (n == 0) return TQ_SUCCESS;
+    if (!x) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    CtxGuard g;
+    tq_status s = ctx_acquire(&g.c);
+    if (s) return s;
+    int64_t chunk = host_chunk_elems(n, row_len, 4);
+    chunk -= chunk % row_len;
+    if (chunk <= 0) chunk = row_len;
+    if ((s = ctx_reserve(g.c, (size_t)chunk * 4))) return s;
+    float* d = (float*)g.c->buf;
+    for (int64_t e0 = 0; e0 < n; e0 += chunk) {
+        const int64_t m = n - e0 < chunk ? n - e0 : chunk;
+        if ((s = cuda_status(cudaMemcpyAsync(d, x + e0, m * 4, cudaMemcpyHostToDevice, g.c->st), "cudaMemcpyAsync H2D")))
+            return s;
+        if ((s = tq_hadamard_randomized_cuda(d, m, row_len, head_dim, seed, g.c->st))) return s;
+        if ((s = cuda_status(cudaMemcpyAsync(x + e0, d, m * 4, cudaMemcpyDeviceToHost, g.c->st), "cudaMemcpyAsync D2H")))
+            return s;
+    }
+    return cuda_status(cudaStreamSynchronize(g.c->st), "cudaStreamSynchronize");
+}
+
+extern "C" tq_status tq_requantize_host(tq_type src_type, const void* src, tq_type dst_type, void* dst, int64_t k) {
+    clear_error();
+    if (!type_ok(src_type) || !type_ok(dst_type)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown block type");
+    if (k < 0 || k % QK) return set_error(TQ_ERROR_INVALID_VALUE, "k=%lld is not a multiple of 32", (long long)k);
+    if (k == 0) return TQ_SUCCESS;
+    if (!src || !dst) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    CtxGuard g;
+    tq_status s = ctx_acquire(&g.c);
+    if (s) return s;
+    const size_t sb = block_bytes(src_type), db = block_bytes(dst_type);
+    const int64_t chunk = host_chunk_elems(k, QK * 8, (sb + db) / QK + 1);
+    const size_t in_bytes = (size_t)(chunk / QK) * sb, out_off = (in_bytes + 255) & ~size_t(255);
+    if ((s = ctx_reserve(g.c, out_off + (size_t)(chunk / QK) * db))) return s;
+    uint8_t* dbuf = (uint8_t*)g.c->buf;
+    for (int64_t e0 = 0; e0 < k; e0 += chunk) {
+        const int64_t n = k - e0 < chunk ? k - e0 : chunk;
+        if ((s = cuda_status(cudaMemcpyAsync(dbuf, (const uint8_t*)src + (e0 / QK) * sb, (n / QK) * sb,
+                                             cudaMemcpyHostToDevice, g.c->st),
+                             "cudaMemcpyAsync H2D")))
+            return s;
+        if ((s = tq_requantize_cuda(src_type, dbuf, dst_type, dbuf + out_off, n, g.c->st))) return s;
+        if ((s = cuda_status(cudaMemcpyAsync((uint8_t*)dst + (e0 / QK) * db, dbuf + out_off, (n / QK) * db,
+                                             cudaMemcpyDeviceToHost, g.c->st),
+                             "cudaMemcpyAsync D2H")))
+            return s;
+    }
+    return cuda_status(cudaStreamSynchronize(g.c->st), "cudaStreamSynchronize");
+}
+
 // ── ggml drop-in names (src/ggml-tq.h:145-190) ───────────────────────────────
 
 [[noreturn]] static void die(const char* fn, const char* why) {
@@ -384,4 +486,44 @@ extern "C" void hadamard_transform_row(float* x, int n, int head_dim) {
     if (head_dim <= 0 || n % head_dim != 0) die(__func__, "n % head_dim != 0 (the reference asserts this)");
     if ((head_dim & (head_dim - 1)) != 0) die(__func__, "head_dim must be a power of two (the reference asserts this)");
     if (tq_hadamard_host(x, n, head_dim) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void quantize_row_tq2_0_ref(const float* TQ_RESTRICT x, block_tq2_0* TQ_RESTRICT y, int64_t k) {
+    check_k(__func__, k);
+    if (tq_quantize_host(TQ_TYPE_TQ2_0, x, TQ_DTYPE_F32, y, k, 0, 0) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void quantize_row_tq2_0(const float* TQ_RESTRICT x, void* TQ_RESTRICT y, int64_t k) {
+    quantize_row_tq2_0_ref(x, (block_tq2_0*)y, k);
+}
+
+extern "C" void dequantize_row_tq2_0(const block_tq2_0* TQ_RESTRICT x, float* TQ_RESTRICT y, int64_t k) {
+    check_k(__func__, k);
+    if (tq_dequantize_host(TQ_TYPE_TQ2_0, x, y, TQ_DTYPE_F32, k) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void requantize_tq4_to_tq3(const block_tq4_0* TQ_RESTRICT src, block_tq3_0* TQ_RESTRICT dst, int64_t k) {
+    check_k(__func__, k);
+    if (tq_requantize_host(TQ_TYPE_TQ4_0, src, TQ_TYPE_TQ3_0, dst, k) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void requantize_tq3_to_tq2(const block_tq3_0* TQ_RESTRICT src, block_tq2_0* TQ_RESTRICT dst, int64_t k) {
+    check_k(__func__, k);
+    if (tq_requantize_host(TQ_TYPE_TQ3_0, src, TQ_TYPE_TQ2_0, dst, k) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void requantize_tq4_to_tq2(const block_tq4_0* TQ_RESTRICT src, block_tq2_0* TQ_RESTRICT dst, int64_t k) {
+    check_k(__func__, k);
+    if (tq_requantize_host(TQ_TYPE_TQ4_0, src, TQ_TYPE_TQ2_0, dst, k) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void randomized_hadamard_transform(float* x, int d, uint32_t seed) {
+    if (d <= 0 || (d & (d - 1)) != 0) die(__func__, "d must be a power of two (the reference asserts this)");
+    if (tq_hadamard_randomized_host(x, d, d, d, seed) != TQ_SUCCESS) die(__func__, g_err);
+}
+
+extern "C" void randomized_hadamard_transform_row(float* x, int n, int head_dim, uint32_t seed) {
+    if (head_dim <= 0 || n % head_dim != 0) die(__func__, "n % head_dim != 0 (the reference asserts this)");
+    if (n == 0) return;
+    if (tq_hadamard_randomized_host(x, n, n, head_dim, seed) != TQ_SUCCESS) die(__func__, g_err);
 }

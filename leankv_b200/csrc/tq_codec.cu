@@ -363,8 +363,10 @@ constexpr uint32_t BIN_MASK = 0x3Fu;
 constexpr int NEAR_ROWS = 64, NEAR_REP = 16;
 
 template <int QT>
-__device__ __forceinline__ float boundary(int k) {   // B_k of src/ggml-tq.h:103-121, exact fp32
-    if constexpr (QT == 4) {
+__device__ __forceinline__ float boundary(int k) {   // B_k of src/ggml-tq.h:93-121, exact fp32
+    if constexpr (QT == 2) {
+        return k == 0 ? -TQ2_P0 : (k == 1 ? 0.0f : TQ2_P0);
+    } else if constexpr (QT == 4) {
         constexpr float P[7] = {TQ4_P0, TQ4_P1, TQ4_P2, TQ4_P3, TQ4_P4, TQ4_P5, TQ4_P6};
         return k < 7 ? -P[6 - k] : (k == 7 ? 0.0f : P[k - 8]);
     } else {
@@ -377,7 +379,7 @@ template <int QT>
 __device__ void near_table_init(uint2* __restrict__ t) {
     // one thread per row: count the boundaries of lower bins, find this bin's boundary,
     // then write the row's 16 replicas
-    constexpr int NB = QT == 4 ? 15 : 7;
+    constexpr int NB = QT == 4 ? 15 : QT == 3 ? 7 : 3;
     for (int row = threadIdx.x; row < NEAR_ROWS; row += CODEC_THREADS) {
         uint32_t cnt = QT == 4 ? 15u : 0u;   // bins past 32: only a NaN reaches them
         float cand = INFINITY;
@@ -411,15 +413,120 @@ __device__ __forceinline__ void near_pair(float2 xn, uint32_t tb, uint32_t& i0, 
     i1 = n1;
 }
 
+// ── one block: amax, fp16 scale, nearest codes (or TQ3 optimal rounding), packing ──
+// v holds the (rotated) float32 block; the packed block is staged at s_out + off when write.
+template <int QT, int MODE>
+__device__ __forceinline__ void encode_block(float (&v)[QK], uint32_t near_tb, const Tq3OptTables* tbl,
+                                             int n_passes, uint8_t* __restrict__ s_out, int off, bool write) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < QK; ++j) amax = fmaxf(amax, fabsf(v[j]));   // NaN never wins
+    const float inv = amax > 0.0f ? 1.0f / amax : 0.0f;
+    const float2 inv2 = make_float2(inv, inv);
+
+    // xn = x * id exactly as the reference (one fp32 multiply per element), then the table
+    uint32_t code[QK];
+#pragma unroll
+    for (int j = 0; j < QK; j += 2)
+        near_pair(__fmul2_rn(make_float2(v[j], v[j + 1]), inv2), near_tb, code[j], code[j + 1]);
+    if (inv == INFINITY) {
+        // amax below 2^-128: xn is +-inf (or NaN for zeros), outside the table's range
+#pragma unroll
+        for (int j = 0; j < QK; ++j) {
+            const float xn = __fmul_rn(v[j], inv);
+            code[j] = (uint32_t)(QT == 4 ? tq4_nearest(xn) : QT == 3 ? tq3_nearest(xn) : tq2_nearest(xn));
+        }
+    }
+
+    uint16_t dh;
+    if constexpr (QT == 4) {
+        dh = half_trunc(amax);
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {   // byte j = code[j] | code[j + 16] << 4
+            const int j = 4 * k;
+            w[k] = code[j] + (code[j + 16] << 4) + (code[j + 1] << 8) + (code[j + 17] << 12) +
+                   (code[j + 2] << 16) + (code[j + 18] << 20) + (code[j + 3] << 24) + (code[j + 19] << 28);
+        }
+        if (write) stage_block<4>(s_out, off, dh, w);
+    } else if constexpr (QT == 2) {
+        dh = half_trunc(amax);
+        uint32_t w[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {   // byte i = codes 4i .. 4i+3 at bits 0, 2, 4, 6
+            uint32_t acc = 0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc += code[16 * k + j] << (2 * j);
+            w[k] = acc;
+        }
+        if (write) stage_block<2>(s_out, off, dh, w);
+    } else {
+        // codes as the four 24-bit group words of the TQ3 layout (code i of a group at bits 3i..3i+2)
+        uint32_t g[4];
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi) {
+            const uint32_t* c = code + 8 * gi;
+            g[gi] = c[0] + (c[1] << 3) + (c[2] << 6) + (c[3] << 9) + (c[4] << 12) + (c[5] << 15) + (c[6] << 18) +
+                    (c[7] << 21);
+        }
+        if constexpr (MODE == 1) {
+            if (amax > 0.0f) {
+                const double d = tq3_opt_refine(v, g, n_passes, tbl);
+                float df = (float)d;
+                if (df != df) df = fabsf(df);
+                dh = half_trunc(df);
+            } else {
+                g[0] = g[1] = g[2] = g[3] = 0u;
+                dh = 0;
+            }
+        } else {
+            dh = half_trunc(amax);
+        }
+        // 12 code bytes as 3 little-endian words
+        const uint32_t w[3] = {g[0] | (g[1] << 24), (g[1] >> 8) | (g[2] << 16), (g[2] >> 16) | (g[3] << 8)};
+        if (write) stage_block<3>(s_out, off, dh, w);
+    }
+}
+
+// float32 values of one block of `QT` at byte pointer blk (dequantize_row_tq*_0, exact)
+template <int QT>
+__device__ __forceinline__ void decode_block(const uint8_t* __restrict__ blk, float (&v)[QK]) {
+    const float d = half_decode((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+    if constexpr (QT == 4) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const uint32_t b = blk[2 + j];
+            v[j] = __fmul_rn(tq4_level(b & 15u), d);
+            v[j + 16] = __fmul_rn(tq4_level(b >> 4), d);
+        }
+    } else if constexpr (QT == 3) {
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi) {
+            const uint32_t w = (uint32_t)blk[2 + 3 * gi] | ((uint32_t)blk[3 + 3 * gi] << 8) |
+                               ((uint32_t)blk[4 + 3 * gi] << 16);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[8 * gi + i] = __fmul_rn(tq3_level((w >> (3 * i)) & 7u), d);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t b = blk[2 + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[4 * i + j] = __fmul_rn(tq2_level((b >> (2 * j)) & 3u), d);
+        }
+    }
+}
+
 // ── quantize ────────────────────────────────────────────────────────────────
 // MODE 0: nearest level (reference).  MODE 1: TQ3 optimal rounding.
 template <int QT, typename IN, int MODE, int L2>
 __global__ void __launch_bounds__(CODEC_THREADS, 4)
 quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nblocks,
-                int log2_hd, float norm, int n_passes, int x_vec, int y_vec, const RowMap map) {
+                int log2_hd, float norm, int n_passes, int x_vec, int y_vec, const RowMap map,
+                uint32_t rseed, int rhpr) {
     constexpr int EB = ElemBits<IN>::bytes;
     constexpr int ROW_BYTES = QK * EB;
-    constexpr int BB = QT == 4 ? TQ4_BYTES : TQ3_BYTES;
+    constexpr int BB = BlockBytes<QT>::value;
     constexpr int NBUF = 2;   // double-buffered input tiles
     __shared__ __align__(128) uint8_t s_in2[NBUF][CODEC_THREADS * ROW_BYTES];
     __shared__ __align__(16) uint8_t s_out[CODEC_THREADS * BB];
@@ -466,65 +573,15 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
 
         float v[QK];
         read_row<IN>(s_in, threadIdx.x < nrows ? threadIdx.x : 0, v);
+        if (rhpr > 0) {
+            // randomized_hadamard_transform_row: chunk h of a row is signed from seed + h
+            const int64_t gb = b0 + threadIdx.x;
+            const int nblk = 1 << (log2_hd - 5);
+            const int64_t head = gb >> (log2_hd - 5);
+            lcg_signs32(v, rseed + (uint32_t)(head % rhpr), (uint32_t)(gb & (nblk - 1)) * 32u);
+        }
         fwht_block<L2>(v, log2_hd, norm);
-
-        float amax = 0.0f;
-#pragma unroll
-        for (int j = 0; j < QK; ++j) amax = fmaxf(amax, fabsf(v[j]));   // NaN never wins
-        const float inv = amax > 0.0f ? 1.0f / amax : 0.0f;
-        const float2 inv2 = make_float2(inv, inv);
-
-        // xn = x * id exactly as the reference (one fp32 multiply per element), then the table
-        uint32_t code[QK];
-#pragma unroll
-        for (int j = 0; j < QK; j += 2)
-            near_pair(__fmul2_rn(make_float2(v[j], v[j + 1]), inv2), near_tb, code[j], code[j + 1]);
-        if (inv == INFINITY) {
-            // amax below 2^-128: xn is +-inf (or NaN for zeros), outside the table's range
-#pragma unroll
-            for (int j = 0; j < QK; ++j) {
-                const float xn = __fmul_rn(v[j], inv);
-                code[j] = (uint32_t)(QT == 4 ? tq4_nearest(xn) : tq3_nearest(xn));
-            }
-        }
-
-        uint16_t dh;
-        if constexpr (QT == 4) {
-            dh = half_trunc(amax);
-            uint32_t w[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {   // byte j = code[j] | code[j + 16] << 4
-                const int j = 4 * k;
-                w[k] = code[j] + (code[j + 16] << 4) + (code[j + 1] << 8) + (code[j + 17] << 12) +
-                       (code[j + 2] << 16) + (code[j + 18] << 20) + (code[j + 3] << 24) + (code[j + 19] << 28);
-            }
-            if (threadIdx.x < nrows) stage_block<4>(s_out, threadIdx.x * BB, dh, w);
-        } else {
-            // codes as the four 24-bit group words of the TQ3 layout (code i of a group at bits 3i..3i+2)
-            uint32_t g[4];
-#pragma unroll
-            for (int gi = 0; gi < 4; ++gi) {
-                const uint32_t* c = code + 8 * gi;
-                g[gi] = c[0] + (c[1] << 3) + (c[2] << 6) + (c[3] << 9) + (c[4] << 12) + (c[5] << 15) + (c[6] << 18) +
-                        (c[7] << 21);
-            }
-            if constexpr (MODE == 1) {
-                if (amax > 0.0f) {
-                    const double d = tq3_opt_refine(v, g, n_passes, &s_tbl);
-                    float df = (float)d;
-                    if (df != df) df = fabsf(df);
-                    dh = half_trunc(df);
-                } else {
-                    g[0] = g[1] = g[2] = g[3] = 0u;
-                    dh = 0;
-                }
-            } else {
-                dh = half_trunc(amax);
-            }
-            // 12 code bytes as 3 little-endian words
-            const uint32_t w[3] = {g[0] | (g[1] << 24), (g[1] >> 8) | (g[2] << 16), (g[2] >> 16) | (g[3] << 8)};
-            if (threadIdx.x < nrows) stage_block<3>(s_out, threadIdx.x * BB, dh, w);
-        }
+        encode_block<QT, MODE>(v, near_tb, &s_tbl, n_passes, s_out, threadIdx.x * BB, threadIdx.x < nrows);
         __syncthreads();          // s_out complete; s_in of this tile fully read
         if (map.cap == 0) store_staged(y + b0 * BB, s_out, nrows * BB, y_vec != 0);
         else store_mapped(y, s_out, s_dst, b0, nrows, BB, map, y_vec != 0);
@@ -535,7 +592,7 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
 
 // ── in-place FWHT (hadamard_transform_row) on fp32 ──────────────────────────
 __global__ void __launch_bounds__(CODEC_THREADS)
-fwht_kernel(float* __restrict__ x, int64_t nblocks, int log2_hd, float norm, int x_vec) {
+fwht_kernel(float* __restrict__ x, int64_t nblocks, int log2_hd, float norm, int x_vec, uint32_t rseed, int rhpr) {
     constexpr int ROW_BYTES = QK * 4;
     __shared__ __align__(16) uint8_t s_in[CODEC_THREADS * ROW_BYTES];
     const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
@@ -548,6 +605,11 @@ fwht_kernel(float* __restrict__ x, int64_t nblocks, int log2_hd, float norm, int
         float v[QK];
         const int r = threadIdx.x < nrows ? threadIdx.x : 0;
         read_row<float>(s_in, r, v);
+        if (rhpr > 0) {   // randomized_hadamard_transform_row (heads of >= 32 elements)
+            const int64_t gb = b0 + r;
+            const int64_t head = gb >> (log2_hd - 5);
+            lcg_signs32(v, rseed + (uint32_t)(head % rhpr), (uint32_t)(gb & ((1 << (log2_hd - 5)) - 1)) * 32u);
+        }
         fwht_block(v, log2_hd, norm);
         __syncthreads();
         if (threadIdx.x < nrows) {
@@ -605,11 +667,11 @@ template <> __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16*
 template <int QT, typename OUT>
 __global__ void __launch_bounds__(DQ_THREADS)
 dequantize_kernel(const uint8_t* __restrict__ xq, OUT* __restrict__ y, int64_t nblocks, int x_vec, int y_vec) {
-    constexpr int BB = QT == 4 ? TQ4_BYTES : TQ3_BYTES;
-    constexpr int NL = QT == 4 ? 16 : 8;
+    constexpr int BB = BlockBytes<QT>::value;
+    constexpr int NL = QT == 4 ? 16 : QT == 3 ? 8 : 4;
     __shared__ __align__(16) uint8_t s_in[DQ_TILE * BB];
     __shared__ float s_lvl[NL];
-    if (threadIdx.x < NL) s_lvl[threadIdx.x] = QT == 4 ? tq4_level(threadIdx.x) : tq3_level(threadIdx.x);
+    if (threadIdx.x < NL) s_lvl[threadIdx.x] = tq_level<QT>(threadIdx.x);
 
     const int64_t ntiles = (nblocks + DQ_TILE - 1) / DQ_TILE;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
@@ -637,6 +699,10 @@ dequantize_kernel(const uint8_t* __restrict__ xq, OUT* __restrict__ y, int64_t n
                                    ((uint32_t)blk[q + 2] << 16) | ((uint32_t)blk[q + 3] << 24);
                 const uint32_t nib = part < 4 ? (w & 0x0F0F0F0Fu) : ((w >> 4) & 0x0F0F0F0Fu);
                 c0 = nib & 15u; c1 = (nib >> 8) & 15u; c2 = (nib >> 16) & 15u; c3 = nib >> 24;
+            } else if constexpr (QT == 2) {
+                // elements 4p..4p+3 = the four 2-bit codes of byte p
+                const uint32_t b = blk[2 + part];
+                c0 = b & 3u; c1 = (b >> 2) & 3u; c2 = (b >> 4) & 3u; c3 = b >> 6;
             } else {
                 // group g = part/2 (3 bytes, 8 codes), half = part%2 -> codes 4*half..+3
                 const int q = 2 + 3 * (part >> 1);
@@ -678,64 +744,131 @@ static int codec_grid(int64_t ntiles, int per_sm) {
     return (int)(ntiles < cap ? (ntiles > 0 ? ntiles : 1) : cap);
 }
 
+struct RandRot {
+    uint32_t seed = 0;
+    int heads_per_row = 0;   // 0: no sign diagonal
+};
+
 template <int QT, typename IN, int MODE, int L2>
 static void launch_quant_k(const void* x, void* y, int64_t nblocks, int log2_hd, float norm, int n_passes,
-                           const RowMap& map, int grid, int xv, int yv, cudaStream_t st) {
+                           const RowMap& map, int grid, int xv, int yv, const RandRot& rr, cudaStream_t st) {
     quantize_kernel<QT, IN, MODE, L2><<<grid, CODEC_THREADS, 0, st>>>((const IN*)x, (uint8_t*)y, nblocks, log2_hd,
-                                                                      norm, n_passes, xv, yv, map);
+                                                                      norm, n_passes, xv, yv, map, rr.seed,
+                                                                      rr.heads_per_row);
 }
 
 template <int QT, typename IN, int MODE>
 static void launch_quant_l2(const void* x, void* y, int64_t nblocks, int log2_hd, float norm, int n_passes,
-                            const RowMap& map, int grid, int xv, int yv, cudaStream_t st) {
+                            const RowMap& map, int grid, int xv, int yv, const RandRot& rr, cudaStream_t st) {
     // head_dim 128 and 256 (and no rotation) get fully unrolled FWHT stages
     switch (log2_hd) {
-        case -1: launch_quant_k<QT, IN, MODE, -1>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, st); break;
-        case 7: launch_quant_k<QT, IN, MODE, 7>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, st); break;
-        case 8: launch_quant_k<QT, IN, MODE, 8>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, st); break;
-        default: launch_quant_k<QT, IN, MODE, -2>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, st); break;
+        case -1: launch_quant_k<QT, IN, MODE, -1>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st); break;
+        case 7: launch_quant_k<QT, IN, MODE, 7>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st); break;
+        case 8: launch_quant_k<QT, IN, MODE, 8>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st); break;
+        default: launch_quant_k<QT, IN, MODE, -2>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st); break;
     }
 }
 
 template <int QT, typename IN>
 static cudaError_t launch_quant_t(const void* x, void* y, int64_t nblocks, int log2_hd, float norm,
-                                  int n_passes, const RowMap& map, cudaStream_t st) {
+                                  int n_passes, const RowMap& map, const RandRot& rr, cudaStream_t st) {
     const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
     const int grid = codec_grid(ntiles, 16);
     const int xv = ((uintptr_t)x & 15) == 0, yv = ((uintptr_t)y & 15) == 0;
     if constexpr (QT == 3) {
         if (n_passes > 0) {
-            launch_quant_l2<QT, IN, 1>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, st);
+            launch_quant_l2<QT, IN, 1>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st);
             return cudaGetLastError();
         }
     }
-    launch_quant_l2<QT, IN, 0>(x, y, nblocks, log2_hd, norm, 0, map, grid, xv, yv, st);
+    launch_quant_l2<QT, IN, 0>(x, y, nblocks, log2_hd, norm, 0, map, grid, xv, yv, rr, st);
     return cudaGetLastError();
 }
 
 cudaError_t launch_quantize(int qtype, int in_dtype, const void* x, void* y, int64_t nblocks, int log2_hd,
-                            float norm, int n_passes, cudaStream_t st, const RowMap& map) {
+                            float norm, int n_passes, cudaStream_t st, const RowMap& map, uint32_t rseed,
+                            int heads_per_row) {
     if (nblocks <= 0) return cudaSuccess;
+    RandRot rr;
+    rr.seed = rseed;
+    rr.heads_per_row = heads_per_row;
     if (qtype == 4) {
         switch (in_dtype) {
-            case DT_F32: return launch_quant_t<4, float>(x, y, nblocks, log2_hd, norm, 0, map, st);
-            case DT_F16: return launch_quant_t<4, __half>(x, y, nblocks, log2_hd, norm, 0, map, st);
-            default: return launch_quant_t<4, __nv_bfloat16>(x, y, nblocks, log2_hd, norm, 0, map, st);
+            case DT_F32: return launch_quant_t<4, float>(x, y, nblocks, log2_hd, norm, 0, map, rr, st);
+            case DT_F16: return launch_quant_t<4, __half>(x, y, nblocks, log2_hd, norm, 0, map, rr, st);
+            default: return launch_quant_t<4, __nv_bfloat16>(x, y, nblocks, log2_hd, norm, 0, map, rr, st);
+        }
+    }
+    if (qtype == 2) {
+        switch (in_dtype) {
+            case DT_F32: return launch_quant_t<2, float>(x, y, nblocks, log2_hd, norm, 0, map, rr, st);
+            case DT_F16: return launch_quant_t<2, __half>(x, y, nblocks, log2_hd, norm, 0, map, rr, st);
+            default: return launch_quant_t<2, __nv_bfloat16>(x, y, nblocks, log2_hd, norm, 0, map, rr, st);
         }
     }
     switch (in_dtype) {
-        case DT_F32: return launch_quant_t<3, float>(x, y, nblocks, log2_hd, norm, n_passes, map, st);
-        case DT_F16: return launch_quant_t<3, __half>(x, y, nblocks, log2_hd, norm, n_passes, map, st);
-        default: return launch_quant_t<3, __nv_bfloat16>(x, y, nblocks, log2_hd, norm, n_passes, map, st);
+        case DT_F32: return launch_quant_t<3, float>(x, y, nblocks, log2_hd, norm, n_passes, map, rr, st);
+        case DT_F16: return launch_quant_t<3, __half>(x, y, nblocks, log2_hd, norm, n_passes, map, rr, st);
+        default: return launch_quant_t<3, __nv_bfloat16>(x, y, nblocks, log2_hd, norm, n_passes, map, rr, st);
     }
 }
 
-cudaError_t launch_fwht(float* x, int64_t nblocks, int log2_hd, float norm, cudaStream_t st) {
+cudaError_t launch_fwht(float* x, int64_t nblocks, int log2_hd, float norm, cudaStream_t st, uint32_t rseed,
+                        int heads_per_row) {
     if (nblocks <= 0) return cudaSuccess;
     const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
     fwht_kernel<<<codec_grid(ntiles, 16), CODEC_THREADS, 0, st>>>(x, nblocks, log2_hd, norm,
-                                                                  ((uintptr_t)x & 15) == 0);
+                                                                  ((uintptr_t)x & 15) == 0, rseed, heads_per_row);
     return cudaGetLastError();
+}
+
+// ── requantize: decode a tile of ST blocks, encode each block as DT ───────────
+template <int ST, int DT>
+__global__ void __launch_bounds__(CODEC_THREADS)
+requant_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t nblocks, int s_vec, int d_vec) {
+    constexpr int SB = BlockBytes<ST>::value, DB = BlockBytes<DT>::value;
+    __shared__ __align__(16) uint8_t s_in[CODEC_THREADS * SB];
+    __shared__ __align__(16) uint8_t s_out[CODEC_THREADS * DB];
+    __shared__ __align__(16) uint2 s_near[NEAR_ROWS * NEAR_REP];
+    near_table_init<DT>(s_near);
+    const uint32_t near_tb = (uint32_t)__cvta_generic_to_shared(s_near) + 8u * (threadIdx.x & (NEAR_REP - 1));
+    const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int64_t b0 = tile * CODEC_THREADS;
+        const int nrows = (int)(nblocks - b0 < CODEC_THREADS ? nblocks - b0 : CODEC_THREADS);
+        __syncthreads();   // s_in / s_out free
+        const int nbytes = nrows * SB;
+        const uint8_t* sp = src + b0 * SB;
+        if (s_vec && (nbytes & 15) == 0) {
+            for (int c = threadIdx.x; c < nbytes / 16; c += CODEC_THREADS)
+                reinterpret_cast<int4*>(s_in)[c] = __ldg(reinterpret_cast<const int4*>(sp) + c);
+        } else {
+            for (int b = threadIdx.x; b < nbytes; b += CODEC_THREADS) s_in[b] = sp[b];
+        }
+        __syncthreads();
+        float v[QK];
+        decode_block<ST>(s_in + (threadIdx.x < nrows ? threadIdx.x : 0) * SB, v);
+        encode_block<DT, 0>(v, near_tb, nullptr, 0, s_out, threadIdx.x * DB, threadIdx.x < nrows);
+        __syncthreads();
+        store_staged(dst + b0 * DB, s_out, nrows * DB, d_vec != 0);
+    }
+}
+
+template <int ST, int DT>
+static cudaError_t launch_requant_t(const void* src, void* dst, int64_t nblocks, cudaStream_t st) {
+    const int64_t ntiles = (nblocks + CODEC_THREADS - 1) / CODEC_THREADS;
+    requant_kernel<ST, DT><<<codec_grid(ntiles, 16), CODEC_THREADS, 0, st>>>(
+        (const uint8_t*)src, (uint8_t*)dst, nblocks, ((uintptr_t)src & 15) == 0, ((uintptr_t)dst & 15) == 0);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_requantize(int src_type, const void* src, int dst_type, void* dst, int64_t nblocks,
+                              cudaStream_t st) {
+    if (nblocks <= 0) return cudaSuccess;
+#define TQ_RQ(S, D) if (src_type == S && dst_type == D) return launch_requant_t<S, D>(src, dst, nblocks, st);
+    TQ_RQ(4, 3) TQ_RQ(4, 2) TQ_RQ(3, 2) TQ_RQ(3, 4) TQ_RQ(2, 4) TQ_RQ(2, 3) TQ_RQ(4, 4) TQ_RQ(3, 3) TQ_RQ(2, 2)
+#undef TQ_RQ
+    return cudaErrorInvalidValue;
 }
 
 template <int QT, typename OUT>
@@ -749,6 +882,13 @@ static cudaError_t launch_dq_t(const void* x, void* y, int64_t nblocks, cudaStre
 
 cudaError_t launch_dequantize(int qtype, int out_dtype, const void* x, void* y, int64_t nblocks, cudaStream_t st) {
     if (nblocks <= 0) return cudaSuccess;
+    if (qtype == 2) {
+        switch (out_dtype) {
+            case DT_F32: return launch_dq_t<2, float>(x, y, nblocks, st);
+            case DT_F16: return launch_dq_t<2, __half>(x, y, nblocks, st);
+            default: return launch_dq_t<2, __nv_bfloat16>(x, y, nblocks, st);
+        }
+    }
     if (qtype == 4) {
         switch (out_dtype) {
             case DT_F32: return launch_dq_t<4, float>(x, y, nblocks, st);

@@ -21,6 +21,8 @@ namespace tq {
 constexpr int QK = 32;
 constexpr int TQ4_BYTES = 18;
 constexpr int TQ3_BYTES = 14;
+constexpr int TQ2_BYTES = 10;
+template <int QT> struct BlockBytes { static constexpr int value = QT == 4 ? TQ4_BYTES : QT == 3 ? TQ3_BYTES : TQ2_BYTES; };
 
 // Lloyd-Max codebooks (src/ggml-tq.h:98-121).  Symmetric: L[n-1-i] == -L[i]
 // and B[n-2-i] == -B[i] exactly in float32, which the nearest-level search
@@ -35,7 +37,14 @@ __host__ __device__ constexpr float tq4_level(int i) {
          : i == 8 ? +0.0470277f : i == 9 ? +0.1421261f : i == 10 ? +0.2405254f : i == 11 ? +0.3450764f
          : i == 12 ? +0.4599576f : i == 13 ? +0.5923403f : i == 14 ? +0.7573038f : +1.0000000f;
 }
-// positive boundaries: TQ3 B[4..6], TQ4 B[8..14]
+__host__ __device__ constexpr float tq2_level(int i) {   // src/ggml-tq.h:89-91
+    return i == 0 ? -1.0000000f : i == 1 ? -0.2997714f : i == 2 ? +0.2997714f : +1.0000000f;
+}
+template <int QT> __host__ __device__ constexpr float tq_level(int i) {
+    return QT == 4 ? tq4_level(i) : QT == 3 ? tq3_level(i) : tq2_level(i);
+}
+// positive boundaries: TQ2 B[2], TQ3 B[4..6], TQ4 B[8..14]
+constexpr float TQ2_P0 = 0.6498857f;
 constexpr float TQ3_P0 = 0.2326114f, TQ3_P1 = 0.4879221f, TQ3_P2 = 0.8122602f;
 constexpr float TQ4_P0 = 0.0945769f, TQ4_P1 = 0.1913257f, TQ4_P2 = 0.2928009f, TQ4_P3 = 0.4025170f,
                 TQ4_P4 = 0.5261490f, TQ4_P5 = 0.6748221f, TQ4_P6 = 0.8786519f;
@@ -104,6 +113,43 @@ __device__ __forceinline__ int tq3_nearest(float xn) {
     const int c = (q1 ? 2 : 0) + (q2 ? 1 : 0);
     int idx = xn > 0.0f ? 4 + c : 3 - (neg ? c : 0);
     return (xn != xn) ? 0 : idx;
+}
+
+__device__ __forceinline__ int tq2_nearest(float xn) {   // linear scan of src/ggml-tq.c:100-106; NaN -> 0
+    const bool neg = xn < 0.0f;
+    float a = fminf(fabsf(xn), 1.0f);
+    a = neg ? nextup_pos(a) : a;
+    const int q = a > TQ2_P0 ? 1 : 0;
+    int idx = xn > 0.0f ? 2 + q : 1 - (neg ? q : 0);
+    return (xn != xn) ? 0 : idx;
+}
+
+// ── LCG of randomized_hadamard_transform (src/ggml-tq.c:383-396) ──────────
+// s <- s * 1664525 + 1013904223 (mod 2^32); element i of a chunk is negated when bit 31
+// of the state after i + 1 steps is set.  lcg_jump(n) gives (A, C) with
+// LCG^n(s) = A s + C, composed by squaring: LCG^(m+n) = (A_m A_n, A_m C_n + C_m).
+constexpr uint32_t LCG_A = 1664525u, LCG_C = 1013904223u;
+__host__ __device__ inline void lcg_jump(uint32_t n, uint32_t& A, uint32_t& C) {
+    uint32_t ra = 1u, rc = 0u, pa = LCG_A, pc = LCG_C;   // result, and the power 2^b step
+    while (n) {
+        if (n & 1u) { rc = pa * rc + pc; ra = pa * ra; }
+        pc = pa * pc + pc;
+        pa = pa * pa;
+        n >>= 1;
+    }
+    A = ra;
+    C = rc;
+}
+// negate v[i] for the 32 elements starting at chunk position j0 of a chunk seeded s0
+__device__ __forceinline__ void lcg_signs32(float (&v)[32], uint32_t s0, uint32_t j0) {
+    uint32_t A, C;
+    lcg_jump(j0, A, C);
+    uint32_t s = A * s0 + C;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        s = s * LCG_A + LCG_C;
+        v[i] = __uint_as_float(__float_as_uint(v[i]) ^ (s & 0x80000000u));
+    }
 }
 
 // ── input element conversion ─────────────────────────────────────────────

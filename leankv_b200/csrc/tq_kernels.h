@@ -23,10 +23,17 @@ struct RowMap {
 
 // [FWHT over heads of 2^log2_hd elements when log2_hd >= 0] + quantize nblocks blocks.
 // qtype 3 or 4; in_dtype DT_F32/DT_F16/DT_BF16; n_passes > 0 selects TQ3 optimal rounding.
+// heads_per_row > 0: randomized_hadamard_transform_row signs (chunk h of a row seeded rseed + h)
+// before the rotation (log2_hd >= 5)
 cudaError_t launch_quantize(int qtype, int in_dtype, const void* x, void* y, int64_t nblocks, int log2_hd,
-                            float norm, int n_passes, cudaStream_t st, const RowMap& map = RowMap());
+                            float norm, int n_passes, cudaStream_t st, const RowMap& map = RowMap(),
+                            uint32_t rseed = 0, int heads_per_row = 0);
 // in-place FWHT of nblocks 32-element rows (heads of 2^log2_hd <= 1024 elements)
-cudaError_t launch_fwht(float* x, int64_t nblocks, int log2_hd, float norm, cudaStream_t st);
+cudaError_t launch_fwht(float* x, int64_t nblocks, int log2_hd, float norm, cudaStream_t st, uint32_t rseed = 0,
+                        int heads_per_row = 0);
+// decode src_type blocks and encode them as dst_type (types 2, 3, 4)
+cudaError_t launch_requantize(int src_type, const void* src, int dst_type, void* dst, int64_t nblocks,
+                              cudaStream_t st);
 // FWHT of a tail shorter than 32 elements (heads smaller than 32)
 cudaError_t launch_fwht_tail(float* x, int n, int log2_hd, float norm, cudaStream_t st);
 // FWHT of rows longer than 1024 elements, one CTA per row

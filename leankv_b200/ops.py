@@ -13,7 +13,7 @@ import torch
 from . import _lib as L
 
 QK = L.QK
-TQ3_0, TQ4_0 = L.TYPE_TQ3_0, L.TYPE_TQ4_0
+TQ2_0, TQ3_0, TQ4_0 = L.TYPE_TQ2_0, L.TYPE_TQ3_0, L.TYPE_TQ4_0
 BLOCK_BYTES = L.BLOCK_BYTES
 _DTYPES = {torch.float32: L.DTYPE_F32, torch.float16: L.DTYPE_F16, torch.bfloat16: L.DTYPE_BF16}
 
@@ -29,20 +29,22 @@ def _need_cuda(*ts: torch.Tensor) -> None:
 
 
 def _qtype(qtype) -> int:
-    q = {3: TQ3_0, 4: TQ4_0, "tq3_0": TQ3_0, "tq4_0": TQ4_0}.get(qtype)
+    q = {2: TQ2_0, 3: TQ3_0, 4: TQ4_0, "tq2_0": TQ2_0, "tq3_0": TQ3_0, "tq4_0": TQ4_0}.get(qtype)
     if q is None:
         raise ValueError(f"unknown TQ type {qtype!r}")
     return q
 
 
 def quantize(x: torch.Tensor, qtype=4, fwht_head_dim: int = 0, opt_passes: int = 0,
-             out: torch.Tensor | None = None) -> torch.Tensor:
+             out: torch.Tensor | None = None, rht_seed: int | None = None, row_len: int | None = None) -> torch.Tensor:
     """[FWHT per fwht_head_dim run] + TQ quantize of a contiguous f32/f16/bf16 tensor.
 
     Returns uint8 blocks shaped (*x.shape[:-1], x.shape[-1] // 32, block_bytes).
     Bit-exact with hadamard_transform_row + quantize_row_tq*_0_ref
     (src/ggml-tq.c) on x.float(); opt_passes=2 with qtype=3 is LeanKV's TQ3
-    optimal rounding (scripts/tq3_rounding.py:74-125).
+    optimal rounding (scripts/tq3_rounding.py:74-125).  With rht_seed, every row of
+    row_len elements (default: the last dimension) is first rotated as
+    randomized_hadamard_transform_row(row, row_len, fwht_head_dim, rht_seed).
     """
     _need_cuda(x)
     q = _qtype(qtype)
@@ -59,6 +61,11 @@ def quantize(x: torch.Tensor, qtype=4, fwht_head_dim: int = 0, opt_passes: int =
         _need_cuda(out)
         if out.dtype != torch.uint8 or out.numel() != x.numel() // QK * BLOCK_BYTES[q] or not out.is_contiguous():
             raise ValueError("out must be a contiguous uint8 tensor of the block size")
+    if rht_seed is not None:
+        L.check(L.load().tq_quantize_randomized_cuda(q, x.data_ptr(), _DTYPES[x.dtype], out.data_ptr(), x.numel(),
+                                                     int(row_len or x.shape[-1]), int(fwht_head_dim),
+                                                     int(rht_seed) & 0xFFFFFFFF, int(opt_passes), _stream(x)))
+        return out
     L.check(L.load().tq_quantize_cuda(q, x.data_ptr(), _DTYPES[x.dtype], out.data_ptr(), x.numel(),
                                       int(fwht_head_dim), int(opt_passes), _stream(x)))
     return out
@@ -134,3 +141,29 @@ def kv_append(src: torch.Tensor, cache: torch.Tensor, pos: torch.Tensor | None =
                                        int(rotate), int(opt_passes),
                                        overflow.data_ptr() if overflow is not None else None, _stream(src)))
     return cache
+
+
+def requantize(blocks: torch.Tensor, src_qtype, dst_qtype) -> torch.Tensor:
+    """Blocks of src_qtype -> blocks of dst_qtype (dequantize + quantize per block, one kernel;
+    requantize_tq4_to_tq3 / tq3_to_tq2 / tq4_to_tq2 of src/ggml-tq.c:329-357)."""
+    _need_cuda(blocks)
+    a, b = _qtype(src_qtype), _qtype(dst_qtype)
+    if blocks.dtype != torch.uint8 or not blocks.is_contiguous() or blocks.numel() % BLOCK_BYTES[a]:
+        raise ValueError("blocks must be a contiguous uint8 tensor of whole blocks")
+    nb = blocks.numel() // BLOCK_BYTES[a]
+    shape = (*blocks.shape[:-1], BLOCK_BYTES[b]) if blocks.dim() >= 1 and blocks.shape[-1] == BLOCK_BYTES[a] \
+        else (nb, BLOCK_BYTES[b])
+    out = torch.empty(shape, dtype=torch.uint8, device=blocks.device)
+    L.check(L.load().tq_requantize_cuda(a, blocks.data_ptr(), b, out.data_ptr(), nb * QK, _stream(blocks)))
+    return out
+
+
+def hadamard_randomized_(x: torch.Tensor, head_dim: int, seed: int, row_len: int | None = None) -> torch.Tensor:
+    """In-place randomized_hadamard_transform_row (src/ggml-tq.c:383-412) on every row of row_len
+    elements (default: the last dimension) of a contiguous float32 tensor."""
+    _need_cuda(x)
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous float32 tensor")
+    L.check(L.load().tq_hadamard_randomized_cuda(x.data_ptr(), x.numel(), int(row_len or x.shape[-1]), int(head_dim),
+                                                 int(seed) & 0xFFFFFFFF, _stream(x)))
+    return x

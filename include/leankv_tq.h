@@ -176,6 +176,46 @@ tq_status tq_hadamard_host(float *x, int64_t n, int head_dim);
 tq_status tq_hadamard_randomized_host(float *x, int64_t n, int row_len, int head_dim, uint32_t seed);
 tq_status tq_requantize_host(tq_type src_type, const void *src, tq_type dst_type, void *dst, int64_t k);
 
+/* ── outlier channels: channel-permuted mixed precision (src/ggml-tq-outlier.h) ─
+ *
+ * Same types, names and semantics as the reference (ggml-tq-outlier.h:31-169):
+ * calibration ranks channels by variance (top outlier_frac, rounded up to whole
+ * 32-element blocks, are the outliers); a head vector is permuted outliers-first
+ * and its two runs are quantized as ordinary blocks of the two tiers.  The
+ * drop-in names take host pointers and handle one head vector per call, like the
+ * reference; the *_cuda variants handle n_vec vectors of device memory
+ * (x: [n_vec][head_dim]; buffers: [n_vec][n_outlier/32 blocks] and
+ * [n_vec][n_normal/32 blocks]).  head_dim: a multiple of 32 up to 256 for
+ * quantize / dequantize. */
+#ifndef GGML_TQ_OUTLIER_H
+#define TQ_OUTLIER_MAX_DIM 256
+typedef enum { TQ_TIER_TQ2 = 0, TQ_TIER_TQ3 = 1, TQ_TIER_TQ4 = 2 } tq_tier_t;
+typedef struct {
+    int head_dim, n_outlier, n_normal;
+    float outlier_frac;
+    tq_tier_t outlier_tier, normal_tier;
+    int perm[TQ_OUTLIER_MAX_DIM];        /* position i holds original channel perm[i] */
+    int inv_perm[TQ_OUTLIER_MAX_DIM];    /* original channel c sits at position inv_perm[c] */
+    float channel_var[TQ_OUTLIER_MAX_DIM];
+} tq_outlier_config;
+#endif
+void tq_identify_outliers(tq_outlier_config *config, const float *calib_data, int n_tokens, int head_dim,
+                          float outlier_frac, tq_tier_t outlier_tier, tq_tier_t normal_tier);
+void tq_outlier_config_init_uniform(tq_outlier_config *config, int head_dim, tq_tier_t tier);
+void tq_mixed_buffer_sizes(const tq_outlier_config *config, size_t *outlier_size, size_t *normal_size);
+float tq_mixed_effective_bpe(const tq_outlier_config *config);
+void tq_mixed_quantize(const float *x, const tq_outlier_config *config, void *outlier_buf, void *normal_buf);
+void tq_mixed_dequantize(const void *outlier_buf, const void *normal_buf, const tq_outlier_config *config, float *y);
+void tq_permute_channels(const float *x, float *y, const int *perm, int n);
+void tq_unpermute_channels(const float *x, float *y, const int *inv_perm, int n);
+/* calibration from device data [n_tokens][head_dim]; fills the host struct (synchronous on stream) */
+tq_status tq_outlier_identify_cuda(tq_outlier_config *config, const float *calib, int n_tokens, int head_dim,
+                                   float outlier_frac, tq_tier_t outlier_tier, tq_tier_t normal_tier, void *stream);
+tq_status tq_mixed_quantize_cuda(const tq_outlier_config *config, const void *x, tq_dtype x_dtype, int64_t n_vec,
+                                 void *outlier_buf, void *normal_buf, void *stream);
+tq_status tq_mixed_dequantize_cuda(const tq_outlier_config *config, const void *outlier_buf, const void *normal_buf,
+                                   int64_t n_vec, float *y, void *stream);
+
 /* ── prototype vector codec (prototype/turboquant, no C counterpart) ─────────
  *
  * The Python prototype's per-vector TurboQuant (prototype/turboquant/quantizer.py:103-221,

@@ -79,6 +79,18 @@ SIGNATURES = {
     "tq_decode_attention_static_cuda": (_i32, [_v, _v]),
     "tq_lse_combine_cuda": (_i32, [_i32, _i64, _i32, _v, _v, _v, _v, _v]),
     "tq_lse_merge_cuda": (_i32, [_i32, _i64, _i32, _v, _i64, _v, _i64, _v, _i32, _v, _v]),
+    # outlier channels (mixed precision); config pointers are host struct pointers
+    "tq_identify_outliers": (None, [_v, _v, _i32, _i32, _f32, _i32, _i32]),
+    "tq_outlier_config_init_uniform": (None, [_v, _i32, _i32]),
+    "tq_mixed_buffer_sizes": (None, [_v, _v, _v]),
+    "tq_mixed_effective_bpe": (_f32, [_v]),
+    "tq_mixed_quantize": (None, [_v, _v, _v, _v]),
+    "tq_mixed_dequantize": (None, [_v, _v, _v, _v]),
+    "tq_permute_channels": (None, [_v, _v, _v, _i32]),
+    "tq_unpermute_channels": (None, [_v, _v, _v, _i32]),
+    "tq_outlier_identify_cuda": (_i32, [_v, _v, _i32, _i32, _f32, _i32, _i32, _v]),
+    "tq_mixed_quantize_cuda": (_i32, [_v, _v, _i32, _i64, _v, _v, _v]),
+    "tq_mixed_dequantize_cuda": (_i32, [_v, _v, _v, _i64, _v, _v]),
     # prototype vector codec (levels / boundaries are host float arrays)
     "tq_proto_encode_cuda": (_i32, [_v, _i32, _v, _i64, _i32, _i32, _v, _i32, _i32, _v, _v, _v, _v, _v, _v, _v]),
     "tq_proto_decode_cuda": (_i32, [_v, _v, _i64, _i32, _i32, _v, _v, _i32, _v, _i32, _v, _v, _v]),

@@ -27,6 +27,7 @@
 
 #include "tq_common.cuh"
 #include "tq_kernels.h"
+#include "tq_outlier.h"
 
 namespace tq {
 
@@ -964,6 +965,171 @@ cudaError_t launch_fwht_large(float* x, int64_t nrows, int log2_hd, float norm, 
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+
+// ── channel-permuted mixed precision (src/ggml-tq-outlier.c:97-290) ────────────
+// Calibration: per-channel mean and variance over the calibration tokens,
+// accumulated in token order exactly as the reference does (one thread per
+// channel, no contraction into fma); the stable descending rank of the variances
+// is the permutation.  Quantize: one thread per output block gathers its 32
+// permuted values and encodes them with the block encoder above (bit-identical
+// to quantize_row_tq*_0_ref); the first n_outlier/32 blocks of a vector use the
+// outlier tier, the rest the normal tier.  Dequantize scatters a decoded block
+// back through the permutation.
+
+// ── runtime-type dispatch of the block encoder / decoder (mixed-precision tiers) ──
+__device__ __forceinline__ int block_bytes_rt(int qt) { return qt == 4 ? TQ4_BYTES : qt == 3 ? TQ3_BYTES : TQ2_BYTES; }
+
+__device__ void near_table_init_rt(int qt, uint2* t) {
+    if (qt == 4) near_table_init<4>(t);
+    else if (qt == 3) near_table_init<3>(t);
+    else near_table_init<2>(t);
+}
+
+// encode v as a block of type qt at global byte address dst (2-byte aligned)
+__device__ void encode_block_rt(int qt, float (&v)[QK], uint32_t near_tb, uint8_t* dst) {
+    uint8_t* base = reinterpret_cast<uint8_t*>((uintptr_t)dst & ~uintptr_t(3));
+    const int off = (int)((uintptr_t)dst & 3u);
+    if (qt == 4) encode_block<4, 0>(v, near_tb, nullptr, 0, base, off, true);
+    else if (qt == 3) encode_block<3, 0>(v, near_tb, nullptr, 0, base, off, true);
+    else encode_block<2, 0>(v, near_tb, nullptr, 0, base, off, true);
+}
+
+__device__ void decode_block_rt(int qt, const uint8_t* blk, float (&v)[QK]) {
+    if (qt == 4) decode_block<4>(blk, v);
+    else if (qt == 3) decode_block<3>(blk, v);
+    else decode_block<2>(blk, v);
+}
+
+
+__global__ void __launch_bounds__(OUTLIER_MAX_DIM)
+outlier_calib_kernel(const float* __restrict__ data, int n_tokens, int hd, float* __restrict__ var_out,
+                     int* __restrict__ perm_out, int* __restrict__ inv_out) {
+    __shared__ float s_var[OUTLIER_MAX_DIM];
+    const int d = threadIdx.x;
+    if (d < hd) {
+        float m = 0.0f;
+        for (int t = 0; t < n_tokens; ++t) m = __fadd_rn(m, data[(int64_t)t * hd + d]);
+        m = __fdiv_rn(m, (float)n_tokens);
+        float v = 0.0f;
+        for (int t = 0; t < n_tokens; ++t) {
+            const float diff = __fsub_rn(data[(int64_t)t * hd + d], m);
+            v = __fadd_rn(v, __fmul_rn(diff, diff));
+        }
+        v = __fdiv_rn(v, (float)n_tokens);
+        s_var[d] = v;
+        var_out[d] = v;
+    }
+    __syncthreads();
+    if (d < hd) {
+        // position of channel d in a stable sort by descending variance
+        int r = 0;
+        for (int e = 0; e < hd; ++e) r += (s_var[e] > s_var[d]) || (s_var[e] == s_var[d] && e < d);
+        perm_out[r] = d;
+        inv_out[d] = r;
+    }
+}
+
+template <typename IN> __device__ __forceinline__ float ld_f(const IN* p);
+template <> __device__ __forceinline__ float ld_f<float>(const float* p) { return *p; }
+template <> __device__ __forceinline__ float ld_f<__half>(const __half* p) { return __half2float(*p); }
+template <> __device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+constexpr int MIX_THREADS = 128;
+
+template <typename IN>
+__global__ void __launch_bounds__(MIX_THREADS)
+mixed_quantize_kernel(const IN* __restrict__ x, int64_t n_vec, const MixedPlan plan, uint8_t* __restrict__ obuf,
+                      uint8_t* __restrict__ nbuf) {
+    __shared__ int s_perm[OUTLIER_MAX_DIM];
+    __shared__ __align__(16) uint2 s_near[2][NEAR_ROWS * NEAR_REP];
+    for (int i = threadIdx.x; i < plan.head_dim; i += MIX_THREADS) s_perm[i] = plan.perm[i];
+    near_table_init_rt(plan.otype, s_near[0]);
+    near_table_init_rt(plan.ntype, s_near[1]);
+    __syncthreads();
+    const int nblk = plan.head_dim / QK, nob = plan.n_outlier / QK, nnb = nblk - nob;
+    const int64_t total = n_vec * nblk;
+    const uint32_t lane_off = 8u * (threadIdx.x & (NEAR_REP - 1));
+    for (int64_t gb = (int64_t)blockIdx.x * MIX_THREADS + threadIdx.x; gb < total; gb += (int64_t)gridDim.x * MIX_THREADS) {
+        const int64_t v = gb / nblk;
+        const int b = (int)(gb - v * nblk);
+        float vals[QK];
+#pragma unroll
+        for (int i = 0; i < QK; ++i) vals[i] = ld_f<IN>(x + v * plan.head_dim + s_perm[QK * b + i]);
+        if (b < nob) {
+            const uint32_t tb = (uint32_t)__cvta_generic_to_shared(s_near[0]) + lane_off;
+            encode_block_rt(plan.otype, vals, tb, obuf + (v * nob + b) * (int64_t)block_bytes_rt(plan.otype));
+        } else {
+            const uint32_t tb = (uint32_t)__cvta_generic_to_shared(s_near[1]) + lane_off;
+            encode_block_rt(plan.ntype, vals, tb, nbuf + (v * nnb + (b - nob)) * (int64_t)block_bytes_rt(plan.ntype));
+        }
+    }
+}
+
+__global__ void __launch_bounds__(MIX_THREADS)
+mixed_dequantize_kernel(const uint8_t* __restrict__ obuf, const uint8_t* __restrict__ nbuf, int64_t n_vec,
+                        const MixedPlan plan, float* __restrict__ y) {
+    __shared__ int s_perm[OUTLIER_MAX_DIM];
+    for (int i = threadIdx.x; i < plan.head_dim; i += MIX_THREADS) s_perm[i] = plan.perm[i];
+    __syncthreads();
+    const int nblk = plan.head_dim / QK, nob = plan.n_outlier / QK, nnb = nblk - nob;
+    const int64_t total = n_vec * nblk;
+    for (int64_t gb = (int64_t)blockIdx.x * MIX_THREADS + threadIdx.x; gb < total; gb += (int64_t)gridDim.x * MIX_THREADS) {
+        const int64_t v = gb / nblk;
+        const int b = (int)(gb - v * nblk);
+        float vals[QK];
+        if (b < nob) decode_block_rt(plan.otype, obuf + (v * nob + b) * (int64_t)block_bytes_rt(plan.otype), vals);
+        else decode_block_rt(plan.ntype, nbuf + (v * nnb + (b - nob)) * (int64_t)block_bytes_rt(plan.ntype), vals);
+        // unpermute: y[perm[j]] = permuted[j]  (== y[i] = permuted[inv_perm[i]])
+#pragma unroll
+        for (int i = 0; i < QK; ++i) y[v * plan.head_dim + s_perm[QK * b + i]] = vals[i];
+    }
+}
+
+// y[i] = x[map[i]] for n_vec vectors of n elements
+__global__ void gather_kernel(const float* __restrict__ x, const MixedPlan plan, int64_t n_vec, float* __restrict__ y) {
+    const int64_t total = n_vec * plan.head_dim;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t v = e / plan.head_dim;
+        const int i = (int)(e - v * plan.head_dim);
+        y[e] = x[v * plan.head_dim + plan.perm[i]];
+    }
+}
+
+static int mix_grid(int64_t work, int threads) {
+    const int64_t g = (work + threads - 1) / threads;
+    const int64_t cap = (int64_t)sm_count() * 16;
+    return (int)(g < 1 ? 1 : (g < cap ? g : cap));
+}
+
+cudaError_t launch_outlier_calib(const float* data, int n_tokens, int hd, float* var, int* perm, int* inv,
+                                 cudaStream_t st) {
+    outlier_calib_kernel<<<1, OUTLIER_MAX_DIM, 0, st>>>(data, n_tokens, hd, var, perm, inv);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mixed_quantize(int in_dtype, const void* x, int64_t n_vec, const MixedPlan& plan, void* obuf,
+                                  void* nbuf, cudaStream_t st) {
+    const int grid = mix_grid(n_vec * (plan.head_dim / QK), MIX_THREADS);
+    switch (in_dtype) {
+        case DT_F32: mixed_quantize_kernel<float><<<grid, MIX_THREADS, 0, st>>>((const float*)x, n_vec, plan, (uint8_t*)obuf, (uint8_t*)nbuf); break;
+        case DT_F16: mixed_quantize_kernel<__half><<<grid, MIX_THREADS, 0, st>>>((const __half*)x, n_vec, plan, (uint8_t*)obuf, (uint8_t*)nbuf); break;
+        default: mixed_quantize_kernel<__nv_bfloat16><<<grid, MIX_THREADS, 0, st>>>((const __nv_bfloat16*)x, n_vec, plan, (uint8_t*)obuf, (uint8_t*)nbuf); break;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mixed_dequantize(const void* obuf, const void* nbuf, int64_t n_vec, const MixedPlan& plan, float* y,
+                                    cudaStream_t st) {
+    const int grid = mix_grid(n_vec * (plan.head_dim / QK), MIX_THREADS);
+    mixed_dequantize_kernel<<<grid, MIX_THREADS, 0, st>>>((const uint8_t*)obuf, (const uint8_t*)nbuf, n_vec, plan, y);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather(const float* x, const MixedPlan& plan, int64_t n_vec, float* y, cudaStream_t st) {
+    gather_kernel<<<mix_grid(n_vec * plan.head_dim, 256), 256, 0, st>>>(x, plan, n_vec, y);
+    return cudaGetLastError();
 }
 
 }  // namespace tq

@@ -167,3 +167,55 @@ def hadamard_randomized_(x: torch.Tensor, head_dim: int, seed: int, row_len: int
     L.check(L.load().tq_hadamard_randomized_cuda(x.data_ptr(), x.numel(), int(row_len or x.shape[-1]), int(head_dim),
                                                  int(seed) & 0xFFFFFFFF, _stream(x)))
     return x
+
+
+class OutlierConfig(C.Structure):
+    """Mirror of tq_outlier_config (src/ggml-tq-outlier.h:44-64, include/leankv_tq.h)."""
+    _fields_ = [("head_dim", C.c_int), ("n_outlier", C.c_int), ("n_normal", C.c_int), ("outlier_frac", C.c_float),
+                ("outlier_tier", C.c_int), ("normal_tier", C.c_int), ("perm", C.c_int * 256),
+                ("inv_perm", C.c_int * 256), ("channel_var", C.c_float * 256)]
+
+
+TIER_TQ2, TIER_TQ3, TIER_TQ4 = 0, 1, 2
+_TIER_BYTES = {TIER_TQ2: 10, TIER_TQ3: 14, TIER_TQ4: 18}
+
+
+def identify_outliers(calib: torch.Tensor, outlier_frac: float = 0.25, outlier_tier: int = TIER_TQ3,
+                      normal_tier: int = TIER_TQ2) -> OutlierConfig:
+    """Per-channel variance ranking of calibration data [n_tokens, head_dim] (float32, CUDA)
+    -> outlier configuration (tq_identify_outliers, src/ggml-tq-outlier.c:97-170)."""
+    _need_cuda(calib)
+    if calib.dtype != torch.float32 or calib.dim() != 2 or not calib.is_contiguous():
+        raise ValueError("calib must be a contiguous float32 [n_tokens, head_dim] tensor")
+    cfg = OutlierConfig()
+    L.check(L.load().tq_outlier_identify_cuda(C.byref(cfg), calib.data_ptr(), calib.shape[0], calib.shape[1],
+                                              float(outlier_frac), int(outlier_tier), int(normal_tier), _stream(calib)))
+    return cfg
+
+
+def mixed_quantize(x: torch.Tensor, cfg: OutlierConfig) -> tuple[torch.Tensor, torch.Tensor]:
+    """Channel-permuted two-tier quantization of head vectors x [..., head_dim]
+    (tq_mixed_quantize per vector) -> (outlier blocks, normal blocks) uint8."""
+    _need_cuda(x)
+    if x.dtype not in _DTYPES or not x.is_contiguous() or x.shape[-1] != cfg.head_dim:
+        raise ValueError("x must be a contiguous f32/f16/bf16 tensor with head_dim last")
+    n_vec = x.numel() // cfg.head_dim
+    ob = torch.empty(*x.shape[:-1], cfg.n_outlier // QK, _TIER_BYTES[cfg.outlier_tier], dtype=torch.uint8, device=x.device)
+    nb = torch.empty(*x.shape[:-1], cfg.n_normal // QK, _TIER_BYTES[cfg.normal_tier], dtype=torch.uint8, device=x.device)
+    L.check(L.load().tq_mixed_quantize_cuda(C.byref(cfg), x.data_ptr(), _DTYPES[x.dtype], n_vec, ob.data_ptr(),
+                                            nb.data_ptr(), _stream(x)))
+    return ob, nb
+
+
+def mixed_dequantize(outlier_blocks: torch.Tensor, normal_blocks: torch.Tensor, cfg: OutlierConfig) -> torch.Tensor:
+    """Inverse of mixed_quantize: float32 [..., head_dim] in the original channel order."""
+    _need_cuda(outlier_blocks, normal_blocks)
+    lead = outlier_blocks.shape[:-2] if cfg.n_outlier else normal_blocks.shape[:-2]
+    n_vec = 1
+    for s in lead:
+        n_vec *= s
+    y = torch.empty(*lead, cfg.head_dim, dtype=torch.float32, device=outlier_blocks.device)
+    L.check(L.load().tq_mixed_dequantize_cuda(C.byref(cfg), outlier_blocks.contiguous().data_ptr(),
+                                              normal_blocks.contiguous().data_ptr(), n_vec, y.data_ptr(),
+                                              _stream(outlier_blocks)))
+    return y

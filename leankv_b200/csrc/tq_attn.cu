@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
     // layout: LUT | stages [warp][stage] | scale scratch [warp] | barriers [warp][stage] | flag
     uint8_t* stages = smem + LUT_BYTES;
     uint8_t* scratch = stages + WARPS * ATT_STAGES * STAGE;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + WARPS * SCR);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + WARPS * 2 * SCR);
     int* s_abort = reinterpret_cast<int*>(bars + WARPS * ATT_STAGES);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
     __syncthreads();
 
     const uint32_t stage0 = smem_u32(stages + warp * ATT_STAGES * STAGE);
-    const uint32_t scr = smem_u32(scratch + warp * SCR);
+    const uint32_t scr = smem_u32(scratch + warp * 2 * SCR);   // tile A at scr, tile B at scr + SCR
     const uint32_t bar0 = smem_u32(&bars[warp * ATT_STAGES]);
     // per-lane fixed offsets inside a stage
     constexpr int KROW8 = (Cfg::tok_of_row(8) - Cfg::tok_of_row(0)) * KB;   // row g+8 relative to row g
@@ -447,107 +447,156 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
             vsrc += (size_t)WARPS * ATT_TILE * VB;
             ++issued;
         };
-        static_for<0, ATT_STAGES - 1>([&](auto sc) { issue_next(sc); });
+        // Tiles are processed in pairs: tiles 2p and 2p + 1 sit in stages 2p mod 4 and
+        // 2p + 1 mod 4, and while a pair is computed the next pair is in flight in the
+        // other two stages.  Two tiles per step give the scheduler two independent
+        // dequantize / mma chains and one softmax update per 32 tokens.
+        static_for<0, 2>([&](auto sc) { issue_next(sc); });
+        uint32_t bad_scale = 0;   // max |d| bits over the block scales seen
 
-        uint32_t bad_scale = 0;
+        // block-scale extraction of one tile into scratch xs: K -> f32 [row][blk], V -> f16 bits
+        // [blk][row]; tokens past `valid` (stale or never-written stage bytes) get scale 0
+        auto extract = [&](uint32_t st, uint32_t xs, int valid) {
+            static_for<0, 2 * NXH>([&](auto r_c) {
+                constexpr int r = decltype(r_c)::value;
+                constexpr bool IS_V = r >= NXH;
+                constexpr int rr = IS_V ? r - NXH : r;
+                const bool xv = xt0 + rr * TSTEP < valid;
+                const uint32_t src = IS_V ? xvs + rr * TSTEP * VB : xks + rr * TSTEP * KB;
+                uint16_t h;
+                asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(st + src));
+                h = xv ? h : (uint16_t)0;
+                // |d| >= 2^15 (|bits| >= 0x7800): exponent 31 decodes as a finite value in the reference but
+                // as inf/nan in IEEE fp16, and P * d could overflow fp16: reported once per segment
+                bad_scale = max(bad_scale, (uint32_t)(h & 0x7FFFu));
+                if (!IS_V) {
+                    const float f = __half2float(__ushort_as_half(h));
+                    asm volatile("st.shared.f32 [%0], %1;" ::"r"(xs + xkd + rr * ROWSTEP * NBLK * 4), "f"(f));
+                } else {
+                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(xs + xvd + rr * ROWSTEP * 2), "h"(h));
+                }
+            });
+        };
+        // S = K q~^T of one tile (block scales applied in fp32); tokens past `valid` -> -inf
+        auto scores = [&](uint32_t st, uint32_t xs, int valid, float (&sc)[4]) {
+            sc[0] = sc[1] = sc[2] = sc[3] = 0.0f;
+            float dka[NBLK], dkb[NBLK];
+            static_for<0, NBLK / 4>([&](auto c_c) {
+                constexpr int c = decltype(c_c)::value;
+                const float4 x = ld128f<c * 16>(xs + gq * NBLK * 4);
+                const float4 y = ld128f<8 * NBLK * 4 + c * 16>(xs + gq * NBLK * 4);
+                dka[4 * c] = x.x; dka[4 * c + 1] = x.y; dka[4 * c + 2] = x.z; dka[4 * c + 3] = x.w;
+                dkb[4 * c] = y.x; dkb[4 * c + 1] = y.y; dkb[4 * c + 2] = y.z; dkb[4 * c + 3] = y.w;
+            });
+            static_for<0, NBLK>([&](auto blk_c) {
+                constexpr int blk = decltype(blk_c)::value;
+                float acc[4];
+                uint32_t af[4];
+                if constexpr (KT == 4) {
+                    const uint32_t kr = st + k_off;
+                    uint32_t w0 = ld16<blk * TQ4_BYTES>(kr), w1 = ld16<blk * TQ4_BYTES + KROW8>(kr);
+                    af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
+                    af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);
+                    af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
+                    af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
+                    mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
+                    w0 = ld16<blk * TQ4_BYTES + 8>(kr);
+                    w1 = ld16<blk * TQ4_BYTES + 8 + KROW8>(kr);
+                    af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
+                    af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);
+                    af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
+                    af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
+                    mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
+                } else {
+                    constexpr int IMM = blk * TQ3_BYTES - 2 * (blk & 1);
+                    const uint32_t kr = st + ((blk & 1) ? k3_off_o : k3_off_e);
+                    const uint32_t sh = (blk & 1) ? k3_sh_o : k3_sh_e;
+                    const uint32_t wg = __funnelshift_r(ld32<IMM>(kr), ld32<IMM + 4>(kr), sh);
+                    const uint32_t wh = __funnelshift_r(ld32<IMM + KROW8>(kr), ld32<IMM + KROW8 + 4>(kr), sh);
+                    af[0] = lut_ld_addr<RES>(tq3_lut_addr<0>(wg, lane4x));
+                    af[1] = lut_ld_addr<RES>(tq3_lut_addr<0>(wh, lane4x));
+                    af[2] = lut_ld_addr<RES>(tq3_lut_addr<1>(wg, lane4x));
+                    af[3] = lut_ld_addr<RES>(tq3_lut_addr<1>(wh, lane4x));
+                    mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
+                    af[0] = lut_ld_addr<RES>(tq3_lut_addr<2>(wg, lane4x));
+                    af[1] = lut_ld_addr<RES>(tq3_lut_addr<2>(wh, lane4x));
+                    af[2] = lut_ld_addr<RES>(tq3_lut_addr<3>(wg, lane4x));
+                    af[3] = lut_ld_addr<RES>(tq3_lut_addr<3>(wh, lane4x));
+                    mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
+                }
+                sc[0] = fmaf(dka[blk], acc[0], sc[0]);
+                sc[1] = fmaf(dka[blk], acc[1], sc[1]);
+                sc[2] = fmaf(dkb[blk], acc[2], sc[2]);
+                sc[3] = fmaf(dkb[blk], acc[3], sc[3]);
+            });
+            if (valid < ATT_TILE) {
+                if (Cfg::tok_of_row(gq) >= valid) { sc[0] = -INFINITY; sc[1] = -INFINITY; }
+                if (Cfg::tok_of_row(gq + 8) >= valid) { sc[2] = -INFINITY; sc[3] = -INFINITY; }
+            }
+        };
+        // O^T += V^T P' of one tile; pb01 / pb23 are the transposed P fragments
+        auto accumulate = [&](uint32_t st, uint32_t xs, uint32_t pb01, uint32_t pb23) {
+            const uint32_t vr = st + KTILE + v_off;
+            const uint32_t sdv = xs + ATT_TILE * NBLK * 4 + 4 * tq;
+            static_for<0, NBLK>([&](auto blk_c) {
+                constexpr int blk = decltype(blk_c)::value;
+                const uint32_t w0 = ld16<blk * TQ4_BYTES>(vr), w1 = ld16<blk * TQ4_BYTES + VO1>(vr);
+                const uint32_t w2 = ld16<blk * TQ4_BYTES + VO8>(vr), w3 = ld16<blk * TQ4_BYTES + VO9>(vr);
+                // bytes [A0 B0 A1 B1] of the two tokens of a k pair; the codebook index of an element
+                // pair is (A nibble | B nibble << 4), built with one bit-select per word
+                const uint32_t ra = prmt(w0, w1, 0x5140u), rb = prmt(w2, w3, 0x5140u);
+                const uint32_t ra4 = ra >> 4, rb4 = rb >> 4, ra8 = ra >> 8, rb8 = rb >> 8;
+                const uint32_t xa = (ra & 0x0F0F0F0Fu) | (ra4 & 0xF0F0F0F0u);
+                const uint32_t ya = (ra4 & 0x0F0F0F0Fu) | (ra8 & 0xF0F0F0F0u);
+                const uint32_t xb = (rb & 0x0F0F0F0Fu) | (rb4 & 0xF0F0F0F0u);
+                const uint32_t yb = (rb4 & 0x0F0F0F0Fu) | (rb8 & 0xF0F0F0F0u);
+                const uint32_t b0 = h2_mul(pb01, ld32<blk * ATT_TILE * 2>(sdv));
+                const uint32_t b1 = h2_mul(pb23, ld32<blk * ATT_TILE * 2 + 16>(sdv));
+                uint32_t af[4];
+                af[0] = lut_ld<RES>(xa, lane4, LUT_SEL0);
+                af[1] = lut_ld<RES>(ya, lane4, LUT_SEL0);
+                af[2] = lut_ld<RES>(xb, lane4, LUT_SEL0);
+                af[3] = lut_ld<RES>(yb, lane4, LUT_SEL0);
+                mma16816(o[2 * blk], af, b0, b1);
+                af[0] = lut_ld<RES>(xa, lane4, LUT_SEL2);
+                af[1] = lut_ld<RES>(ya, lane4, LUT_SEL2);
+                af[2] = lut_ld<RES>(xb, lane4, LUT_SEL2);
+                af[3] = lut_ld<RES>(yb, lane4, LUT_SEL2);
+                mma16816(o[2 * blk + 1], af, b0, b1);
+            });
+        };
+
         bool timed_out = false;
         for (int i0 = 0; i0 < ntiles && !timed_out; i0 += ATT_STAGES) {
-            static_for<0, ATT_STAGES>([&](auto stage_c) {
-                constexpr int S = decltype(stage_c)::value;
-                const int i = i0 + S;
-                if (i >= ntiles || timed_out) return;
-                issue_next(std::integral_constant<int, (S + ATT_STAGES - 1) % ATT_STAGES>{});
+            static_for<0, 2>([&](auto pair_c) {
+                constexpr int SA = 2 * decltype(pair_c)::value, SB = SA + 1;
+                const int ia = i0 + SA;
+                if (ia >= ntiles || timed_out) return;
+                const bool has_b = ia + 1 < ntiles;
+                // the next pair goes into the stages the previous pair released
+                issue_next(std::integral_constant<int, (SA + 2) % ATT_STAGES>{});
+                issue_next(std::integral_constant<int, (SB + 2) % ATT_STAGES>{});
                 // every lane waits; the outcome is made warp-uniform before any warp collective
-                const bool arrived = __all_sync(0xffffffffu, mbar_wait(bar0 + 8 * S, (phase_bits >> S) & 1u));
-                if (!arrived) {
+                bool ok = mbar_wait(bar0 + 8 * SA, (phase_bits >> SA) & 1u);
+                if (has_b) ok = ok && mbar_wait(bar0 + 8 * SB, (phase_bits >> SB) & 1u);
+                if (!__all_sync(0xffffffffu, ok)) {
                     timed_out = true;
                     return;
                 }
-                phase_bits ^= 1u << S;
-                const uint32_t st = stage0 + S * STAGE;
-                const int valid = i == ntiles - 1 ? last_valid : ATT_TILE;
-
-                // block scales: K -> f32 [row][blk], V -> f16 bits [blk][row]; tokens past the
-                // valid range (stale or never-written stage bytes) get scale 0
-                static_for<0, 2 * NXH>([&](auto r_c) {
-                    constexpr int r = decltype(r_c)::value;
-                    constexpr bool IS_V = r >= NXH;
-                    constexpr int rr = IS_V ? r - NXH : r;
-                    const bool xv = xt0 + rr * TSTEP < valid;
-                    const uint32_t src = IS_V ? xvs + rr * TSTEP * VB : xks + rr * TSTEP * KB;
-                    uint16_t h;
-                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(st + src));
-                    h = xv ? h : (uint16_t)0;
-                    // |d| >= 2^15: exponent 31 decodes as a finite value in the reference but as
-                    // inf/nan in IEEE fp16, and P * d could overflow fp16: reported once per segment
-                    bad_scale |= (h & 0x7C00u) >= 0x7800u;
-                    if (!IS_V) {
-                        const float f = __half2float(__ushort_as_half(h));
-                        asm volatile("st.shared.f32 [%0], %1;" ::"r"(scr + xkd + rr * ROWSTEP * NBLK * 4), "f"(f));
-                    } else {
-                        asm volatile("st.shared.u16 [%0], %1;" ::"r"(scr + xvd + rr * ROWSTEP * 2), "h"(h));
-                    }
-                });
+                phase_bits ^= (1u << SA) | (has_b ? (1u << SB) : 0u);
+                const int valid_a = ia == ntiles - 1 ? last_valid : ATT_TILE;
+                const int valid_b = !has_b ? 0 : (ia + 1 == ntiles - 1 ? last_valid : ATT_TILE);
+                const uint32_t sta = stage0 + SA * STAGE, stb = stage0 + SB * STAGE;
+                extract(sta, scr, valid_a);
+                extract(stb, scr + SCR, valid_b);
                 __syncwarp();
+                float sa[4], sb[4];
+                scores(sta, scr, valid_a, sa);
+                scores(stb, scr + SCR, valid_b, sb);
 
-                // ---- S = K q~^T ----
-                float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                float dka[NBLK], dkb[NBLK];
-                static_for<0, NBLK / 4>([&](auto c_c) {
-                    constexpr int c = decltype(c_c)::value;
-                    const float4 x = ld128f<c * 16>(scr + gq * NBLK * 4);
-                    const float4 y = ld128f<8 * NBLK * 4 + c * 16>(scr + gq * NBLK * 4);
-                    dka[4 * c] = x.x; dka[4 * c + 1] = x.y; dka[4 * c + 2] = x.z; dka[4 * c + 3] = x.w;
-                    dkb[4 * c] = y.x; dkb[4 * c + 1] = y.y; dkb[4 * c + 2] = y.z; dkb[4 * c + 3] = y.w;
-                });
-                static_for<0, NBLK>([&](auto blk_c) {
-                    constexpr int blk = decltype(blk_c)::value;
-                    float acc[4];
-                    uint32_t af[4];
-                    if constexpr (KT == 4) {
-                        const uint32_t kr = st + k_off;
-                        uint32_t w0 = ld16<blk * TQ4_BYTES>(kr), w1 = ld16<blk * TQ4_BYTES + KROW8>(kr);
-                        af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
-                        af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);
-                        af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
-                        af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
-                        mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
-                        w0 = ld16<blk * TQ4_BYTES + 8>(kr);
-                        w1 = ld16<blk * TQ4_BYTES + 8 + KROW8>(kr);
-                        af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
-                        af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);
-                        af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
-                        af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
-                        mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
-                    } else {
-                        constexpr int IMM = blk * TQ3_BYTES - 2 * (blk & 1);
-                        const uint32_t kr = st + ((blk & 1) ? k3_off_o : k3_off_e);
-                        const uint32_t sh = (blk & 1) ? k3_sh_o : k3_sh_e;
-                        const uint32_t wg = __funnelshift_r(ld32<IMM>(kr), ld32<IMM + 4>(kr), sh);
-                        const uint32_t wh = __funnelshift_r(ld32<IMM + KROW8>(kr), ld32<IMM + KROW8 + 4>(kr), sh);
-                        af[0] = lut_ld_addr<RES>(tq3_lut_addr<0>(wg, lane4x));
-                        af[1] = lut_ld_addr<RES>(tq3_lut_addr<0>(wh, lane4x));
-                        af[2] = lut_ld_addr<RES>(tq3_lut_addr<1>(wg, lane4x));
-                        af[3] = lut_ld_addr<RES>(tq3_lut_addr<1>(wh, lane4x));
-                        mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
-                        af[0] = lut_ld_addr<RES>(tq3_lut_addr<2>(wg, lane4x));
-                        af[1] = lut_ld_addr<RES>(tq3_lut_addr<2>(wh, lane4x));
-                        af[2] = lut_ld_addr<RES>(tq3_lut_addr<3>(wg, lane4x));
-                        af[3] = lut_ld_addr<RES>(tq3_lut_addr<3>(wh, lane4x));
-                        mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
-                    }
-                    sc[0] = fmaf(dka[blk], acc[0], sc[0]);
-                    sc[1] = fmaf(dka[blk], acc[1], sc[1]);
-                    sc[2] = fmaf(dkb[blk], acc[2], sc[2]);
-                    sc[3] = fmaf(dkb[blk], acc[3], sc[3]);
-                });
-                if (valid < ATT_TILE) {
-                    if (Cfg::tok_of_row(gq) >= valid) { sc[0] = -INFINITY; sc[1] = -INFINITY; }
-                    if (Cfg::tok_of_row(gq + 8) >= valid) { sc[2] = -INFINITY; sc[3] = -INFINITY; }
-                }
-
-                // ---- online softmax (log2 domain) ----
-                float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+                // ---- online softmax over the 32 tokens (log2 domain) ----
+                float mx0 = fmaxf(fmaxf(sa[0], sa[2]), fmaxf(sb[0], sb[2]));
+                float mx1 = fmaxf(fmaxf(sa[1], sa[3]), fmaxf(sb[1], sb[3]));
 #pragma unroll
                 for (int sh = 4; sh < 32; sh <<= 1) {
                     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
@@ -567,41 +616,15 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     l0 *= al0;
                     l1 *= al1;
                 }
-                const float p0 = ex2(sc[0] - m_run0), p1 = ex2(sc[1] - m_run1);
-                const float p2 = ex2(sc[2] - m_run0), p3 = ex2(sc[3] - m_run1);
-                l0 += p0 + p2;
-                l1 += p1 + p3;
-                const uint32_t pb01 = movmatrix_t(pack_h2(p0, p1));
-                const uint32_t pb23 = movmatrix_t(pack_h2(p2, p3));
-
-                // ---- O^T += V^T P' ----
-                const uint32_t vr = st + KTILE + v_off;
-                const uint32_t sdv = scr + ATT_TILE * NBLK * 4 + 4 * tq;
-                static_for<0, NBLK>([&](auto blk_c) {
-                    constexpr int blk = decltype(blk_c)::value;
-                    const uint32_t w0 = ld16<blk * TQ4_BYTES>(vr), w1 = ld16<blk * TQ4_BYTES + VO1>(vr);
-                    const uint32_t w2 = ld16<blk * TQ4_BYTES + VO8>(vr), w3 = ld16<blk * TQ4_BYTES + VO9>(vr);
-                    const uint32_t ra = prmt(w0, w1, 0x5140u), rb = prmt(w2, w3, 0x5140u);
-                    const uint32_t ra4 = ra >> 4, rb4 = rb >> 4;
-                    const uint32_t xa = (ra & 0x000F000Fu) | (ra4 & 0x00F000F0u);
-                    const uint32_t ya = (ra4 & 0x000F000Fu) | ((ra >> 8) & 0x00F000F0u);
-                    const uint32_t xb = (rb & 0x000F000Fu) | (rb4 & 0x00F000F0u);
-                    const uint32_t yb = (rb4 & 0x000F000Fu) | ((rb >> 8) & 0x00F000F0u);
-                    const uint32_t b0 = h2_mul(pb01, ld32<blk * ATT_TILE * 2>(sdv));
-                    const uint32_t b1 = h2_mul(pb23, ld32<blk * ATT_TILE * 2 + 16>(sdv));
-                    uint32_t af[4];
-                    af[0] = lut_ld<RES>(xa, lane4, LUT_SEL0);
-                    af[1] = lut_ld<RES>(ya, lane4, LUT_SEL0);
-                    af[2] = lut_ld<RES>(xb, lane4, LUT_SEL0);
-                    af[3] = lut_ld<RES>(yb, lane4, LUT_SEL0);
-                    mma16816(o[2 * blk], af, b0, b1);
-                    af[0] = lut_ld<RES>(xa, lane4, LUT_SEL2);
-                    af[1] = lut_ld<RES>(ya, lane4, LUT_SEL2);
-                    af[2] = lut_ld<RES>(xb, lane4, LUT_SEL2);
-                    af[3] = lut_ld<RES>(yb, lane4, LUT_SEL2);
-                    mma16816(o[2 * blk + 1], af, b0, b1);
-                });
-                __syncwarp();   // stage S and the scratch may be overwritten from here on
+                const float pa0 = ex2(sa[0] - m_run0), pa1 = ex2(sa[1] - m_run1);
+                const float pa2 = ex2(sa[2] - m_run0), pa3 = ex2(sa[3] - m_run1);
+                const float pb0 = ex2(sb[0] - m_run0), pb1 = ex2(sb[1] - m_run1);
+                const float pb2 = ex2(sb[2] - m_run0), pb3 = ex2(sb[3] - m_run1);
+                l0 += (pa0 + pa2) + (pb0 + pb2);
+                l1 += (pa1 + pa3) + (pb1 + pb3);
+                accumulate(sta, scr, movmatrix_t(pack_h2(pa0, pa1)), movmatrix_t(pack_h2(pa2, pa3)));
+                accumulate(stb, scr + SCR, movmatrix_t(pack_h2(pb0, pb1)), movmatrix_t(pack_h2(pb2, pb3)));
+                __syncwarp();   // stages SA, SB and the scratch may be overwritten from here on
             });
         }
         if (timed_out) {
@@ -613,7 +636,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
 #pragma unroll
             for (int s2 = 0; s2 < ATT_STAGES; ++s2) mbar_wait(bar0 + 8 * s2, (phase_bits >> s2) & 1u);
         }
-        if (__any_sync(0xffffffffu, bad_scale != 0) && lane == 0) atomicExch(a.err, (int)TQ_ERROR_UNSUPPORTED);
+        if (__any_sync(0xffffffffu, bad_scale >= 0x7800u) && lane == 0) atomicExch(a.err, (int)TQ_ERROR_UNSUPPORTED);
 
         // ---- merge the warps, write the (pair, slot) partial ----
 #pragma unroll
@@ -745,7 +768,7 @@ static size_t decode_smem_bytes() {
     const size_t stg = (size_t)Cfg::WARPS * ATT_STAGES * Cfg::STAGE;
     const size_t red = (size_t)Cfg::WARPS * ATT_N * (D + 2) * 4;   // warp merge scratch reuses the stages
     s += stg > red ? stg : red;
-    s += (size_t)Cfg::WARPS * Cfg::SCR;
+    s += (size_t)Cfg::WARPS * 2 * Cfg::SCR;
     s += (size_t)Cfg::WARPS * ATT_STAGES * 8;
     s += 16;
     return s;

@@ -53,12 +53,16 @@ size_t dtype_bytes(int dt) { return dt == TQ_DTYPE_F32 ? 4 : 2; }
 bool dtype_ok(int dt) { return dt == TQ_DTYPE_F32 || dt == TQ_DTYPE_F16 || dt == TQ_DTYPE_BF16; }
 bool type_ok(int t) { return t == TQ_TYPE_TQ2_0 || t == TQ_TYPE_TQ3_0 || t == TQ_TYPE_TQ4_0; }
 
-// ── host-API contexts: one stream + grow-only device buffer each ───────────
+// ── host-API contexts: two streams + two grow-only device staging buffers ───
+// Host calls move their data in chunks that alternate between the two streams:
+// chunk c copies in, computes and copies out on stream c % 2, so the copies of one
+// chunk overlap the kernel and the copies of the other, and the host-to-device
+// and device-to-host copy engines run at the same time.
 struct HostCtx {
     int dev = -1;
-    cudaStream_t st = nullptr;
-    void* buf = nullptr;
-    size_t cap = 0;
+    cudaStream_t st[2] = {nullptr, nullptr};
+    void* buf[2] = {nullptr, nullptr};
+    size_t cap = 0;   // bytes of each staging buffer
 };
 
 static std::mutex g_pool_mu;
@@ -85,8 +89,14 @@ static tq_status ctx_acquire(HostCtx** out) {
     }
     HostCtx* c = new HostCtx;
     c->dev = dev;
-    s = cuda_status(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking), "cudaStreamCreate");
-    if (s) { delete c; return s; }
+    for (int i = 0; i < 2; ++i) {
+        s = cuda_status(cudaStreamCreateWithFlags(&c->st[i], cudaStreamNonBlocking), "cudaStreamCreate");
+        if (s) {
+            if (i) cudaStreamDestroy(c->st[0]);
+            delete c;
+            return s;
+        }
+    }
     *out = c;
     return TQ_SUCCESS;
 }
@@ -98,15 +108,17 @@ static void ctx_release(HostCtx* c) {
 
 static tq_status ctx_reserve(HostCtx* c, size_t bytes) {
     if (bytes <= c->cap) return TQ_SUCCESS;
-    if (c->buf) {
-        cudaStreamSynchronize(c->st);
-        cudaFree(c->buf);
-        c->buf = nullptr;
-        c->cap = 0;
+    for (int i = 0; i < 2; ++i) {
+        cudaStreamSynchronize(c->st[i]);
+        if (c->buf[i]) cudaFree(c->buf[i]);
+        c->buf[i] = nullptr;
     }
-    size_t cap = (bytes + ((1u << 20) - 1)) & ~size_t((1u << 20) - 1);
-    tq_status s = cuda_status(cudaMalloc(&c->buf, cap), "cudaMalloc (host API staging)");
-    if (s) return s;
+    c->cap = 0;
+    const size_t cap = (bytes + ((1u << 20) - 1)) & ~size_t((1u << 20) - 1);
+    for (int i = 0; i < 2; ++i) {
+        tq_status s = cuda_status(cudaMalloc(&c->buf[i], cap), "cudaMalloc (host API staging)");
+        if (s) return s;
+    }
     c->cap = cap;
     return TQ_SUCCESS;
 }
@@ -117,13 +129,40 @@ struct CtxGuard {
     ~CtxGuard() { if (c) ctx_release(c); }
 };
 
-// chunk size (elements) for host calls: bounded device staging
-static int64_t host_chunk_elems(int64_t k, int64_t unit, size_t bytes_per_elem) {
-    const size_t budget = size_t(512) << 20;   // 512 MiB of staging per call
-    int64_t ch = (int64_t)(budget / (bytes_per_elem ? bytes_per_elem : 1));
-    ch = ch / unit * unit;
-    if (ch < unit) ch = unit;
-    return ch < k ? ch : k;
+// Pipelined host operation over `total` units (elements or blocks).  A chunk of n
+// units reads n * in_per bytes from hin + u0 * in_per and writes n * out_per bytes to
+// hout + u0 * out_per; op(dev_in, dev_out, u0, n, stream) computes it on the device
+// (dev_out may equal dev_in for in-place operations).  Chunks hold about an eighth of
+// the work, between 1 MiB and 64 MiB of traffic, in multiples of `align` units.
+template <typename Op>
+static tq_status host_pipeline(HostCtx* c, int64_t total, int64_t align, size_t in_per, size_t out_per,
+                               const void* hin, void* hout, bool in_place, Op op) {
+    const size_t per = in_per + out_per;
+    int64_t ch = (total + 7) / 8;
+    const int64_t lo = (int64_t)((size_t(1) << 20) / per), hi = (int64_t)((size_t(64) << 20) / per);
+    if (ch < lo) ch = lo;
+    if (ch > hi) ch = hi;
+    ch = (ch + align - 1) / align * align;
+    if (ch > total) ch = total;
+    const size_t in_bytes = (size_t)ch * in_per, out_off = in_place ? 0 : (in_bytes + 255) & ~size_t(255);
+    tq_status s = ctx_reserve(c, out_off + (in_place ? in_bytes : (size_t)ch * out_per));
+    if (s) return s;
+    int k = 0;
+    for (int64_t u0 = 0; u0 < total && !s; u0 += ch, ++k) {
+        const int64_t n = total - u0 < ch ? total - u0 : ch;
+        cudaStream_t st = c->st[k & 1];
+        uint8_t* d = (uint8_t*)c->buf[k & 1];
+        s = cuda_status(cudaMemcpyAsync(d, (const uint8_t*)hin + u0 * in_per, n * in_per, cudaMemcpyHostToDevice, st),
+                        "cudaMemcpyAsync H2D");
+        if (!s) s = op(d, d + out_off, u0, n, st);
+        if (!s)
+            s = cuda_status(cudaMemcpyAsync((uint8_t*)hout + u0 * out_per, d + out_off, n * out_per,
+                                            cudaMemcpyDeviceToHost, st),
+                            "cudaMemcpyAsync D2H");
+    }
+    const tq_status s0 = cuda_status(cudaStreamSynchronize(c->st[0]), "cudaStreamSynchronize");
+    const tq_status s1 = cuda_status(cudaStreamSynchronize(c->st[1]), "cudaStreamSynchronize");
+    return s ? s : (s0 ? s0 : s1);
 }
 
 }  // namespace tq
@@ -298,28 +337,16 @@ extern "C" tq_status tq_quantize_host(tq_type type, const void* x, tq_dtype x_dt
     if (k < 0 || k % QK) return set_error(TQ_ERROR_INVALID_VALUE, "k=%lld is not a multiple of 32", (long long)k);
     if (k == 0) return TQ_SUCCESS;
     if (!x || !y) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
-    const int64_t unit = fwht_head_dim > QK ? fwht_head_dim : QK;
     if (fwht_head_dim > 0 && k % fwht_head_dim) return set_error(TQ_ERROR_INVALID_VALUE, "k is not a multiple of fwht_head_dim");
     CtxGuard g;
     tq_status s = ctx_acquire(&g.c);
     if (s) return s;
-    const size_t eb = dtype_bytes(x_dtype), bb = block_bytes(type);
-    const int64_t chunk = host_chunk_elems(k, unit, eb + bb / QK + 1);
-    const size_t in_bytes = (size_t)chunk * eb, out_off = (in_bytes + 255) & ~size_t(255);
-    if ((s = ctx_reserve(g.c, out_off + (size_t)(chunk / QK) * bb))) return s;
-    uint8_t* dbuf = (uint8_t*)g.c->buf;
-    for (int64_t e0 = 0; e0 < k; e0 += chunk) {
-        const int64_t n = k - e0 < chunk ? k - e0 : chunk;
-        if ((s = cuda_status(cudaMemcpyAsync(dbuf, (const uint8_t*)x + e0 * eb, n * eb, cudaMemcpyHostToDevice, g.c->st),
-                             "cudaMemcpyAsync H2D")))
-            return s;
-        if ((s = tq_quantize_cuda(type, dbuf, x_dtype, dbuf + out_off, n, fwht_head_dim, opt_passes, g.c->st))) return s;
-        if ((s = cuda_status(cudaMemcpyAsync((uint8_t*)y + (e0 / QK) * bb, dbuf + out_off, (n / QK) * bb,
-                                             cudaMemcpyDeviceToHost, g.c->st),
-                             "cudaMemcpyAsync D2H")))
-            return s;
-    }
-    return cuda_status(cudaStreamSynchronize(g.c->st), "cudaStreamSynchronize");
+    // units: blocks of 32 elements, chunks aligned to whole heads
+    const int64_t align = fwht_head_dim > QK ? fwht_head_dim / QK : 1;
+    return host_pipeline(g.c, k / QK, align, QK * dtype_bytes(x_dtype), block_bytes(type), x, y, false,
+                         [&](uint8_t* din, uint8_t* dout, int64_t, int64_t n, cudaStream_t st) {
+                             return tq_quantize_cuda(type, din, x_dtype, dout, n * QK, fwht_head_dim, opt_passes, st);
+                         });
 }
 
 extern "C" tq_status tq_dequantize_host(tq_type type, const void* x, void* y, tq_dtype y_dtype, int64_t k) {
@@ -331,24 +358,10 @@ extern "C" tq_status tq_dequantize_host(tq_type type, const void* x, void* y, tq
     CtxGuard g;
     tq_status s = ctx_acquire(&g.c);
     if (s) return s;
-    const size_t eb = dtype_bytes(y_dtype), bb = block_bytes(type);
-    const int64_t chunk = host_chunk_elems(k, QK * 8, eb + bb / QK + 1);
-    const size_t in_bytes = (size_t)(chunk / QK) * bb, out_off = (in_bytes + 255) & ~size_t(255);
-    if ((s = ctx_reserve(g.c, out_off + (size_t)chunk * eb))) return s;
-    uint8_t* dbuf = (uint8_t*)g.c->buf;
-    for (int64_t e0 = 0; e0 < k; e0 += chunk) {
-        const int64_t n = k - e0 < chunk ? k - e0 : chunk;
-        if ((s = cuda_status(cudaMemcpyAsync(dbuf, (const uint8_t*)x + (e0 / QK) * bb, (n / QK) * bb,
-                                             cudaMemcpyHostToDevice, g.c->st),
-                             "cudaMemcpyAsync H2D")))
-            return s;
-        if ((s = tq_dequantize_cuda(type, dbuf, dbuf + out_off, y_dtype, n, g.c->st))) return s;
-        if ((s = cuda_status(cudaMemcpyAsync((uint8_t*)y + e0 * eb, dbuf + out_off, n * eb, cudaMemcpyDeviceToHost,
-                                             g.c->st),
-                             "cudaMemcpyAsync D2H")))
-            return s;
-    }
-    return cuda_status(cudaStreamSynchronize(g.c->st), "cudaStreamSynchronize");
+    return host_pipeline(g.c, k / QK, 8, block_bytes(type), QK * dtype_bytes(y_dtype), x, y, false,
+                         [&](uint8_t* din, uint8_t* dout, int64_t, int64_t n, cudaStream_t st) {
+                             return tq_dequantize_cuda(type, din, dout, y_dtype, n * QK, st);
+                         });
 }
 
 extern "C" tq_status tq_hadamard_host(float* x, int64_t n, int head_dim) {
@@ -360,20 +373,12 @@ extern "C" tq_status tq_hadamard_host(float* x, int64_t n, int head_dim) {
     CtxGuard g;
     tq_status s = ctx_acquire(&g.c);
     if (s) return s;
-    const int64_t unit = head_dim > QK ? head_dim : QK;
-    int64_t chunk = host_chunk_elems(n, unit, 4);
-    if (chunk < n && chunk % head_dim) chunk -= chunk % head_dim;
-    if ((s = ctx_reserve(g.c, (size_t)chunk * 4))) return s;
-    float* d = (float*)g.c->buf;
-    for (int64_t e0 = 0; e0 < n; e0 += chunk) {
-        const int64_t m = n - e0 < chunk ? n - e0 : chunk;
-        if ((s = cuda_status(cudaMemcpyAsync(d, x + e0, m * 4, cudaMemcpyHostToDevice, g.c->st), "cudaMemcpyAsync H2D")))
-            return s;
-        if ((s = tq_hadamard_cuda(d, m, head_dim, g.c->st))) return s;
-        if ((s = cuda_status(cudaMemcpyAsync(x + e0, d, m * 4, cudaMemcpyDeviceToHost, g.c->st), "cudaMemcpyAsync D2H")))
-            return s;
-    }
-    return cuda_status(cudaStreamSynchronize(g.c->st), "cudaStreamSynchronize");
+    // units: floats, chunks aligned to whole heads (and to 32-element tiles)
+    const int64_t align = head_dim > QK ? head_dim : QK;
+    return host_pipeline(g.c, n, n % align ? n : align, 4, 4, x, x, true,
+                         [&](uint8_t* din, uint8_t*, int64_t, int64_t m, cudaStream_t st) {
+                             return tq_hadamard_cuda((float*)din, m, head_dim, st);
+                         });
 }
 
 extern "C" tq_status tq_hadamard_randomized_host(float* x, int64_t n, int row_len, int head_dim, uint32_t seed) {
@@ -387,20 +392,10 @@ extern "C" tq_status tq_hadamard_randomized_host(float* x, int64_t n, int row_le
     CtxGuard g;
     tq_status s = ctx_acquire(&g.c);
     if (s) return s;
-    int64_t chunk = host_chunk_elems(n, row_len, 4);
-    chunk -= chunk % row_len;
-    if (chunk <= 0) chunk = row_len;
-    if ((s = ctx_reserve(g.c, (size_t)chunk * 4))) return s;
-    float* d = (float*)g.c->buf;
-    for (int64_t e0 = 0; e0 < n; e0 += chunk) {
-        const int64_t m = n - e0 < chunk ? n - e0 : chunk;
-        if ((s = cuda_status(cudaMemcpyAsync(d, x + e0, m * 4, cudaMemcpyHostToDevice, g.c->st), "cudaMemcpyAsync H2D")))
-            return s;
-        if ((s = tq_hadamard_randomized_cuda(d, m, row_len, head_dim, seed, g.c->st))) return s;
-        if ((s = cuda_status(cudaMemcpyAsync(x + e0, d, m * 4, cudaMemcpyDeviceToHost, g.c->st), "cudaMemcpyAsync D2H")))
-            return s;
-    }
-    return cuda_status(cudaStreamSynchronize(g.c->st), "cudaStreamSynchronize");
+    return host_pipeline(g.c, n, row_len, 4, 4, x, x, true,
+                         [&](uint8_t* din, uint8_t*, int64_t, int64_t m, cudaStream_t st) {
+                             return tq_hadamard_randomized_cuda((float*)din, m, row_len, head_dim, seed, st);
+                         });
 }
 
 extern "C" tq_status tq_requantize_host(tq_type src_type, const void* src, tq_type dst_type, void* dst, int64_t k) {
@@ -412,24 +407,10 @@ extern "C" tq_status tq_requantize_host(tq_type src_type, const void* src, tq_ty
     CtxGuard g;
     tq_status s = ctx_acquire(&g.c);
     if (s) return s;
-    const size_t sb = block_bytes(src_type), db = block_bytes(dst_type);
-    const int64_t chunk = host_chunk_elems(k, QK * 8, (sb + db) / QK + 1);
-    const size_t in_bytes = (size_t)(chunk / QK) * sb, out_off = (in_bytes + 255) & ~size_t(255);
-    if ((s = ctx_reserve(g.c, out_off + (size_t)(chunk / QK) * db))) return s;
-    uint8_t* dbuf = (uint8_t*)g.c->buf;
-    for (int64_t e0 = 0; e0 < k; e0 += chunk) {
-        const int64_t n = k - e0 < chunk ? k - e0 : chunk;
-        if ((s = cuda_status(cudaMemcpyAsync(dbuf, (const uint8_t*)src + (e0 / QK) * sb, (n / QK) * sb,
-                                             cudaMemcpyHostToDevice, g.c->st),
-                             "cudaMemcpyAsync H2D")))
-            return s;
-        if ((s = tq_requantize_cuda(src_type, dbuf, dst_type, dbuf + out_off, n, g.c->st))) return s;
-        if ((s = cuda_status(cudaMemcpyAsync((uint8_t*)dst + (e0 / QK) * db, dbuf + out_off, (n / QK) * db,
-                                             cudaMemcpyDeviceToHost, g.c->st),
-                             "cudaMemcpyAsync D2H")))
-            return s;
-    }
-    return cuda_status(cudaStreamSynchronize(g.c->st), "cudaStreamSynchronize");
+    return host_pipeline(g.c, k / QK, 8, block_bytes(src_type), block_bytes(dst_type), src, dst, false,
+                         [&](uint8_t* din, uint8_t* dout, int64_t, int64_t n, cudaStream_t st) {
+                             return tq_requantize_cuda(src_type, din, dst_type, dout, n * QK, st);
+                         });
 }
 
 // ── ggml drop-in names (src/ggml-tq.h:145-190) ───────────────────────────────

@@ -133,7 +133,8 @@ def dist_setup():
         import datetime
         import torch.distributed as dist
         # rank 0 prints exactly one JSON line on stdout: keep NCCL's version banner off it
-        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))

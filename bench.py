@@ -302,7 +302,7 @@ class Attn:
         self.bytes_per_step = kv_bytes + self.q.numel() * 2 + self.out.numel() * 2          # this rank
         kv_total = B * Hkv * T * (D // 32) * (kb + 18)
         self.job_bytes = kv_total + B * Hq * D * 2 * 2                                       # all ranks
-        self.launches_per_step = 4 if self.split else 3
+        self.launches_per_step = 2 if self.split else 1        # decode (+ rank merge)
         self.scaling = "strong"
         self.flush_l2 = False
         self.l2_note = f"KV {kv_total / 1e9:.2f} GB per step (> L2 126 MB), no flush"
@@ -359,7 +359,7 @@ class Stream:
     Prefill quantizes 16384 bf16 tokens per sequence into every layer (quantize-on-write with the
     head_dim Hadamard rotation).  A step is one decode step of all 80 layers: append one token's K
     and V per sequence at its current length, then decode attention (32 query heads, group 4) over
-    the grown context.  The 80-layer step (400 kernel launches) is captured once in a CUDA graph
+    the grown context.  The 80-layer step (240 kernel launches) is captured once in a CUDA graph
     and replayed; the append slots and lengths live on the device and advance inside the graph.
     Ranks split the batch of 32 ("strong" scaling, no collective).
     """
@@ -413,7 +413,7 @@ class Stream:
         with torch.cuda.graph(self.graph):
             self._body()
         self.steps_done -= 1                     # capture records the step without running it
-        self.launches_per_step = self.nl * 5
+        self.launches_per_step = self.nl * 3                   # K append, V append, decode
         per_tok = H * nb * 18 * 2                                       # K + V bytes per token and sequence
         self._per_tok = per_tok
         self.scaling = "strong"

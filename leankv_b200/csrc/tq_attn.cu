@@ -8,25 +8,29 @@
 // blocks; the kernel never materialises them in memory.
 //
 // Kernels
-//   attn_qprep_kernel   FWHT(q) * sm_scale * log2(e) -> fp16, scattered into the
-//                       register layout of the mma B operand (once per step)
 //   attn_decode_kernel  persistent; CTA = 16 warps, each warp streams its own
 //                       16-token K/V tiles through a 4-stage ring of 1-D bulk
 //                       copies (cp.async.bulk + mbarrier), dequantizes them
 //                       straight into mma.sync.m16n8k16 fragments through a
 //                       shared-memory byte -> half2 codebook table, and keeps an
-//                       online softmax; warps of a CTA merge in shared memory and
-//                       write one (m, l, O) partial per (sequence, KV head, split)
-//   attn_combine_kernel log-sum-exp merge of the split partials, inverse FWHT,
-//                       output cast, optional lse
+//                       online softmax.  Per (sequence, KV head) segment the CTA
+//                       first rotates and scales the query heads of the group
+//                       (FWHT(q) * sm_scale * log2(e) -> fp16 fragments) while
+//                       its first tiles are in flight; at the end its warps merge
+//                       in shared memory and write one (m, l, O) partial.  The
+//                       last CTA to finish a pair (atomic counter) merges that
+//                       pair's partials, applies the inverse FWHT, casts the
+//                       output and writes the optional lse: one launch per step.
 //   lse_combine_kernel  the same merge for partial results of several ranks
 //
 // Fragment bookkeeping (lane = 4*g + t, g = lane/4, t = lane%4):
 //   S = K Q~^T: M = 16 tokens, N = 8 query heads of the GQA group (padded),
-//     K-chunk kk = 2*blk + h covers qs bytes 8h .. 8h+7 of block blk; lane t
-//     supplies the byte pair (8h + 2t, 8h + 2t + 1), the low byte giving the
-//     elements (j, j+16) at k-cols (2t, 2t+1), the high byte at (2t+8, 2t+9).
-//     q~ is permuted identically in the prep kernel.  Each block's two chunks
+//     K-chunk kk = 2*blk + h of a TQ4 block; lane t supplies a byte pair, the
+//     low byte giving the elements (j, j+16) at k-cols (2t, 2t+1), the high byte
+//     at (2t+8, 2t+9): bytes (8h + 2t, 8h + 2t + 1) in even blocks (their codes
+//     start 2 mod 4: two 16-bit loads per token), bytes (4t + 2h, 4t + 2h + 1)
+//     in odd blocks (codes 4-byte aligned: one 32-bit load serves both chunks).
+//     q~ is permuted identically when its fragments are built.  Each block's two chunks
 //     accumulate separately and are scaled by that token's block scale in fp32.
 //   O^T = V^T P: M = 16 rows of one V block per m-tile (mt -> block mt/2),
 //     row r of m-tile mt is element 32*(mt/2) + 2*(r%8) + (mt%2) + 16*(r/8);
@@ -149,55 +153,42 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
     return v;
 }
 
-// ── q preparation ─────────────────────────────────────────────────────────────
-// One CTA (128 threads) per (sequence, KV head): FWHT of the grp query heads
-// (same butterfly order as src/ggml-tq.c:365-374), scale, fp16, fragment layout.
+// ── query rotation and output merge helpers ──────────────────────────────────
 
-template <typename QT>
-__device__ __forceinline__ float load_q(const QT* p);
-template <> __device__ __forceinline__ float load_q<float>(const float* p) { return *p; }
-template <> __device__ __forceinline__ float load_q<__half>(const __half* p) { return __half2float(*p); }
-template <> __device__ __forceinline__ float load_q<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ float load_q(const void* q, int dt, size_t i) {
+    if (dt == DT_F32) return static_cast<const float*>(q)[i];
+    if (dt == DT_F16) return __half2float(static_cast<const __half*>(q)[i]);
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(q)[i]);
+}
 
-template <typename QT, int D, int KT>
-__global__ void __launch_bounds__(128) attn_qprep_kernel(const QT* __restrict__ q, uint32_t* __restrict__ qfrag,
-                                                         int Hq, int Hkv, int grp, float scale, int rotate) {
-    __shared__ float sq[ATT_N][D];
-    const int pair = blockIdx.x;
-    const int b = pair / Hkv, g = pair % Hkv;
-    for (int i = threadIdx.x; i < ATT_N * D; i += 128) {
-        const int h = i / D, e = i % D;
-        sq[h][e] = h < grp ? load_q<QT>(q + ((size_t)b * Hq + (size_t)g * grp + h) * D + e) : 0.0f;
-    }
-    __syncthreads();
-    if (rotate) {
-        for (int hstep = 1; hstep < D; hstep <<= 1) {
-            for (int i = threadIdx.x; i < ATT_N * D / 2; i += 128) {
-                const int h = i / (D / 2), p = i % (D / 2);
-                const int lg = __ffs(hstep) - 1;
-                const int j = ((p >> lg) << (lg + 1)) | (p & (hstep - 1));
-                const float a = sq[h][j], c = sq[h][j + hstep];
-                sq[h][j] = a + c;
-                sq[h][j + hstep] = a - c;
+__device__ __forceinline__ void store_out_rt(void* out, int dt, size_t i, float v) {
+    if (dt == DT_F32) static_cast<float*>(out)[i] = v;
+    else if (dt == DT_F16) static_cast<__half*>(out)[i] = __float2half_rn(v);
+    else static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+}
+
+// In-place FWHT of one row held by a warp, elements lane * EPL .. lane * EPL + EPL - 1 in v:
+// stages h = 1, 2, 4, ... in the order of src/ggml-tq.c:365-374 (x[j] = a + c, x[j + h] = a - c
+// for j with bit h clear), the first log2(EPL) stages in registers, the rest by shuffles.
+template <int EPL>
+__device__ __forceinline__ void fwht_warp_row(float (&v)[EPL], int lane) {
+#pragma unroll
+    for (int h = 1; h < EPL; h <<= 1) {
+#pragma unroll
+        for (int i = 0; i < EPL; ++i)
+            if (!(i & h)) {
+                const float x = v[i], y = v[i + h];
+                v[i] = x + y;
+                v[i + h] = x - y;
             }
-            __syncthreads();
-        }
     }
-    // scale = sm_scale * log2(e) [* 1/sqrt(D) of the FWHT folded in by the caller]
-    constexpr int NCH = D / 16;
-    uint32_t* out = qfrag + (size_t)pair * NCH * 64;
-    for (int i = threadIdx.x; i < NCH * 32; i += 128) {
-        const int kk = i / 32, lane = i % 32;
-        const int gl = lane >> 2, t = lane & 3;
-        const int blk = kk >> 1, h = kk & 1;
-        if (KT == 4) {   // TQ4 byte pairs: k-cols (2t, 2t+1) = elements (j, j+16), (2t+8, 2t+9) = (j+1, j+17)
-            const int e0 = 32 * blk + 8 * h + 2 * t;
-            out[kk * 64 + lane * 2 + 0] = pack_h2(sq[gl][e0] * scale, sq[gl][e0 + 16] * scale);
-            out[kk * 64 + lane * 2 + 1] = pack_h2(sq[gl][e0 + 1] * scale, sq[gl][e0 + 17] * scale);
-        } else {         // TQ3 group t: k-cols (2t, 2t+1) = codes 4h, 4h+1 of group t, (2t+8, 2t+9) = 4h+2, 4h+3
-            const int e0 = 32 * blk + 8 * t + 4 * h;
-            out[kk * 64 + lane * 2 + 0] = pack_h2(sq[gl][e0] * scale, sq[gl][e0 + 1] * scale);
-            out[kk * 64 + lane * 2 + 1] = pack_h2(sq[gl][e0 + 2] * scale, sq[gl][e0 + 3] * scale);
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const bool upper = (lane & d) != 0;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[i], d);
+            v[i] = upper ? o - v[i] : v[i] + o;
         }
     }
 }
@@ -211,18 +202,26 @@ __global__ void __launch_bounds__(128) attn_qprep_kernel(const QT* __restrict__ 
 // (16 tokens each) through its private 4-stage bulk-copy ring.  At the end of a
 // segment the 16 warps merge their (max, sum, O) in shared memory and the CTA
 // writes one partial for (pair, slot), slot = CTA index - first CTA of the pair.
-
+// It then counts itself in the pair's counter; the CTA that brings the count to
+// the number of slots the pair spans reads all of them back from L2 (its
+// predecessors fenced their partials before counting) and writes the output.
 struct AttnKernelArgs {
-    const uint32_t* qfrag;      // [pairs][D/16][32][2]
+    const void* q;              // [B][Hq][D] in q_dtype
     const uint8_t* k;
     const uint8_t* v;
     const int32_t* kv_len;      // [B] or null
     float* part;                // [pairs][slots][ATT_N][D + 2]
     int* err;
+    int* cnt;                   // [pairs] CTAs finished per pair, zero at launch
+    void* out;                  // [B][Hq][D] in out_dtype
+    float* lse;                 // [B][Hq] or null
     int64_t cap;                // token capacity per (sequence, KV head)
     int64_t lnom;               // nominal tokens per pair (multiple of 16, >= every kv_len used)
     int64_t chunk;              // tokens per CTA (multiple of 256)
-    int B, Hkv, slots;
+    float qscale;               // sm_scale * log2(e) [* 1/sqrt(D) of the query FWHT]
+    float onorm;                // 1/sqrt(D) of the output FWHT
+    int B, Hq, Hkv, grp, slots;
+    int q_dtype, out_dtype, rotate_q, v_rotated;
 };
 
 template <int RES>
@@ -241,6 +240,19 @@ template <int OFF>
 __device__ __forceinline__ uint32_t ld32(uint32_t base) {
     uint32_t v;
     asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(base), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ __forceinline__ uint2 ld64u(uint32_t base) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(base), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ __forceinline__ uint4 ld128u(uint32_t base) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4+%5];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(base), "n"(OFF));
     return v;
 }
 template <int OFF>
@@ -305,7 +317,8 @@ struct AttnCfg {
     static constexpr int KTILE = ATT_TILE * KB, VTILE = ATT_TILE * VB;
     static constexpr int STAGE = KTILE + VTILE;
     static constexpr int NCH = D / 16, NMT = D / 16;
-    static constexpr int SCR = ATT_TILE * NBLK * 4 + NBLK * ATT_TILE * 2;   // dK f32 [row][blk] | dV f16 [blk][row]
+    // scale scratch of one tile: dK f32 [row][blk] | dV f16 [t][blk][rows 2t, 2t+1, 2t+8, 2t+9]
+    static constexpr int SCR = ATT_TILE * NBLK * 4 + NBLK * ATT_TILE * 2;
     static constexpr bool INTERLEAVE = D == 128;
     __host__ __device__ static constexpr int tok_of_row(int r) {
         return INTERLEAVE ? (r < 8 ? 2 * r : 2 * (r - 8) + 1) : r;
@@ -373,8 +386,11 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
     // per-lane fixed offsets inside a stage
     constexpr int KROW8 = (Cfg::tok_of_row(8) - Cfg::tok_of_row(0)) * KB;   // row g+8 relative to row g
     const int ktok = Cfg::tok_of_row(gq);
-    // TQ4 K: byte pair (8h + 2t, 8h + 2t + 1) of each block
+    // TQ4 K, even blocks (codes start 2 mod 4): byte pair (8h + 2t, 8h + 2t + 1) for chunk h;
+    // odd blocks (codes start 0 mod 4): the aligned word of bytes 4t .. 4t + 3, chunk h = bytes
+    // (4t + 2h, 4t + 2h + 1)
     const uint32_t k_off = ktok * KB + 2 * tq + 2;
+    const uint32_t k_off_w = ktok * KB + 4 * tq + 2;
     // TQ3 K: group t of each block, read as two aligned words and a funnel shift; blocks
     // start at 14 * blk bytes, which is 0 mod 4 for even and 2 mod 4 for odd blk
     const uint32_t k3_off_e = ktok * KB + ((2 + 3 * tq) & ~3), k3_sh_e = 8 * ((2 + 3 * tq) & 3);
@@ -390,7 +406,11 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
     constexpr int TSTEP = 32 / NBLK, ROWSTEP = Cfg::INTERLEAVE ? TSTEP / 2 : TSTEP, NXH = NBLK / 2;
     const int xt0 = lane / NBLK, xb = lane % NBLK, xrow0 = Cfg::row_of_tok(xt0);
     const uint32_t xks = xt0 * KB + xb * KBB, xkd = (xrow0 * NBLK + xb) * 4;
-    const uint32_t xvs = KTILE + xt0 * VB + xb * TQ4_BYTES, xvd = ATT_TILE * NBLK * 4 + (xb * ATT_TILE + xrow0) * 2;
+    // dV of row r, block b at (((r & 7) >> 1) * NBLK + b) * 8 + ((r & 1) + 2 * (r >> 3)) * 2: lane t then
+    // finds the four P rows of every block in 2 * NBLK consecutive words.  Entry rr adds
+    // rr * ROWSTEP rows to a first row whose low three bits stay below 4, hence VDELTA(rr).
+    const uint32_t xvs = KTILE + xt0 * VB + xb * TQ4_BYTES,
+                   xvd = ATT_TILE * NBLK * 4 + ((((xrow0 & 7) >> 1) * NBLK + xb) * 8 + ((xrow0 & 1) + 2 * (xrow0 >> 3)) * 2);
     uint32_t phase_bits = 0;
 
     const int64_t pairs = (int64_t)a.B * a.Hkv;
@@ -413,15 +433,6 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         const uint8_t* kbase = a.k + (size_t)pair * a.cap * KB;
         const uint8_t* vbase = a.v + (size_t)pair * a.cap * VB;
 
-        uint32_t qf[NCH][2];
-        {
-            const uint32_t* src = a.qfrag + (size_t)pair * NCH * 64;
-#pragma unroll
-            for (int kk = 0; kk < NCH; ++kk) {
-                qf[kk][0] = src[kk * 64 + lane * 2];
-                qf[kk][1] = src[kk * 64 + lane * 2 + 1];
-            }
-        }
         float o[NMT][4];
 #pragma unroll
         for (int mt = 0; mt < NMT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
@@ -452,6 +463,50 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         // other two stages.  Two tiles per step give the scheduler two independent
         // dequantize / mma chains and one softmax update per 32 tokens.
         static_for<0, 2>([&](auto sc) { issue_next(sc); });
+
+        // q~ of this pair while the first tiles are in flight: warp h < 8 loads query head h of
+        // the group (zeros past grp), rotates it and scales it into the (still unused) scale
+        // scratch; every warp then builds its fp16 mma B fragments from there.
+        uint32_t qf[NCH][2];
+        {
+            constexpr int SQS = D + 4;   // row pitch: the fragment reads below are at most 2-way conflicted
+            static_assert(ATT_N * SQS * 4 <= WARPS * 2 * SCR, "q~ must fit the scale scratch");
+            float* sq = reinterpret_cast<float*>(scratch);   // [ATT_N][SQS]
+            if (warp < ATT_N) {
+                constexpr int EPL = D / 32;
+                float qv[EPL];
+                if (warp < a.grp) {
+                    const int64_t b = pair / a.Hkv, g = pair - b * a.Hkv;
+                    const size_t row = ((size_t)b * a.Hq + (size_t)g * a.grp + warp) * D + (size_t)lane * EPL;
+#pragma unroll
+                    for (int i = 0; i < EPL; ++i) qv[i] = load_q(a.q, a.q_dtype, row + i);
+                    if (a.rotate_q) fwht_warp_row<EPL>(qv, lane);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < EPL; ++i) qv[i] = 0.0f;
+                }
+#pragma unroll
+                for (int i = 0; i < EPL; i += 4)
+                    *reinterpret_cast<float4*>(sq + warp * SQS + lane * EPL + i) =
+                        make_float4(qv[i] * a.qscale, qv[i + 1] * a.qscale, qv[i + 2] * a.qscale, qv[i + 3] * a.qscale);
+            }
+            __syncthreads();
+            const float* mq = sq + gq * SQS;
+#pragma unroll
+            for (int kk = 0; kk < NCH; ++kk) {
+                const int blk = kk >> 1, h = kk & 1;
+                if constexpr (KT == 4) {   // k-cols (2t, 2t+1) = elements (j, j+16), (2t+8, 2t+9) = (j+1, j+17)
+                    const int e0 = 32 * blk + ((blk & 1) ? 4 * tq + 2 * h : 8 * h + 2 * tq);
+                    qf[kk][0] = pack_h2(mq[e0], mq[e0 + 16]);
+                    qf[kk][1] = pack_h2(mq[e0 + 1], mq[e0 + 17]);
+                } else {                   // TQ3 group t: codes 4h, 4h+1 | 4h+2, 4h+3 of group t
+                    const int e0 = 32 * blk + 8 * tq + 4 * h;
+                    qf[kk][0] = pack_h2(mq[e0], mq[e0 + 1]);
+                    qf[kk][1] = pack_h2(mq[e0 + 2], mq[e0 + 3]);
+                }
+            }
+            __syncthreads();   // q~ read by all warps before the scale scratch is reused
+        }
         uint32_t bad_scale = 0;   // max |d| bits over the block scales seen
 
         // block-scale extraction of one tile into scratch xs: K -> f32 [row][blk], V -> f16 bits
@@ -473,7 +528,8 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     const float f = __half2float(__ushort_as_half(h));
                     asm volatile("st.shared.f32 [%0], %1;" ::"r"(xs + xkd + rr * ROWSTEP * NBLK * 4), "f"(f));
                 } else {
-                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(xs + xvd + rr * ROWSTEP * 2), "h"(h));
+                    constexpr int VDELTA = (((rr * ROWSTEP) & 7) >> 1) * NBLK * 8 + ((rr * ROWSTEP) >> 3) * 4;
+                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(xs + xvd + VDELTA), "h"(h));
                 }
             });
         };
@@ -492,7 +548,20 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 constexpr int blk = decltype(blk_c)::value;
                 float acc[4];
                 uint32_t af[4];
-                if constexpr (KT == 4) {
+                if constexpr (KT == 4 && (blk & 1)) {
+                    const uint32_t kr = st + k_off_w;
+                    const uint32_t w0 = ld32<blk * TQ4_BYTES>(kr), w1 = ld32<blk * TQ4_BYTES + KROW8>(kr);
+                    af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
+                    af[1] = lut_ld<RES>(w1, lane4, LUT_SEL0);
+                    af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
+                    af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
+                    mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
+                    af[0] = lut_ld<RES>(w0, lane4, LUT_SEL2);
+                    af[1] = lut_ld<RES>(w1, lane4, LUT_SEL2);
+                    af[2] = lut_ld<RES>(w0, lane4, LUT_SEL3);
+                    af[3] = lut_ld<RES>(w1, lane4, LUT_SEL3);
+                    mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
+                } else if constexpr (KT == 4) {
                     const uint32_t kr = st + k_off;
                     uint32_t w0 = ld16<blk * TQ4_BYTES>(kr), w1 = ld16<blk * TQ4_BYTES + KROW8>(kr);
                     af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
@@ -537,7 +606,8 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         // O^T += V^T P' of one tile; pb01 / pb23 are the transposed P fragments
         auto accumulate = [&](uint32_t st, uint32_t xs, uint32_t pb01, uint32_t pb23) {
             const uint32_t vr = st + KTILE + v_off;
-            const uint32_t sdv = xs + ATT_TILE * NBLK * 4 + 4 * tq;
+            const uint32_t sdv = xs + ATT_TILE * NBLK * 4 + tq * NBLK * 8;
+            uint4 dvw;   // dV words of blocks blk, blk + 1: (rows 2t, 2t+1 | rows 2t+8, 2t+9) each
             static_for<0, NBLK>([&](auto blk_c) {
                 constexpr int blk = decltype(blk_c)::value;
                 const uint32_t w0 = ld16<blk * TQ4_BYTES>(vr), w1 = ld16<blk * TQ4_BYTES + VO1>(vr);
@@ -550,8 +620,17 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 const uint32_t ya = (ra4 & 0x0F0F0F0Fu) | (ra8 & 0xF0F0F0F0u);
                 const uint32_t xb = (rb & 0x0F0F0F0Fu) | (rb4 & 0xF0F0F0F0u);
                 const uint32_t yb = (rb4 & 0x0F0F0F0Fu) | (rb8 & 0xF0F0F0F0u);
-                const uint32_t b0 = h2_mul(pb01, ld32<blk * ATT_TILE * 2>(sdv));
-                const uint32_t b1 = h2_mul(pb23, ld32<blk * ATT_TILE * 2 + 16>(sdv));
+                // TQ4 K: one 128-bit load per block pair; TQ3 K (more live offsets) one 64-bit load per block
+                if constexpr (KT == 3) {
+                    const uint2 d2 = ld64u<blk * 8>(sdv);
+                    dvw.x = d2.x;
+                    dvw.y = d2.y;
+                } else if constexpr ((blk & 1) == 0) {
+                    dvw = ld128u<blk * 8>(sdv);
+                }
+                const bool hi = KT == 4 && (blk & 1);
+                const uint32_t b0 = h2_mul(pb01, hi ? dvw.z : dvw.x);
+                const uint32_t b1 = h2_mul(pb23, hi ? dvw.w : dvw.y);
                 uint32_t af[4];
                 af[0] = lut_ld<RES>(xa, lane4, LUT_SEL0);
                 af[1] = lut_ld<RES>(ya, lane4, LUT_SEL0);
@@ -663,74 +742,82 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
             mine[(2 * tq + 1) * (D + 2) + 2 + e0 + 16] = o[mt][3];
         }
         __syncthreads();
-        float* dst = a.part + ((size_t)pair * a.slots + slot) * ATT_N * (D + 2);
+        // per query head: the maximum over the warps, then each warp's weight 2^(m_w - M)
+        float* smax = reinterpret_cast<float*>(scratch);   // [ATT_N] (the scale scratch is free here)
+        float* swt = smax + ATT_N;                          // [ATT_N][WARPS]
+        if (threadIdx.x < ATT_N) {
+            float M = M_FLOOR;
+            for (int w = 0; w < WARPS; ++w) M = fmaxf(M, red[w * ATT_N * (D + 2) + threadIdx.x * (D + 2)]);
+            smax[threadIdx.x] = M;
+        }
+        __syncthreads();
+        if (threadIdx.x < ATT_N * WARPS) {
+            const int h = threadIdx.x / WARPS, w = threadIdx.x % WARPS;
+            swt[threadIdx.x] = ex2(red[w * ATT_N * (D + 2) + h * (D + 2)] - smax[h]);
+        }
+        __syncthreads();
+        const size_t sstride = (size_t)ATT_N * (D + 2);
+        float* dst = a.part + ((size_t)pair * a.slots + slot) * sstride;
         for (int idx = threadIdx.x; idx < ATT_N * (D + 2); idx += THREADS) {
             const int h = idx / (D + 2), c = idx % (D + 2);
-            float M = M_FLOOR;
-            for (int w = 0; w < WARPS; ++w) M = fmaxf(M, red[w * ATT_N * (D + 2) + h * (D + 2)]);
-            float acc = M;
+            float acc = smax[h];
             if (c > 0) {
                 acc = 0.0f;
-                for (int w = 0; w < WARPS; ++w)
-                    acc += ex2(red[w * ATT_N * (D + 2) + h * (D + 2)] - M) * red[w * ATT_N * (D + 2) + idx];
+                for (int w = 0; w < WARPS; ++w) acc += swt[h * WARPS + w] * red[w * ATT_N * (D + 2) + idx];
             }
             dst[idx] = acc;
         }
-        __syncthreads();   // scratch (= stages) free before the next segment's copies
+        // publish the partial, count this CTA in the pair; the stages are free for the next
+        // segment's copies after this barrier
+        __threadfence();
+        __syncthreads();
+        const int64_t c_first = (pair * a.lnom) / a.chunk, c_last = ((pair + 1) * a.lnom - 1) / a.chunk;
+        const int nslot = (int)(c_last - c_first + 1);
+        if (threadIdx.x == 0) s_abort[1] = atomicAdd(a.cnt + pair, 1) == nslot - 1;
+        __syncthreads();
+        if (s_abort[1] && warp < a.grp) {
+            // last CTA of the pair: log-sum-exp merge of the nslot partials of query head
+            // hh = warp, inverse FWHT, cast; lse in natural log
+            __threadfence();
+            constexpr int EPL = D / 32;
+            const float* p0 = a.part + (size_t)pair * a.slots * sstride + warp * (D + 2);
+            float M = M_FLOOR, L = 0.0f;
+            float ov[EPL];
+#pragma unroll
+            for (int i = 0; i < EPL; ++i) ov[i] = 0.0f;
+            for (int s = 0; s < nslot; ++s) M = fmaxf(M, __ldcg(p0 + s * sstride));
+            for (int s = 0; s < nslot; ++s) L += ex2(__ldcg(p0 + s * sstride) - M) * __ldcg(p0 + s * sstride + 1);
+            if (L > 0.0f)
+                for (int s = 0; s < nslot; ++s) {
+                    const float w = ex2(__ldcg(p0 + s * sstride) - M);
+#pragma unroll
+                    for (int i = 0; i < EPL; ++i) ov[i] += w * __ldcg(p0 + s * sstride + 2 + lane * EPL + i);
+                }
+            const bool empty = !(L > 0.0f);
+            if (!empty) {
+#pragma unroll
+                for (int i = 0; i < EPL; ++i) ov[i] /= L;
+            }
+            if (a.v_rotated) {
+                fwht_warp_row<EPL>(ov, lane);
+#pragma unroll
+                for (int i = 0; i < EPL; ++i) ov[i] *= a.onorm;
+            }
+            const int64_t b = pair / a.Hkv, g = pair - b * a.Hkv;
+            const size_t bh = (size_t)b * a.Hq + (size_t)g * a.grp + warp;
+#pragma unroll
+            for (int i = 0; i < EPL; ++i) store_out_rt(a.out, a.out_dtype, bh * D + lane * EPL + i, ov[i]);
+            if (a.lse && lane == 0) a.lse[bh] = empty ? -INFINITY : (M + __log2f(L)) * 0.6931471805599453f;
+        }
     }
 }
 
-// ── split combine + inverse FWHT + cast ──────────────────────────────────────
+// ── output stores, multi-rank log-sum-exp merge ──────────────────────────────
 
 template <typename OT> __device__ __forceinline__ void store_out(OT* p, float v);
 template <> __device__ __forceinline__ void store_out<float>(float* p, float v) { *p = v; }
 template <> __device__ __forceinline__ void store_out<__half>(__half* p, float v) { *p = __float2half_rn(v); }
 template <> __device__ __forceinline__ void store_out<__nv_bfloat16>(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
-
-template <typename OT, int D>
-__global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restrict__ part, OT* __restrict__ out,
-                                                           float* __restrict__ lse, int Hq, int Hkv, int grp,
-                                                           int slots, int64_t lnom, int64_t chunk, int v_rotated,
-                                                           float fwht_norm) {
-    __shared__ float so[D];
-    const int bh = blockIdx.x;             // sequence * Hq + head
-    const int b = bh / Hq, h = bh % Hq;
-    const int g = h / grp, hh = h % grp;
-    const int64_t pair = (int64_t)b * Hkv + g;
-    // the CTAs whose chunks intersect this pair wrote slots 0 .. nslot-1
-    const int64_t c_first = (pair * lnom) / chunk, c_last = ((pair + 1) * lnom - 1) / chunk;
-    const int nslot = (int)(c_last - c_first + 1);
-    const size_t sstride = (size_t)ATT_N * (D + 2);
-    const float* p0 = part + (size_t)pair * slots * sstride + hh * (D + 2);
-    float M = M_FLOOR;
-    for (int s = 0; s < nslot; ++s) M = fmaxf(M, p0[s * sstride]);
-    float L = 0.0f;
-    for (int s = 0; s < nslot; ++s) L += ex2(p0[s * sstride] - M) * p0[s * sstride + 1];
-    const bool empty = !(L > 0.0f);
-    for (int e = threadIdx.x; e < D; e += 128) {
-        float acc = 0.0f;
-        if (!empty) {
-            for (int s = 0; s < nslot; ++s) acc += ex2(p0[s * sstride] - M) * p0[s * sstride + 2 + e];
-            acc /= L;
-        }
-        so[e] = acc;
-    }
-    __syncthreads();
-    if (v_rotated) {
-        for (int hs = 1; hs < D; hs <<= 1) {
-            for (int p = threadIdx.x; p < D / 2; p += 128) {
-                const int lg = __ffs(hs) - 1;
-                const int j = ((p >> lg) << (lg + 1)) | (p & (hs - 1));
-                const float x = so[j], y = so[j + hs];
-                so[j] = x + y;
-                so[j + hs] = x - y;
-            }
-            __syncthreads();
-        }
-    }
-    for (int e = threadIdx.x; e < D; e += 128) store_out<OT>(out + (size_t)bh * D + e, v_rotated ? so[e] * fwht_norm : so[e]);
-    if (lse && threadIdx.x == 0) lse[bh] = empty ? -INFINITY : (M + __log2f(L)) * 0.6931471805599453f;
-}
 
 // log-sum-exp merge of P partial results (natural-log lse), e.g. from several ranks;
 // part p at o + p * o_stride, lse + p * lse_stride
@@ -792,11 +879,12 @@ AttnPlan attn_plan(int B, int Hkv, int D, int64_t cap, int64_t max_len) {
     return p;
 }
 
+// workspace: error word | per-pair CTA counters (cleared together before each launch) | partials
+static size_t attn_counters_end(size_t pairs) { return 256 + pairs * sizeof(int); }
+
 size_t attn_workspace_bytes(int B, int Hkv, int D, const AttnPlan& p) {
     const size_t pairs = (size_t)B * Hkv;
-    size_t bytes = 256;                                           // error word (+ alignment)
-    bytes += pairs * (D / 16) * 64 * sizeof(uint32_t);            // q fragments
-    bytes = (bytes + 255) & ~size_t(255);
+    size_t bytes = (attn_counters_end(pairs) + 255) & ~size_t(255);
     bytes += pairs * p.slots * ATT_N * (D + 2) * sizeof(float);   // split partials
     return bytes;
 }
@@ -814,24 +902,6 @@ static int reserved_smem() {
         init[dev] = true;
     }
     return cached[dev];
-}
-
-template <typename QT, int D>
-static cudaError_t launch_qprep(const void* q, uint32_t* qfrag, int B, int Hq, int Hkv, int grp, float scale,
-                                int rotate, int k_type, cudaStream_t st) {
-    if (k_type == 4)
-        attn_qprep_kernel<QT, D, 4><<<B * Hkv, 128, 0, st>>>((const QT*)q, qfrag, Hq, Hkv, grp, scale, rotate);
-    else
-        attn_qprep_kernel<QT, D, 3><<<B * Hkv, 128, 0, st>>>((const QT*)q, qfrag, Hq, Hkv, grp, scale, rotate);
-    return cudaGetLastError();
-}
-
-template <typename OT, int D>
-static cudaError_t launch_combine(const float* part, void* out, float* lse, int B, int Hq, int Hkv, int grp,
-                                  const AttnPlan& p, int v_rotated, cudaStream_t st) {
-    attn_combine_kernel<OT, D><<<B * Hq, 128, 0, st>>>(part, (OT*)out, lse, Hq, Hkv, grp, p.slots, p.lnom,
-                                                        p.chunk, v_rotated, fwht_norm(D));
-    return cudaGetLastError();
 }
 
 template <int D, int KT, int RES>
@@ -859,44 +929,39 @@ static cudaError_t launch_decode_kt(const AttnKernelArgs& a, int k_type, int gri
 
 template <int D>
 static cudaError_t run_decode(const AttnRun& r, const AttnPlan& p, uint8_t* ws, cudaStream_t st) {
-    int* err = reinterpret_cast<int*>(ws);
-    uint32_t* qfrag = reinterpret_cast<uint32_t*>(ws + 256);
-    size_t off = 256 + (size_t)r.B * r.Hkv * (D / 16) * 64 * sizeof(uint32_t);
-    off = (off + 255) & ~size_t(255);
-    float* part = reinterpret_cast<float*>(ws + off);
-    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), st);
-    if (e != cudaSuccess) return e;
-    // q~ = FWHT(q) / sqrt(D) * sm_scale * log2(e): the FWHT normalisation folds into the scale
-    const float scale = r.sm_scale * LOG2E * (r.rotate_q ? fwht_norm(D) : 1.0f);
-    switch (r.q_dtype) {
-        case DT_F32: e = launch_qprep<float, D>(r.q, qfrag, r.B, r.Hq, r.Hkv, r.grp, scale, r.rotate_q, r.k_type, st); break;
-        case DT_F16: e = launch_qprep<__half, D>(r.q, qfrag, r.B, r.Hq, r.Hkv, r.grp, scale, r.rotate_q, r.k_type, st); break;
-        default: e = launch_qprep<__nv_bfloat16, D>(r.q, qfrag, r.B, r.Hq, r.Hkv, r.grp, scale, r.rotate_q, r.k_type, st); break;
-    }
+    const size_t pairs = (size_t)r.B * r.Hkv;
+    const size_t cnt_end = attn_counters_end(pairs);
+    cudaError_t e = cudaMemsetAsync(ws, 0, cnt_end, st);
     if (e != cudaSuccess) return e;
     AttnKernelArgs a;
-    a.qfrag = qfrag;
+    a.q = r.q;
     a.k = (const uint8_t*)r.k;
     a.v = (const uint8_t*)r.v;
     a.kv_len = r.kv_len;
-    a.part = part;
-    a.err = err;
+    a.part = reinterpret_cast<float*>(ws + ((cnt_end + 255) & ~size_t(255)));
+    a.err = reinterpret_cast<int*>(ws);
+    a.cnt = reinterpret_cast<int*>(ws + 256);
+    a.out = r.out;
+    a.lse = r.lse;
     a.cap = r.cap;
     a.lnom = p.lnom;
     a.chunk = p.chunk;
+    // q~ = FWHT(q) / sqrt(D) * sm_scale * log2(e): the FWHT normalisation folds into the scale
+    a.qscale = r.sm_scale * LOG2E * (r.rotate_q ? fwht_norm(D) : 1.0f);
+    a.onorm = fwht_norm(D);
     a.B = r.B;
+    a.Hq = r.Hq;
     a.Hkv = r.Hkv;
+    a.grp = r.grp;
     a.slots = p.slots;
+    a.q_dtype = r.q_dtype;
+    a.out_dtype = r.out_dtype;
+    a.rotate_q = r.rotate_q;
+    a.v_rotated = r.v_rotated;
     const int res = reserved_smem();
-    if (res == 0) e = launch_decode_kt<D, 0>(a, r.k_type, p.grid, st);
-    else if (res == 1024) e = launch_decode_kt<D, 1024>(a, r.k_type, p.grid, st);
-    else return cudaErrorNotSupported;
-    if (e != cudaSuccess) return e;
-    switch (r.out_dtype) {
-        case DT_F32: return launch_combine<float, D>(part, r.out, r.lse, r.B, r.Hq, r.Hkv, r.grp, p, r.v_rotated, st);
-        case DT_F16: return launch_combine<__half, D>(part, r.out, r.lse, r.B, r.Hq, r.Hkv, r.grp, p, r.v_rotated, st);
-        default: return launch_combine<__nv_bfloat16, D>(part, r.out, r.lse, r.B, r.Hq, r.Hkv, r.grp, p, r.v_rotated, st);
-    }
+    if (res == 0) return launch_decode_kt<D, 0>(a, r.k_type, p.grid, st);
+    if (res == 1024) return launch_decode_kt<D, 1024>(a, r.k_type, p.grid, st);
+    return cudaErrorNotSupported;
 }
 
 cudaError_t launch_decode_attention(const AttnRun& r, const AttnPlan& p, void* workspace, cudaStream_t st) {

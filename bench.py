@@ -194,14 +194,18 @@ class Codec:
         if name == "tq3opt":
             self.x = c2_input(2 + 1000 * rank, tokens=tokens or 32768)
             self.qtype, self.hd, self.passes = 3, 128, 2
+            self.limiter = ("instruction issue of the float64 coordinate descent (two passes x 32 elements x two "
+                            "neighbours per block); DRAM is about 6 % busy, so the HBM fraction is not the bound")
             self.config = {"workload": "TQ3_0 optimal-rounding quantize (2 CD passes + LS scale), FWHT fused",
                            "input": "bf16 [32768 tokens, 8 KV heads, 128], Student-t(4) x log-normal channel scales",
                            "blocks_per_step": self.x.numel() // 32}
         else:
             self.x = c1_input(1 + 1000 * rank, tokens=tokens or 4096)
             self.qtype, self.hd, self.passes = 4, 128, 0
-            self.config = {"workload": "TQ4_0 quantize, FWHT fused (fp32 [4096, 8, 128], N(0,1) + 4 outlier ch x20)",
+            self.config = {"workload": "C1 TQ4_0 quantize (FWHT fused) + dequantize round trip",
+                           "input": "fp32 [4096 tokens, 8 KV heads, 128], N(0,1) + 4 outlier channels per head x20",
                            "blocks_per_step": self.x.numel() // 32}
+        self.round_trip = self.qtype == 4
         self.k = self.x.numel()
         bb = 14 if self.qtype == 3 else 18
         self.y = torch.empty(self.k // 32 * bb, dtype=torch.uint8, device="cuda")
@@ -209,24 +213,47 @@ class Codec:
         self.ops = ops
         self.launches_per_step = 1
         self.dtype = "bf16->u8 (fp32/fp64 math)" if self.passes else "f32->u8"
+        if self.round_trip:
+            # dequantize back to fp32 (rotated domain, as dequantize_row_tq4_0 returns it)
+            self.xr = torch.empty_like(self.x)
+            self.bytes_per_step *= 2
+            self.launches_per_step = 2
+            self.dtype = "f32->u8->f32"
+            self.step()
+            rot = self.x.clone()
+            ops.hadamard_(rot, self.hd)
+            err = (self.xr - rot).double()
+            mse = float(err.pow(2).mean())
+            self.config["reconstruction_mse"] = round(mse, 8)
+            self.config["relative_mse"] = round(mse / float(rot.double().pow(2).mean()), 8)
 
     def step(self):
         self.ops.quantize(self.x, self.qtype, fwht_head_dim=self.hd, opt_passes=self.passes, out=self.y)
+        if self.round_trip:
+            self.ops.dequantize(self.y, self.qtype, out=self.xr)
 
     # end-to-end through the C ABI with pinned host buffers
     def e2e_setup(self):
         import torch
         self.hx = self.x.cpu().pin_memory()
         self.hy = torch.empty(self.y.numel(), dtype=torch.uint8).pin_memory()
+        if self.round_trip:
+            self.hxr = torch.empty_like(self.hx).pin_memory()
 
     def e2e_step(self):
         from leankv_b200 import _lib as L
         dt = {2: L.DTYPE_BF16, 4: L.DTYPE_F32}[self.x.element_size()]
         L.check(L.load().tq_quantize_host(self.qtype, C.c_void_p(self.hx.data_ptr()), dt,
                                           C.c_void_p(self.hy.data_ptr()), self.k, self.hd, self.passes))
+        if self.round_trip:
+            L.check(L.load().tq_dequantize_host(self.qtype, C.c_void_p(self.hy.data_ptr()),
+                                                C.c_void_p(self.hxr.data_ptr()), L.DTYPE_F32, self.k))
 
     def e2e_bytes(self):
-        return self.hx.numel() * self.hx.element_size(), self.hy.numel()
+        h2d, d2h = self.hx.numel() * self.hx.element_size(), self.hy.numel()
+        if self.round_trip:
+            h2d, d2h = h2d + self.hy.numel(), d2h + self.hxr.numel() * 4
+        return h2d, d2h
 
     # CPU baseline on a bounded sample of the same workload
     def cpu_run(self, frac_tokens: int, nthreads: int, impl: str):
@@ -239,7 +266,9 @@ class Codec:
         else:
             arr = xs.cpu().numpy()
         t0 = time.perf_counter()
-        O.parallel_quantize(arr, self.qtype, self.hd, nthreads, impl=impl, opt_passes=self.passes)
+        blocks = O.parallel_quantize(arr, self.qtype, self.hd, nthreads, impl=impl, opt_passes=self.passes)
+        if self.round_trip:
+            O.parallel_dequantize(blocks, self.qtype, arr.shape[1], nthreads)
         dt = time.perf_counter() - t0
         sample_bytes = self.bytes_per_step / frac_tokens
         return sample_bytes / dt / 1e9, tokens
@@ -574,7 +603,8 @@ def run_ours(args, ws, rank, local):
                        "kind": "port" if wl.passes else "reference",
                        "sample": f"{tokens} of {wl.x.shape[0]} tokens (1/16 of the workload), {n} threads; "
                                  + ("C restatement of scripts/tq3_rounding.py + reference hadamard_transform_row"
-                                    if wl.passes else "reference src/ggml-tq.c hadamard_transform_row + quantize_row")}
+                                    if wl.passes else "reference src/ggml-tq.c hadamard_transform_row + quantize_row"
+                                    + (" + dequantize_row" if getattr(wl, "round_trip", False) else ""))}
         is_codec = isinstance(wl, Codec)
         out = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
@@ -589,9 +619,11 @@ def run_ours(args, ws, rank, local):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "traffic": profile_traffic(args.workload),
-                         "algorithmic_bytes_per_launch": int(rank_bytes) if is_codec else None,
+                         "algorithmic_bytes_per_launch": int(rank_bytes / wl.launches_per_step) if is_codec else None,
                          "algorithmic_bytes_per_step_per_rank": int(rank_bytes),
-                         "timed": "the kernel" if is_codec else "the whole step on the launching stream"},
+                         "timed": ("the quantize and dequantize kernels" if getattr(wl, "round_trip", False) else "the kernel")
+                                  if is_codec else "the whole step on the launching stream",
+                         **({"limiter": wl.limiter} if getattr(wl, "limiter", None) else {})},
             "e2e": e2e,
             "gpu_launches": args.steps * wl.launches_per_step,
             "clocks": clk.summary(),
@@ -634,9 +666,11 @@ def run_reference(args, ws, rank):
     else:
         tokens = 4096
         arr = torch.randn(tokens, 8 * 128).numpy()
-        bytes_ = arr.size * 4 + arr.size // 32 * 18
-        fn = lambda: O.parallel_quantize(arr, 4, 128, n, impl="reference")  # noqa: E731
-        kind, sample = "reference", "full [4096, 8, 128] per step; src/ggml-tq.c hadamard_transform_row + quantize_row_tq4_0"
+        bytes_ = 2 * (arr.size * 4 + arr.size // 32 * 18)
+        fn = lambda: O.parallel_dequantize(O.parallel_quantize(arr, 4, 128, n, impl="reference"),  # noqa: E731
+                                           4, arr.shape[1], n)
+        kind, sample = "reference", ("full [4096, 8, 128] per step; src/ggml-tq.c hadamard_transform_row + "
+                                     "quantize_row_tq4_0 + dequantize_row_tq4_0")
     for _ in range(args.warmup):
         fn()
     t0 = time.perf_counter()
@@ -647,7 +681,7 @@ def run_reference(args, ws, rank):
     return {"metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None,
-            "dtype": {"tq3opt": "bf16->u8", "tq4": "f32->u8", "attn": "f64"}[args.workload],
+            "dtype": {"tq3opt": "bf16->u8", "tq4": "f32->u8->f32", "attn": "f64"}[args.workload],
             "data": "synthetic (seeded)", "impl": "reference",
             "config": {"workload": args.workload, "parallelism": "host threads"},
             "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": n, "kind": kind, "sample": sample},

@@ -132,12 +132,23 @@ def dist_setup():
     if ws > 1:
         import datetime
         import torch.distributed as dist
-        # rank 0 prints exactly one JSON line on stdout: keep NCCL's version banner off it
-        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
-            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        # rank 0 prints exactly one JSON line on stdout; NCCL prints its version banner with
+        # printf (NCCL_DEBUG=WARN or VERSION) when the communicator is created, so fd 1 points at
+        # stderr until the first collective has run (C stdio flushed before it is restored)
+        libc = C.CDLL(None)
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
+        finally:
+            libc.fflush(None)
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return ws, rank, local

@@ -521,7 +521,7 @@ __device__ __forceinline__ void decode_block(const uint8_t* __restrict__ blk, fl
 // ── quantize ────────────────────────────────────────────────────────────────
 // MODE 0: nearest level (reference).  MODE 1: TQ3 optimal rounding.
 template <int QT, typename IN, int MODE, int L2>
-__global__ void __launch_bounds__(CODEC_THREADS, 4)
+__global__ void __launch_bounds__(CODEC_THREADS, (MODE == 0 && sizeof(IN) == 4) ? 3 : 4)
 quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nblocks,
                 int log2_hd, float norm, int n_passes, int x_vec, int y_vec, const RowMap map,
                 uint32_t rseed, int rhpr) {
@@ -635,8 +635,11 @@ fwht_kernel(float* __restrict__ x, int64_t nblocks, int log2_hd, float norm, int
 }
 
 // ── dequantize ──────────────────────────────────────────────────────────────
-// 8 lanes per block, each producing 4 consecutive outputs (one 16-byte store
-// for fp32), so a warp writes 4 whole blocks = 512 contiguous bytes.
+// 4 lanes per block, 8 outputs each.  fp16 / bf16: lane p writes elements
+// 8p .. 8p+7 (one 16-byte store, the 4 lanes of a block 64 contiguous bytes).
+// fp32: lane p writes elements 4p .. 4p+3 and 16+4p .. 16+4p+3 (two 16-byte
+// stores, each covering whole 32-byte sectors across the 4 lanes; for TQ4 these
+// are the low and high nibbles of qs bytes 4p .. 4p+3).
 constexpr int DQ_THREADS = 256;
 constexpr int DQ_TILE = 256;   // blocks per tile
 
@@ -645,24 +648,27 @@ template <> __device__ __forceinline__ float from_float<float>(float f) { return
 template <> __device__ __forceinline__ __half from_float<__half>(float f) { return __float2half_rn(f); }
 template <> __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float f) { return __float2bfloat16_rn(f); }
 
+__device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+// eight consecutive outputs at a 16-byte aligned address
 template <typename OUT>
-__device__ __forceinline__ void store4(OUT* dst, float a, float b, float c, float d);
-template <> __device__ __forceinline__ void store4<float>(float* dst, float a, float b, float c, float d) {
-    *reinterpret_cast<float4*>(dst) = make_float4(a, b, c, d);
+__device__ __forceinline__ void store8(OUT* dst, const float (&o)[8]) {
+    if constexpr (sizeof(OUT) == 4) {
+        reinterpret_cast<float4*>(dst)[0] = make_float4(o[0], o[1], o[2], o[3]);
+        reinterpret_cast<float4*>(dst)[1] = make_float4(o[4], o[5], o[6], o[7]);
+    } else {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pack2(o[0], o[1], dst), pack2(o[2], o[3], dst),
+                                                    pack2(o[4], o[5], dst), pack2(o[6], o[7], dst));
+    }
 }
-template <> __device__ __forceinline__ void store4<__half>(__half* dst, float a, float b, float c, float d) {
-    const __half2 lo = __floats2half2_rn(a, b), hi = __floats2half2_rn(c, d);
-    uint2 u;
-    u.x = *reinterpret_cast<const uint32_t*>(&lo);
-    u.y = *reinterpret_cast<const uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(dst) = u;
-}
-template <> __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* dst, float a, float b, float c, float d) {
-    const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
-    uint2 u;
-    u.x = *reinterpret_cast<const uint32_t*>(&lo);
-    u.y = *reinterpret_cast<const uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(dst) = u;
+__device__ __forceinline__ uint32_t lds_u16_at(const uint8_t* p) {   // 2-byte aligned shared read
+    return *reinterpret_cast<const uint16_t*>(p);
 }
 
 template <int QT, typename OUT>
@@ -688,37 +694,85 @@ dequantize_kernel(const uint8_t* __restrict__ xq, OUT* __restrict__ y, int64_t n
             for (int b = threadIdx.x; b < nbytes; b += DQ_THREADS) s_in[b] = src[b];
         }
         __syncthreads();
-        const int part = threadIdx.x & 7;
-        for (int r = threadIdx.x >> 3; r < nrows; r += DQ_THREADS / 8) {
+        const int part = threadIdx.x & 3;
+        constexpr bool SPLIT = sizeof(OUT) == 4;   // outputs 4p..4p+3 | 16+4p..16+4p+3, else 8p..8p+7
+        for (int r = threadIdx.x >> 2; r < nrows; r += DQ_THREADS / 4) {
             const uint8_t* blk = s_in + r * BB;
-            const float d = half_decode((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
-            uint32_t c0, c1, c2, c3;
+            const float d = half_decode(lds_u16_at(blk));
+            uint32_t c[8];
             if constexpr (QT == 4) {
-                // elements 4p..4p+3: low nibbles of bytes 4p.. (p < 4) or high nibbles of 4(p-4)..
-                const int q = 2 + 4 * (part & 3);
-                const uint32_t w = (uint32_t)blk[q] | ((uint32_t)blk[q + 1] << 8) |
-                                   ((uint32_t)blk[q + 2] << 16) | ((uint32_t)blk[q + 3] << 24);
-                const uint32_t nib = part < 4 ? (w & 0x0F0F0F0Fu) : ((w >> 4) & 0x0F0F0F0Fu);
-                c0 = nib & 15u; c1 = (nib >> 8) & 15u; c2 = (nib >> 16) & 15u; c3 = nib >> 24;
+                if constexpr (SPLIT) {
+                    // low and high nibbles of qs bytes 4p .. 4p+3
+                    const uint8_t* q = blk + 2 + 4 * part;
+                    const uint32_t w = lds_u16_at(q) | (lds_u16_at(q + 2) << 16);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        c[i] = (w >> (8 * i)) & 15u;
+                        c[4 + i] = (w >> (8 * i + 4)) & 15u;
+                    }
+                } else {
+                    // low nibbles of qs bytes 8p .. 8p+7 (p < 2), high nibbles of bytes 8(p-2) .. (p >= 2)
+                    const uint8_t* q = blk + 2 + 8 * (part & 1);
+                    const uint32_t sh = part < 2 ? 0u : 4u;
+                    const uint32_t n0 = ((lds_u16_at(q) | (lds_u16_at(q + 2) << 16)) >> sh) & 0x0F0F0F0Fu;
+                    const uint32_t n1 = ((lds_u16_at(q + 4) | (lds_u16_at(q + 6) << 16)) >> sh) & 0x0F0F0F0Fu;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        c[i] = (n0 >> (8 * i)) & 0xFFu;
+                        c[4 + i] = (n1 >> (8 * i)) & 0xFFu;
+                    }
+                }
             } else if constexpr (QT == 2) {
-                // elements 4p..4p+3 = the four 2-bit codes of byte p
-                const uint32_t b = blk[2 + part];
-                c0 = b & 3u; c1 = (b >> 2) & 3u; c2 = (b >> 4) & 3u; c3 = b >> 6;
+                // qs byte i holds codes 4i .. 4i+3
+                const uint32_t b = SPLIT ? ((uint32_t)blk[2 + part] | ((uint32_t)blk[6 + part] << 8))
+                                         : lds_u16_at(blk + 2 + 2 * part);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) c[i] = (b >> (2 * i)) & 3u;
             } else {
-                // group g = part/2 (3 bytes, 8 codes), half = part%2 -> codes 4*half..+3
-                const int q = 2 + 3 * (part >> 1);
-                const uint32_t w = (uint32_t)blk[q] | ((uint32_t)blk[q + 1] << 8) | ((uint32_t)blk[q + 2] << 16);
-                const uint32_t s = w >> (12 * (part & 1));
-                c0 = s & 7u; c1 = (s >> 3) & 7u; c2 = (s >> 6) & 7u; c3 = (s >> 9) & 7u;
+                // group g (3 bytes) holds codes 8g .. 8g+7
+                auto group = [&](int g) {
+                    const uint8_t* q = blk + 2 + 3 * g;
+                    return (uint32_t)q[0] | ((uint32_t)q[1] << 8) | ((uint32_t)q[2] << 16);
+                };
+                if constexpr (SPLIT) {
+                    const uint32_t w0 = group(part >> 1) >> (12 * (part & 1));
+                    const uint32_t w1 = group(2 + (part >> 1)) >> (12 * (part & 1));
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        c[i] = (w0 >> (3 * i)) & 7u;
+                        c[4 + i] = (w1 >> (3 * i)) & 7u;
+                    }
+                } else {
+                    const uint32_t w = group(part);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) c[i] = (w >> (3 * i)) & 7u;
+                }
             }
-            const float o0 = __fmul_rn(s_lvl[c0], d), o1 = __fmul_rn(s_lvl[c1], d);
-            const float o2 = __fmul_rn(s_lvl[c2], d), o3 = __fmul_rn(s_lvl[c3], d);
-            OUT* dst = y + (b0 + r) * QK + 4 * part;
-            if (y_vec) {
-                store4<OUT>(dst, o0, o1, o2, o3);
+            float o[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(s_lvl[c[i]], d);
+            OUT* row = y + (b0 + r) * QK;
+            if constexpr (SPLIT) {
+                float* dst0 = reinterpret_cast<float*>(row) + 4 * part;
+                float* dst1 = dst0 + 16;
+                if (y_vec) {
+                    *reinterpret_cast<float4*>(dst0) = make_float4(o[0], o[1], o[2], o[3]);
+                    *reinterpret_cast<float4*>(dst1) = make_float4(o[4], o[5], o[6], o[7]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        dst0[i] = o[i];
+                        dst1[i] = o[4 + i];
+                    }
+                }
             } else {
-                dst[0] = from_float<OUT>(o0); dst[1] = from_float<OUT>(o1);
-                dst[2] = from_float<OUT>(o2); dst[3] = from_float<OUT>(o3);
+                OUT* dst = row + 8 * part;
+                if (y_vec) {
+                    store8<OUT>(dst, o);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) dst[i] = from_float<OUT>(o[i]);
+                }
             }
         }
     }
@@ -876,8 +930,7 @@ template <int QT, typename OUT>
 static cudaError_t launch_dq_t(const void* x, void* y, int64_t nblocks, cudaStream_t st) {
     const int64_t ntiles = (nblocks + DQ_TILE - 1) / DQ_TILE;
     dequantize_kernel<QT, OUT><<<codec_grid(ntiles, 8), DQ_THREADS, 0, st>>>(
-        (const uint8_t*)x, (OUT*)y, nblocks, ((uintptr_t)x & 15) == 0,
-        ((uintptr_t)y & (sizeof(OUT) == 4 ? 15 : 7)) == 0);
+        (const uint8_t*)x, (OUT*)y, nblocks, ((uintptr_t)x & 15) == 0, ((uintptr_t)y & 15) == 0);
     return cudaGetLastError();
 }
 

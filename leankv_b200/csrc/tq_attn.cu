@@ -64,10 +64,6 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
 }
 
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -85,13 +81,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
-}
-
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar)
-        : "memory");
 }
 
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -133,25 +122,12 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 // Codebook table: entry for byte k (lo nibble n0, hi nibble n1) is half2(L[n0], L[n1]),
 // replicated so that lane l always reads bank l: address = (k << 8) | (lane << 2).
 // The TQ3 table (6-bit index, codes c0 | c1 << 3) sits at offset 128 in rows 0..63.
-__device__ __forceinline__ uint32_t lut_addr(uint32_t word, uint32_t lane4, uint32_t sel) {
-    return prmt(word, lane4, sel);
-}
-// selectors putting byte k of `word` at bits 8..15 and lane4 at bits 0..7
+// prmt(word, lane4, LUT_SELk) is that address for byte k of `word`: byte k at bits 8..15,
+// lane4 at bits 0..7.
 #define LUT_SEL0 0x5504u
 #define LUT_SEL1 0x5514u
 #define LUT_SEL2 0x5524u
 #define LUT_SEL3 0x5534u
-
-__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
-__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
-    uint16_t v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
-    return v;
-}
 
 // ── query rotation and output merge helpers ──────────────────────────────────
 

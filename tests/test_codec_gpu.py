@@ -148,6 +148,26 @@ def test_dequantize_low_precision_outputs(orc, t, dtype):
     assert torch.equal(y.cpu().view(torch.int16), ref.view(torch.int16))
 
 
+@pytest.mark.parametrize("t", [2, 3, 4])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("nblocks", [1, 255, 257, 1001])
+def test_dequantize_every_output_layout(orc, t, dtype, nblocks):
+    """Random block bytes (finite scales), every output dtype, 16-byte aligned and unaligned
+    outputs (the vector and the scalar store paths), ragged tile counts."""
+    rng = np.random.default_rng(100 * t + nblocks)
+    bb = L.BLOCK_BYTES[t]
+    q = rng.integers(0, 256, size=(nblocks, bb), dtype=np.uint8)
+    q[:, 1] &= 0xBB                                   # exponent <= 14: every product finite in fp16
+    ref32 = orc.ref_dequantize(t, q) if t == 2 else orc.dequantize(t, q)
+    ref = torch.from_numpy(ref32).to(dtype)
+    view = torch.int32 if dtype == torch.float32 else torch.int16
+    y = ops.dequantize(gpu(q), t, dtype=dtype)
+    assert torch.equal(y.cpu().view(view), ref.view(view))
+    out = torch.zeros(nblocks * 32 + 1, dtype=dtype, device=DEV)
+    ops.dequantize(gpu(q), t, out=out[1:])
+    assert torch.equal(out[1:].cpu().view(view), ref.view(view))
+
+
 @pytest.mark.parametrize("nblocks", [1, 3, 127, 128, 129, 4097, 300001])
 def test_ragged_block_counts(orc, nblocks):
     rng = np.random.default_rng(nblocks)

@@ -132,7 +132,7 @@ extern "C" tq_status tq_decode_attention_static_cuda(const tq_decode_attention_a
                          need, (size_t)TQ_STATIC_SCRATCH_BYTES);
     void* ws = nullptr;
     if ((s = static_scratch(&ws))) return s;
-    // the error word is cleared and every partial / q fragment is written before it is read,
-    // so the previous call's contents never leak into this one
+    // the launch clears the error word and the per-pair counters, and every partial is written
+    // before it is read, so the previous call's contents never leak into this one
     return cuda_status(launch_decode_attention(r, p, ws, (cudaStream_t)stream), "decode attention launch");
 }

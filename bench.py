@@ -172,6 +172,20 @@ def max_over_ranks(x: float, ws: int) -> float:
 
 # ── workloads ──────────────────────────────────────────────────────────────────
 
+# Workload names as both arms report them (the reference arm uses the same strings).
+WORKLOAD = {
+    "tq3opt": "TQ3_0 optimal-rounding quantize (2 CD passes + LS scale), FWHT fused",
+    "tq4": "C1 TQ4_0 quantize (FWHT fused) + dequantize round trip",
+    "attn": "C3 fused TQ4_0/TQ4_0 decode attention (FWHT(q), split-KV, LSE combine, FWHT(o))",
+    "c4": "C4 fused TQ3_0-K / TQ4_0-V decode attention, split-KV by sequence",
+    "c5": "C5 streaming append + decode, 80-layer TQ4_0 KV cache, one CUDA graph per step",
+}
+INPUT = {
+    "tq3opt": "bf16 [32768 tokens, 8 KV heads, 128], Student-t(4) x log-normal channel scales",
+    "tq4": "fp32 [4096 tokens, 8 KV heads, 128], N(0,1) + 4 outlier channels per head x20",
+}
+
+
 def c2_input(seed: int, tokens=32768, heads=8, hd=128):
     import torch
     g = torch.Generator(device="cuda").manual_seed(seed)
@@ -207,14 +221,12 @@ class Codec:
             self.qtype, self.hd, self.passes = 3, 128, 2
             self.limiter = ("instruction issue of the float64 coordinate descent (two passes x 32 elements x two "
                             "neighbours per block); DRAM is about 6 % busy, so the HBM fraction is not the bound")
-            self.config = {"workload": "TQ3_0 optimal-rounding quantize (2 CD passes + LS scale), FWHT fused",
-                           "input": "bf16 [32768 tokens, 8 KV heads, 128], Student-t(4) x log-normal channel scales",
+            self.config = {"workload": WORKLOAD["tq3opt"], "input": INPUT["tq3opt"],
                            "blocks_per_step": self.x.numel() // 32}
         else:
             self.x = c1_input(1 + 1000 * rank, tokens=tokens or 4096)
             self.qtype, self.hd, self.passes = 4, 128, 0
-            self.config = {"workload": "C1 TQ4_0 quantize (FWHT fused) + dequantize round trip",
-                           "input": "fp32 [4096 tokens, 8 KV heads, 128], N(0,1) + 4 outlier channels per head x20",
+            self.config = {"workload": WORKLOAD["tq4"], "input": INPUT["tq4"],
                            "blocks_per_step": self.x.numel() // 32}
         self.round_trip = self.qtype == 4
         self.k = self.x.numel()
@@ -347,11 +359,11 @@ class Attn:
         self.flush_l2 = False
         self.l2_note = f"KV {kv_total / 1e9:.2f} GB per step (> L2 126 MB), no flush"
         if name == "attn":
-            self.config = {"workload": "C3 fused TQ4_0/TQ4_0 decode attention (FWHT(q), split-KV, LSE combine, FWHT(o))",
+            self.config = {"workload": WORKLOAD["attn"],
                            "shape": f"B={B} Hq={Hq} Hkv={Hkv} D={D} ctx={T}, fp16 q/out", "kv_bytes": kv_total}
             self.parallelism = f"batch shards x{ws} (sequences {b0}..{b1 - 1} on rank {rank}), no collective"
         else:
-            self.config = {"workload": "C4 fused TQ3_0-K / TQ4_0-V decode attention, split-KV by sequence",
+            self.config = {"workload": WORKLOAD["c4"],
                            "shape": f"B={B} Hq={Hq} Hkv={Hkv} D={D} ctx={T}, fp16 q/out", "kv_bytes": kv_total}
             self.parallelism = (f"token shards x{ws} ({L} tokens per rank); all_gather of packed (O, lse) over NCCL "
                                 "+ LSE merge on every rank" if ws > 1 else "one GPU holds the whole context")
@@ -459,7 +471,7 @@ class Stream:
         self.scaling = "strong"
         self.flush_l2 = False
         self.l2_note = "cache > 10 GB per rank (> L2 126 MB), no flush"
-        self.config = {"workload": "C5 streaming append + decode, 80-layer TQ4_0 KV cache, one CUDA graph per step",
+        self.config = {"workload": WORKLOAD["c5"],
                        "shape": f"batch {self.BATCH} (x{ws} ranks: {B} each) Hkv={H} Hq={Hq} D={D} prefill {T0} "
                                 f"+ up to {self.GROWTH} appended tokens, bf16 inputs/outputs",
                        "layers": self.nl, "prefill": self.prefill}
@@ -644,44 +656,75 @@ def run_ours(args, ws, rank, local):
     return out
 
 
+def _ref_cache(rng, O, qtype, hkv, ctx, d):
+    """K or V of one sequence as the reference C writes it: N(0,1) with 4 outlier channels x20,
+    hadamard_transform_row over head_dim, quantize_row_tq*_0; [1, hkv, ctx, d/32, block bytes]."""
+    import numpy as np
+    x = rng.standard_normal((hkv, ctx, d), dtype=np.float32)
+    for h in range(hkv):
+        x[h, :, rng.permutation(d)[:4]] *= 20.0
+    bb = O.BLOCK_BYTES[qtype]
+    return O.ref_quantize(qtype, O.ref_fwht(x, d)).reshape(1, hkv, ctx, d // 32, bb)
+
+
 def run_reference(args, ws, rank):
-    """The reference's CPU implementation of the path on this host's cores."""
+    """The reference's CPU implementation of the path on this host's cores, on a bounded sample of
+    the same workload (same config, metric and unit as this repository's arm; inputs made on the
+    host by the reference C, nothing of this repository's GPU path involved)."""
     if rank != 0:
         return None
+    import numpy as np
     import torch
     from oracle import oracle as O
     n = os.cpu_count() or 1
     torch.manual_seed(0)
-    if args.workload == "attn":
-        import numpy as np
-        Hq, Hkv, D, T = 32, 8, 128, 32768
-        rng = np.random.default_rng(3)
-        x = rng.standard_normal((2, Hkv, T, D), dtype=np.float32)
-        x[:, :, :, :4] *= 20.0
-        blocks = O.ref_quantize(4, O.ref_fwht(x, D)).reshape(2, 1, Hkv, T, D // 32, 18)
-        kc, vc = blocks[0], blocks[1]
+    rng = np.random.default_rng(3)
+    wl = args.workload
+    config = {"workload": WORKLOAD[wl]}
+    scaling = "weak" if wl in ("tq3opt", "tq4") else "strong"
+    note_att = ("float64 restatement (reference dequantize_row_tq*_0 + hadamard_transform + exact softmax); "
+                "no reference CPU attention exists in-tree")
+    if wl in ("attn", "c4", "c5"):
+        # one sequence (of one layer for C5), context shortened for C4 to keep a step bounded
+        Hq, Hkv, D, T, kt, seqs = {"attn": (32, 8, 128, 32768, 4, 16), "c4": (64, 8, 128, 131072 // 8, 3, 64),
+                                   "c5": (32, 8, 256, 16384, 4, 32)}[wl]
+        kc, vc = _ref_cache(rng, O, kt, Hkv, T, D), _ref_cache(rng, O, 4, Hkv, T, D)
         q = rng.standard_normal((1, Hq, D), dtype=np.float32)
-        bytes_ = kc.size + vc.size + q.size * 4
-        fn = lambda: O.decode_attention(q, kc, 4, vc, 4, Hkv, nthreads=n)  # noqa: E731
-        kind, sample = "port", ("1 of the 16 sequences of B16 Hq32 Hkv8 D128 ctx 32768 per step; float64 restatement "
-                                "(reference dequantize_row_tq4_0 + hadamard_transform + exact softmax), no reference "
-                                "CPU attention exists in-tree")
-    elif args.workload == "tq3opt":
+        bytes_ = kc.size + vc.size + (q.size * 2 * 2 if wl != "c5" else 0)
+        fn = lambda: O.decode_attention(q, kc, kt, vc, 4, Hkv, nthreads=n)  # noqa: E731
+        config["shape"] = {"attn": "B=16 Hq=32 Hkv=8 D=128 ctx=32768, fp16 q/out",
+                           "c4": "B=64 Hq=64 Hkv=8 D=128 ctx=131072, fp16 q/out",
+                           "c5": "batch 32 (x1 ranks: 32 each) Hkv=8 Hq=32 D=256 prefill 16384 + up to 256 "
+                                 "appended tokens, bf16 inputs/outputs"}[wl]
+        sample = {"attn": "1 of the 16 sequences per step; ",
+                  "c4": "1 of the 64 sequences at 1/8 of the context per step; ",
+                  "c5": "1 layer x 1 sequence of the decode step at context 16384, GB/s of cache read; "}[wl] + note_att
+        kind = "port"
+    elif wl == "tq3opt":
         tokens = 32768 // 16
-        x = torch.randn(tokens, 8 * 128) * torch.exp(torch.randn(1, 8 * 128))
-        arr = x.to(torch.bfloat16).view(torch.int16).numpy().view("uint16")
+        # the workload's generator on the host: Student-t(4) = N / sqrt(chi2_4 / 4), log-normal channel scales
+        nrm = torch.randn(tokens, 8, 128)
+        chi = sum(torch.randn(tokens, 8, 128) ** 2 for _ in range(4))
+        x = (nrm / torch.sqrt(chi / 4.0)) * torch.exp(torch.randn(1, 8, 128))
+        arr = x.reshape(tokens, -1).to(torch.bfloat16).view(torch.int16).numpy().view("uint16")
         bytes_ = arr.size * 2 + arr.size // 32 * 14
         fn = lambda: O.parallel_quantize(arr, 3, 128, n, impl="port", opt_passes=2)  # noqa: E731
-        kind, sample = "port", f"{tokens} of 32768 tokens per step (bf16 [.., 8, 128]); C restatement of " \
-                               "scripts/tq3_rounding.py (no reference C exists) + reference hadamard_transform_row"
+        config["input"] = INPUT[wl]
+        kind, sample = "port", (f"{tokens} of 32768 tokens per step; C restatement of scripts/tq3_rounding.py "
+                                "(no reference C exists) + reference hadamard_transform_row")
     else:
         tokens = 4096
-        arr = torch.randn(tokens, 8 * 128).numpy()
+        x = rng.standard_normal((tokens, 8, 128), dtype=np.float32)
+        for h in range(8):
+            x[:, h, rng.permutation(128)[:4]] *= 20.0
+        arr = np.ascontiguousarray(x.reshape(tokens, -1))
         bytes_ = 2 * (arr.size * 4 + arr.size // 32 * 18)
         fn = lambda: O.parallel_dequantize(O.parallel_quantize(arr, 4, 128, n, impl="reference"),  # noqa: E731
                                            4, arr.shape[1], n)
+        config["input"] = INPUT[wl]
         kind, sample = "reference", ("full [4096, 8, 128] per step; src/ggml-tq.c hadamard_transform_row + "
                                      "quantize_row_tq4_0 + dequantize_row_tq4_0")
+    config["parallelism"] = f"{n} host threads"
     for _ in range(args.warmup):
         fn()
     t0 = time.perf_counter()
@@ -690,11 +733,10 @@ def run_reference(args, ws, rank):
     dt = (time.perf_counter() - t0) / args.steps
     v = bytes_ / dt / 1e9
     return {"metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None,
-            "dtype": {"tq3opt": "bf16->u8", "tq4": "f32->u8->f32", "attn": "f64"}[args.workload],
-            "data": "synthetic (seeded)", "impl": "reference",
-            "config": {"workload": args.workload, "parallelism": "host threads"},
+            "dtype": {"tq3opt": "bf16->u8", "tq4": "f32->u8->f32"}.get(wl, "f64"),
+            "data": "synthetic (seeded)", "impl": "reference", "config": config,
             "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": n, "kind": kind, "sample": sample},
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 

@@ -431,22 +431,29 @@ class Stream:
         self.kc = [torch.empty(B, H, cap, nb, 18, dtype=torch.uint8, device="cuda") for _ in range(self.nl)]
         self.vc = [torch.empty(B, H, cap, nb, 18, dtype=torch.uint8, device="cuda") for _ in range(self.nl)]
         g = torch.Generator(device="cuda").manual_seed(5 + 1000 * rank)
-        # prefill: inputs generated on the device layer by layer (bf16), quantize-on-write timed with events
+        # prefill: quantize-on-write of every layer's K and V (bf16, head_dim rotation).  The whole input
+        # (all layers) cannot be held, so two device-generated chunks of the configured shape and
+        # distribution are reused across layers; one untimed launch loads the kernel, then all
+        # launches run back to back between two events.
         chunk = max(1, min(B, (1 << 28) // (H * T0 * D)))
-        pre_ms, pre_bytes = 0.0, 0
+        pool = [_outlier_rows(g, (chunk, H, T0, D), D).to(torch.bfloat16) for _ in range(2)]
+        ops.kv_append(pool[0][:min(chunk, B)], self.kc[0][:min(chunk, B)])
+        pre_bytes, i = 0, 0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
         for l in range(self.nl):
             for cache in (self.kc[l], self.vc[l]):
                 for c0 in range(0, B, chunk):
                     c1 = min(B, c0 + chunk)
-                    x = _outlier_rows(g, (c1 - c0, H, T0, D), D).to(torch.bfloat16)
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    e0.record()
+                    x = pool[i % 2][:c1 - c0]
                     ops.kv_append(x, cache[c0:c1])
-                    e1.record()
-                    e1.synchronize()
-                    pre_ms += e0.elapsed_time(e1)
                     pre_bytes += x.numel() * 2 + x.numel() // 32 * 18
-                    del x
+                    i += 1
+        e1.record()
+        e1.synchronize()
+        pre_ms = e0.elapsed_time(e1)
+        del pool
         self.prefill = {"ms": round(pre_ms, 3), "bytes": pre_bytes, "GB_per_s": round(pre_bytes / pre_ms / 1e6, 1),
                         "tokens_per_seq": T0, "launches": self.nl * 2 * ((B + chunk - 1) // chunk)}
         # decode-step inputs for all layers in single buffers (one H2D / D2H each in e2e)

@@ -245,14 +245,28 @@ __device__ __forceinline__ void copy_rows(uint8_t* __restrict__ y, const uint8_t
     }
 }
 
-__device__ __forceinline__ void store_mapped(uint8_t* __restrict__ y, const uint8_t* __restrict__ smem,
-                                             int64_t* __restrict__ s_dst, int64_t b0, int nrows, int bb,
-                                             const RowMap& map, bool y_vec) {
-    const int nb = map.nblk, row_bytes = nb * bb, nr = nrows / nb;
+// Destination of each head row of the tile starting at block b0 (threads < rows of the tile;
+// the caller's next block-wide barrier publishes s_dst).  A head row holds nblk blocks, a power
+// of two; rows and sequences are divided in 32 bits whenever every row index fits.
+__device__ __forceinline__ void map_rows(int64_t* __restrict__ s_dst, int64_t b0, int nrows, int bb,
+                                         const RowMap& map) {
+    const int nb = map.nblk, row_bytes = nb * bb, lnb = __ffs(nb) - 1, nr = nrows >> lnb;
     if (threadIdx.x < nr) {
-        const int64_t R = b0 / nb + threadIdx.x;
-        const int64_t sh = R / map.n_new, t = R - sh * map.n_new;
-        const int64_t slot = (map.pos ? (int64_t)map.pos[sh / map.hkv] : 0) + t;
+        const int64_t R = (b0 >> lnb) + threadIdx.x, R1 = (b0 >> lnb) + nr - 1;   // this row, the tile's last
+        int64_t sh, t, seq, sh1;
+        if (R1 < (int64_t(1) << 31) && map.n_new < (int64_t(1) << 31)) {
+            const uint32_t r32 = (uint32_t)R, n32 = (uint32_t)map.n_new, sh32 = r32 / n32;
+            sh = sh32;
+            t = r32 - sh32 * n32;
+            seq = sh32 / (uint32_t)map.hkv;
+            sh1 = (uint32_t)R1 / n32;
+        } else {
+            sh = R / map.n_new;
+            t = R - sh * map.n_new;
+            seq = sh / map.hkv;
+            sh1 = R1 / map.n_new;
+        }
+        const int64_t slot = (map.pos ? (int64_t)map.pos[seq] : 0) + t;
         int64_t off = -1;
         if (slot >= 0 && slot < map.cap) off = (sh * map.cap + slot) * row_bytes;
         else if (map.overflow) atomicAdd(map.overflow, 1);
@@ -260,11 +274,16 @@ __device__ __forceinline__ void store_mapped(uint8_t* __restrict__ y, const uint
         if (threadIdx.x == 0) {
             // the whole tile lands in consecutive slots of one (sequence, head) when its last
             // row belongs to the same (sequence, head) and still fits
-            const int64_t R1 = R + nr - 1, sh1 = R1 / map.n_new;
             s_dst[CODEC_THREADS] = (off >= 0 && sh1 == sh && slot + (nr - 1) < map.cap) ? 1 : 0;
         }
     }
-    __syncthreads();
+}
+
+// Store the staged tile to the rows map_rows() placed (s_dst published by an earlier barrier).
+__device__ __forceinline__ void store_mapped(uint8_t* __restrict__ y, const uint8_t* __restrict__ smem,
+                                             const int64_t* __restrict__ s_dst, int nrows, int bb,
+                                             const RowMap& map, bool y_vec) {
+    const int nb = map.nblk, row_bytes = nb * bb, nr = nrows / nb;
     if (s_dst[CODEC_THREADS]) {
         uint8_t* dst = y + s_dst[0];
         store_staged(dst, smem, nrows * bb, y_vec && (((uintptr_t)dst) & 15) == 0);
@@ -561,6 +580,8 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const int64_t b0 = tile * CODEC_THREADS;
         const int nrows = rows_of(tile);
+        // cache placement of this tile's rows, while its copies land (the barrier below publishes it)
+        if (map.cap != 0) map_rows(s_dst, b0, nrows, BB, map);
         uint8_t* s_in = s_in2[it % NBUF];
         if (async_tiles) {
             const int64_t nxt = tile + gridDim.x;
@@ -570,7 +591,7 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
         } else {
             load_tile<IN>(s_in, x + b0 * QK, nrows, x_vec != 0);
         }
-        __syncthreads();          // every thread's copies have landed
+        __syncthreads();          // every thread's copies have landed; s_dst is complete
 
         float v[QK];
         read_row<IN>(s_in, threadIdx.x < nrows ? threadIdx.x : 0, v);
@@ -585,7 +606,7 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
         encode_block<QT, MODE>(v, near_tb, &s_tbl, n_passes, s_out, threadIdx.x * BB, threadIdx.x < nrows);
         __syncthreads();          // s_out complete; s_in of this tile fully read
         if (map.cap == 0) store_staged(y + b0 * BB, s_out, nrows * BB, y_vec != 0);
-        else store_mapped(y, s_out, s_dst, b0, nrows, BB, map, y_vec != 0);
+        else store_mapped(y, s_out, s_dst, nrows, BB, map, y_vec != 0);
         __syncthreads();          // s_out free for the next tile
     }
     cp_async_wait<0>();

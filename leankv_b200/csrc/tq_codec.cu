@@ -551,7 +551,9 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
     __shared__ __align__(128) uint8_t s_in2[NBUF][CODEC_THREADS * ROW_BYTES];
     __shared__ __align__(16) uint8_t s_out[CODEC_THREADS * BB];
     __shared__ Tq3OptTables s_tbl;
-    __shared__ int64_t s_dst[CODEC_THREADS + 1];   // row-mapped output: byte offset of each head row | contiguous flag
+    // row-mapped output: byte offset of each head row | contiguous flag; two tiles' worth, since
+    // tile i + 1's placement is written while tile i is still being stored
+    __shared__ int64_t s_dst2[2][CODEC_THREADS + 1];
     __shared__ __align__(16) uint2 s_near[NEAR_ROWS * NEAR_REP];
 
     near_table_init<QT>(s_near);
@@ -581,6 +583,7 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
         const int64_t b0 = tile * CODEC_THREADS;
         const int nrows = rows_of(tile);
         // cache placement of this tile's rows, while its copies land (the barrier below publishes it)
+        int64_t* s_dst = s_dst2[it & 1];
         if (map.cap != 0) map_rows(s_dst, b0, nrows, BB, map);
         uint8_t* s_in = s_in2[it % NBUF];
         if (async_tiles) {
@@ -607,7 +610,8 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
         __syncthreads();          // s_out complete; s_in of this tile fully read
         if (map.cap == 0) store_staged(y + b0 * BB, s_out, nrows * BB, y_vec != 0);
         else store_mapped(y, s_out, s_dst, nrows, BB, map, y_vec != 0);
-        __syncthreads();          // s_out free for the next tile
+        // No barrier here: the next tile writes s_out only after its own first barrier, which
+        // every thread reaches after finishing this store; its placement goes to the other s_dst.
     }
     cp_async_wait<0>();
 }

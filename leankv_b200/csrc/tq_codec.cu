@@ -216,15 +216,17 @@ __device__ __forceinline__ void stage_block(uint8_t* __restrict__ smem, int off,
     }
 }
 
-// cooperative copy of nbytes from shared staging to global
+// cooperative copy of nbytes from shared staging to global by threads t0, t0 + stride, ...
+// (the whole CTA by default, one warp with t0 = lane, stride = 32)
 __device__ __forceinline__ void store_staged(uint8_t* __restrict__ dst, const uint8_t* __restrict__ smem,
-                                             int nbytes, bool vec_ok) {
+                                             int nbytes, bool vec_ok, int t0 = threadIdx.x,
+                                             int stride = CODEC_THREADS) {
     if (vec_ok && (nbytes & 15) == 0) {
         int4* d4 = reinterpret_cast<int4*>(dst);
         const int4* s4 = reinterpret_cast<const int4*>(smem);
-        for (int c = threadIdx.x; c < nbytes / 16; c += CODEC_THREADS) d4[c] = s4[c];
+        for (int c = t0; c < nbytes / 16; c += stride) d4[c] = s4[c];
     } else {
-        for (int b = threadIdx.x; b < nbytes; b += CODEC_THREADS) dst[b] = smem[b];
+        for (int b = t0; b < nbytes; b += stride) dst[b] = smem[b];
     }
 }
 
@@ -235,9 +237,10 @@ __device__ __forceinline__ void store_staged(uint8_t* __restrict__ dst, const ui
 // divides the row size (rows and the cache start are 16-byte aligned otherwise).
 template <typename W>
 __device__ __forceinline__ void copy_rows(uint8_t* __restrict__ y, const uint8_t* __restrict__ smem,
-                                          const int64_t* __restrict__ dst, int nr, int row_bytes) {
+                                          const int64_t* __restrict__ dst, int nr, int row_bytes,
+                                          int t0 = threadIdx.x, int stride = CODEC_THREADS) {
     const int wpr = row_bytes / (int)sizeof(W);
-    for (int c = threadIdx.x; c < nr * wpr; c += CODEC_THREADS) {
+    for (int c = t0; c < nr * wpr; c += stride) {
         const int r = c / wpr, w = c - r * wpr;
         const int64_t off = dst[r];
         if (off >= 0)
@@ -279,20 +282,26 @@ __device__ __forceinline__ void map_rows(int64_t* __restrict__ s_dst, int64_t b0
     }
 }
 
-// Store the staged tile to the rows map_rows() placed (s_dst published by an earlier barrier).
-__device__ __forceinline__ void store_mapped(uint8_t* __restrict__ y, const uint8_t* __restrict__ smem,
-                                             const int64_t* __restrict__ s_dst, int nrows, int bb,
-                                             const RowMap& map, bool y_vec) {
+// Staged head rows stored to the rows map_rows() placed (s_dst published by an earlier barrier):
+// the whole tile by all threads (t0 = threadIdx.x, stride = CODEC_THREADS, part ignored), or
+// warp `part`'s 32 blocks (32 / nblk whole head rows) by its lanes (t0 = lane, stride = 32).
+__device__ __forceinline__ void store_mapped_warp(uint8_t* __restrict__ y, const uint8_t* __restrict__ smem,
+                                                  const int64_t* __restrict__ s_dst, int nrows, int bb,
+                                                  const RowMap& map, bool y_vec, int part, int t0, int stride) {
     const int nb = map.nblk, row_bytes = nb * bb, nr = nrows / nb;
+    const int rpw = stride == CODEC_THREADS ? nr : 32 / nb;
+    const int r0 = stride == CODEC_THREADS ? 0 : part * rpw, r1 = nr < r0 + rpw ? nr : r0 + rpw;
+    if (r0 >= r1) return;
+    const uint8_t* src = smem + r0 * row_bytes;
     if (s_dst[CODEC_THREADS]) {
-        uint8_t* dst = y + s_dst[0];
-        store_staged(dst, smem, nrows * bb, y_vec && (((uintptr_t)dst) & 15) == 0);
+        uint8_t* dst = y + s_dst[0] + (int64_t)r0 * row_bytes;
+        store_staged(dst, src, (r1 - r0) * row_bytes, y_vec && (((uintptr_t)dst) & 15) == 0, t0, stride);
     } else if ((row_bytes & 7) == 0) {
-        copy_rows<uint2>(y, smem, s_dst, nr, row_bytes);
+        copy_rows<uint2>(y, src, s_dst + r0, r1 - r0, row_bytes, t0, stride);
     } else if ((row_bytes & 3) == 0) {
-        copy_rows<uint32_t>(y, smem, s_dst, nr, row_bytes);
+        copy_rows<uint32_t>(y, src, s_dst + r0, r1 - r0, row_bytes, t0, stride);
     } else {
-        copy_rows<uint16_t>(y, smem, s_dst, nr, row_bytes);
+        copy_rows<uint16_t>(y, src, s_dst + r0, r1 - r0, row_bytes, t0, stride);
     }
 }
 
@@ -573,28 +582,46 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
         const int64_t b = t * CODEC_THREADS;
         return (int)(nblocks - b < CODEC_THREADS ? nblocks - b : CODEC_THREADS);
     };
-    // tile i is read from s_in2[i & 1]; tile i + 1 is in flight (cp.async) while tile i computes
+    // Tile i is read from s_in2[i & 1]; tile i + 1 is in flight (cp.async) while tile i computes.
+    // Two schedules, chosen by measurement:
+    //  * bandwidth-bound modes (MODE 0): tile i + 1's copies are issued before tile i's landing
+    //    wait, so they overlap the barrier too; a second barrier (staged blocks complete, tile i's
+    //    input read) precedes the block-wide store;
+    //  * TQ3 optimal rounding (MODE 1, compute bound): one barrier per tile; after it every thread
+    //    is done with tile i - 1, so the prefetch into that buffer is issued behind it, and each
+    //    warp stores its own 32 staged blocks.
+    constexpr bool ONE_BARRIER = MODE == 1;
     const bool async_tiles = NBUF == 2 && x_vec;
     if (async_tiles && (int64_t)blockIdx.x < ntiles)
         load_tile_async<IN>(s_in2[0], x + (int64_t)blockIdx.x * CODEC_THREADS * QK, rows_of(blockIdx.x));
     cp_async_commit();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int it = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const int64_t b0 = tile * CODEC_THREADS;
         const int nrows = rows_of(tile);
-        // cache placement of this tile's rows, while its copies land (the barrier below publishes it)
+        // cache placement of this tile's rows, while its copies land (the barrier below publishes it;
+        // two buffers, since a thread may still be storing the previous tile)
         int64_t* s_dst = s_dst2[it & 1];
         if (map.cap != 0) map_rows(s_dst, b0, nrows, BB, map);
         uint8_t* s_in = s_in2[it % NBUF];
+        const int64_t nxt = tile + gridDim.x;
         if (async_tiles) {
-            const int64_t nxt = tile + gridDim.x;
-            if (nxt < ntiles) load_tile_async<IN>(s_in2[(it + 1) % NBUF], x + nxt * CODEC_THREADS * QK, rows_of(nxt));
-            cp_async_commit();
-            cp_async_wait<1>();   // this thread's copies of the current tile have landed
+            if (!ONE_BARRIER) {
+                if (nxt < ntiles) load_tile_async<IN>(s_in2[(it + 1) % NBUF], x + nxt * CODEC_THREADS * QK, rows_of(nxt));
+                cp_async_commit();
+                cp_async_wait<1>();   // this thread's copies of the current tile have landed
+            } else {
+                cp_async_wait<0>();
+            }
         } else {
             load_tile<IN>(s_in, x + b0 * QK, nrows, x_vec != 0);
         }
         __syncthreads();          // every thread's copies have landed; s_dst is complete
+        if (ONE_BARRIER && async_tiles) {
+            if (nxt < ntiles) load_tile_async<IN>(s_in2[(it + 1) % NBUF], x + nxt * CODEC_THREADS * QK, rows_of(nxt));
+            cp_async_commit();
+        }
 
         float v[QK];
         read_row<IN>(s_in, threadIdx.x < nrows ? threadIdx.x : 0, v);
@@ -607,10 +634,22 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
         }
         fwht_block<L2>(v, log2_hd, norm);
         encode_block<QT, MODE>(v, near_tb, &s_tbl, n_passes, s_out, threadIdx.x * BB, threadIdx.x < nrows);
-        __syncthreads();          // s_out complete; s_in of this tile fully read
-        if (map.cap == 0) store_staged(y + b0 * BB, s_out, nrows * BB, y_vec != 0);
-        else store_mapped(y, s_out, s_dst, nrows, BB, map, y_vec != 0);
-        // No barrier here: the next tile writes s_out only after its own first barrier, which
+        if (!ONE_BARRIER) {
+            __syncthreads();      // s_out complete; s_in of this tile fully read
+            if (map.cap == 0) store_staged(y + b0 * BB, s_out, nrows * BB, y_vec != 0);
+            else store_mapped_warp(y, s_out, s_dst, nrows, BB, map, y_vec != 0, 0, threadIdx.x, CODEC_THREADS);
+        } else {
+            __syncwarp();         // this warp's 32 staged blocks are complete
+            if (map.cap == 0) {
+                const int nw = nrows - 32 * warp;   // blocks of this warp
+                if (nw > 0)
+                    store_staged(y + (b0 + 32 * warp) * BB, s_out + 32 * warp * BB, (nw < 32 ? nw : 32) * BB,
+                                 y_vec != 0, lane, 32);
+            } else {
+                store_mapped_warp(y, s_out, s_dst, nrows, BB, map, y_vec != 0, warp, lane, 32);
+            }
+        }
+        // No barrier here: the next tile writes s_out only after its own landing barrier, which
         // every thread reaches after finishing this store; its placement goes to the other s_dst.
     }
     cp_async_wait<0>();

@@ -83,6 +83,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     return false;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -272,9 +276,12 @@ __device__ __forceinline__ void static_for(F&& f) {
     }
 }
 
-// Per-configuration constants.  head_dim 256 runs 8 warps per CTA so that the
-// O and q fragments (96 registers) fit the 255-register limit; head_dim 128
-// runs 16.  Token order inside a 16-token tile (mma row / k index r holds
+// Per-configuration constants.  A CTA runs 16 warps.  At head_dim 128 every warp
+// streams its own tiles over all 4 blocks of a token row; at head_dim 256 the
+// warps work in pairs (SPLIT = 2): both warps of a pair take the same tiles from
+// one shared ring, each covers 4 of the 8 blocks (half the dimensions), and they
+// add their partial scores through shared memory, so each warp's O and q
+// fragments stay those of head_dim 128.  Token order inside a 16-token tile (mma row / k index r holds
 // token tok_of_row(r)) is chosen per token pitch so that every fragment load is
 // free of bank conflicts:
 //   head_dim 128 (K pitch 72 or 56 bytes, V pitch 72): r < 8 -> 2r, r >= 8 -> 2(r-8)+1,
@@ -284,17 +291,22 @@ __device__ __forceinline__ void static_for(F&& f) {
 // The softmax sum over tokens is order-free.
 template <int D, int KT>
 struct AttnCfg {
-    static constexpr int NBLK = D / 32;
-    static constexpr int WARPS = D == 128 ? 16 : 8;
+    static constexpr int NBLK = D / 32;                  // blocks per token row
+    static constexpr int SPLIT = D / 128;                // warps per tile stream
+    static constexpr int NBW = NBLK / SPLIT;             // blocks per warp (4)
+    static constexpr int WARPS = 16;
+    static constexpr int RINGS = WARPS / SPLIT;          // tile streams (rings) per CTA
+    // stage-release barriers: the second warp of a pair frees a stage before the first refills it
+    static constexpr int EBARS = SPLIT == 2 ? RINGS * ATT_STAGES : 0;
     static constexpr int THREADS = WARPS * 32;
     static constexpr int KBB = KT == 4 ? TQ4_BYTES : TQ3_BYTES;   // K bytes per block
     static constexpr int KB = KBB * NBLK;                          // K bytes per token
     static constexpr int VB = TQ4_BYTES * NBLK;                    // V bytes per token
     static constexpr int KTILE = ATT_TILE * KB, VTILE = ATT_TILE * VB;
     static constexpr int STAGE = KTILE + VTILE;
-    static constexpr int NCH = D / 16, NMT = D / 16;
-    // scale scratch of one tile: dK f32 [row][blk] | dV f16 [t][blk][rows 2t, 2t+1, 2t+8, 2t+9]
-    static constexpr int SCR = ATT_TILE * NBLK * 4 + NBLK * ATT_TILE * 2;
+    static constexpr int NCH = 2 * NBW, NMT = 2 * NBW;   // mma k-chunks / m-tiles of one warp
+    // scale scratch of one tile and warp: dK f32 [row][blk] | dV f16 [t][blk][rows 2t, 2t+1, 2t+8, 2t+9]
+    static constexpr int SCR = ATT_TILE * NBW * 4 + NBW * ATT_TILE * 2;
     static constexpr bool INTERLEAVE = D == 128;
     __host__ __device__ static constexpr int tok_of_row(int r) {
         return INTERLEAVE ? (r < 8 ? 2 * r : 2 * (r - 8) + 1) : r;
@@ -303,7 +315,7 @@ struct AttnCfg {
     static_assert(KTILE % 16 == 0 && STAGE % 16 == 0, "bulk-copy destinations must stay 16-byte aligned");
 };
 
-__host__ __device__ constexpr int att_warps(int D) { return D == 128 ? 16 : 8; }
+__host__ __device__ constexpr int att_warps(int) { return 16; }
 
 // TQ3 code pairs -> byte address in the codebook table: pair i of a 24-bit group word
 // (codes 2i, 2i+1) indexes row ((w >> 6i) & 63), TQ3 half of the row (byte 128 + 4 * lane).
@@ -319,10 +331,16 @@ __device__ __forceinline__ uint32_t lut_ld_addr(uint32_t addr) {
     return v;
 }
 
+// named barrier of the two warps of a pair (barrier 0 is __syncthreads)
+__device__ __forceinline__ void pair_sync(int ring) {
+    asm volatile("bar.sync %0, 64;" ::"r"(ring + 1) : "memory");
+}
+
 template <int D, int KT, int RES>
 __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const AttnKernelArgs a) {
     using Cfg = AttnCfg<D, KT>;
-    constexpr int NBLK = Cfg::NBLK, WARPS = Cfg::WARPS, THREADS = Cfg::THREADS;
+    constexpr int WARPS = Cfg::WARPS, THREADS = Cfg::THREADS;
+    constexpr int SPLIT = Cfg::SPLIT, RINGS = Cfg::RINGS, NBLK = Cfg::NBW;   // NBLK: this warp's blocks
     constexpr int KBB = Cfg::KBB, KB = Cfg::KB, VB = Cfg::VB;
     constexpr int KTILE = Cfg::KTILE, STAGE = Cfg::STAGE;
     constexpr int NCH = Cfg::NCH, NMT = Cfg::NMT, SCR = Cfg::SCR;
@@ -330,13 +348,16 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
     static_assert(D == 128 || D == 256, "head_dim 128 or 256");
 
     extern __shared__ __align__(1024) uint8_t smem[];
-    // layout: LUT | stages [warp][stage] | scale scratch [warp] | barriers [warp][stage] | flag
+    // layout: LUT | stages [ring][stage] | scale scratch [warp] | barriers [ring][stage] |
+    // release barriers [ring][stage] (pairs only) | flag
     uint8_t* stages = smem + LUT_BYTES;
-    uint8_t* scratch = stages + WARPS * ATT_STAGES * STAGE;
+    uint8_t* scratch = stages + RINGS * ATT_STAGES * STAGE;
     uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + WARPS * 2 * SCR);
-    int* s_abort = reinterpret_cast<int*>(bars + WARPS * ATT_STAGES);
+    uint64_t* ebars = bars + RINGS * ATT_STAGES;
+    int* s_abort = reinterpret_cast<int*>(ebars + Cfg::EBARS);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ring = warp / SPLIT, half = warp % SPLIT;   // tile stream, half of the dimensions
     const int gq = lane >> 2, tq = lane & 3;
     const uint32_t lane4 = (uint32_t)lane << 2;
 
@@ -350,44 +371,51 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         if (KT == 3 && k < 64)
             *reinterpret_cast<uint32_t*>(smem + (k << 8) + 128 + (l << 2)) = pack_h2(tq3_level(k & 7), tq3_level(k >> 3));
     }
-    if (lane == 0)
-        for (int s = 0; s < ATT_STAGES; ++s) mbar_init(smem_u32(&bars[warp * ATT_STAGES + s]), 1);
+    if (lane == 0 && half == 0)
+        for (int s = 0; s < ATT_STAGES; ++s) {
+            mbar_init(smem_u32(&bars[ring * ATT_STAGES + s]), 1);
+            if constexpr (SPLIT == 2) mbar_init(smem_u32(&ebars[ring * ATT_STAGES + s]), 1);
+        }
     if (threadIdx.x == 0) *s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     __syncthreads();
 
-    const uint32_t stage0 = smem_u32(stages + warp * ATT_STAGES * STAGE);
+    const uint32_t stage0 = smem_u32(stages + ring * ATT_STAGES * STAGE);
     const uint32_t scr = smem_u32(scratch + warp * 2 * SCR);   // tile A at scr, tile B at scr + SCR
-    const uint32_t bar0 = smem_u32(&bars[warp * ATT_STAGES]);
+    const uint32_t bar0 = smem_u32(&bars[ring * ATT_STAGES]);
+    const uint32_t ebar0 = smem_u32(ebars + ring * ATT_STAGES);   // valid when SPLIT == 2
+    // this warp's blocks start hk / hv bytes into a token's K / V row
+    const uint32_t hk = half * NBLK * KBB, hv = half * NBLK * TQ4_BYTES;
     // per-lane fixed offsets inside a stage
     constexpr int KROW8 = (Cfg::tok_of_row(8) - Cfg::tok_of_row(0)) * KB;   // row g+8 relative to row g
     const int ktok = Cfg::tok_of_row(gq);
     // TQ4 K, even blocks (codes start 2 mod 4): byte pair (8h + 2t, 8h + 2t + 1) for chunk h;
     // odd blocks (codes start 0 mod 4): the aligned word of bytes 4t .. 4t + 3, chunk h = bytes
     // (4t + 2h, 4t + 2h + 1)
-    const uint32_t k_off = ktok * KB + 2 * tq + 2;
-    const uint32_t k_off_w = ktok * KB + 4 * tq + 2;
+    const uint32_t k_off = ktok * KB + hk + 2 * tq + 2;
+    const uint32_t k_off_w = ktok * KB + hk + 4 * tq + 2;
     // TQ3 K: group t of each block, read as two aligned words and a funnel shift; blocks
     // start at 14 * blk bytes, which is 0 mod 4 for even and 2 mod 4 for odd blk
-    const uint32_t k3_off_e = ktok * KB + ((2 + 3 * tq) & ~3), k3_sh_e = 8 * ((2 + 3 * tq) & 3);
-    const uint32_t k3_off_o = ktok * KB + ((4 + 3 * tq) & ~3), k3_sh_o = 8 * ((4 + 3 * tq) & 3);
+    const uint32_t k3_off_e = ktok * KB + hk + ((2 + 3 * tq) & ~3), k3_sh_e = 8 * ((2 + 3 * tq) & 3);
+    const uint32_t k3_off_o = ktok * KB + hk + ((4 + 3 * tq) & ~3), k3_sh_o = 8 * ((4 + 3 * tq) & 3);
     const uint32_t lane4x = lane4 | 0x80u;
     // V: k-indices 2t, 2t+1, 2t+8, 2t+9 of the P fragment
     constexpr int VT0 = Cfg::tok_of_row(0);
     constexpr int VO1 = (Cfg::tok_of_row(1) - VT0) * VB, VO8 = (Cfg::tok_of_row(8) - VT0) * VB,
                   VO9 = (Cfg::tok_of_row(9) - VT0) * VB;
-    const uint32_t v_off = Cfg::tok_of_row(2 * tq) * VB + 2 * gq + 2;
+    const uint32_t v_off = Cfg::tok_of_row(2 * tq) * VB + hv + 2 * gq + 2;
     // scale extraction: lane handles K entries r = 0 .. NBLK/2-1 and V entries likewise; entry r
     // of this lane is token xt0 + r * TSTEP, block xb
     constexpr int TSTEP = 32 / NBLK, ROWSTEP = Cfg::INTERLEAVE ? TSTEP / 2 : TSTEP, NXH = NBLK / 2;
     const int xt0 = lane / NBLK, xb = lane % NBLK, xrow0 = Cfg::row_of_tok(xt0);
-    const uint32_t xks = xt0 * KB + xb * KBB, xkd = (xrow0 * NBLK + xb) * 4;
+    const uint32_t xks = xt0 * KB + hk + xb * KBB, xkd = (xrow0 * NBLK + xb) * 4;
     // dV of row r, block b at (((r & 7) >> 1) * NBLK + b) * 8 + ((r & 1) + 2 * (r >> 3)) * 2: lane t then
     // finds the four P rows of every block in 2 * NBLK consecutive words.  Entry rr adds
     // rr * ROWSTEP rows to a first row whose low three bits stay below 4, hence VDELTA(rr).
-    const uint32_t xvs = KTILE + xt0 * VB + xb * TQ4_BYTES,
+    const uint32_t xvs = KTILE + xt0 * VB + hv + xb * TQ4_BYTES,
                    xvd = ATT_TILE * NBLK * 4 + ((((xrow0 & 7) >> 1) * NBLK + xb) * 8 + ((xrow0 & 1) + 2 * (xrow0 >> 3)) * 2);
     uint32_t phase_bits = 0;
+    uint32_t ephase_bits = 0;   // release-barrier parities, kept by the issuing lane of a pair
 
     const int64_t pairs = (int64_t)a.B * a.Hkv;
     const int64_t total = pairs * a.lnom;
@@ -404,7 +432,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         if (len > a.cap) len = a.cap;
         if (t1 > len) t1 = len;
         const int ntiles_seg = t1 > t0 ? (int)((t1 - t0 + ATT_TILE - 1) / ATT_TILE) : 0;
-        const int ntiles = ntiles_seg > warp ? (ntiles_seg - warp + WARPS - 1) / WARPS : 0;
+        const int ntiles = ntiles_seg > ring ? (ntiles_seg - ring + RINGS - 1) / RINGS : 0;
 
         const uint8_t* kbase = a.k + (size_t)pair * a.cap * KB;
         const uint8_t* vbase = a.v + (size_t)pair * a.cap * VB;
@@ -414,12 +442,12 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         for (int mt = 0; mt < NMT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
         float m_run0 = M_FLOOR, m_run1 = M_FLOOR, l0 = 0.0f, l1 = 0.0f;
 
-        // copy sources advance by one CTA tile row (WARPS x 16 tokens) per warp tile
-        const uint8_t* ksrc = kbase + (t0 + (int64_t)warp * ATT_TILE) * KB;
-        const uint8_t* vsrc = vbase + (t0 + (int64_t)warp * ATT_TILE) * VB;
-        const int64_t tok_first = t0 + (int64_t)warp * ATT_TILE;      // first token of tile 0
+        // copy sources advance by one CTA tile row (RINGS x 16 tokens) per ring tile
+        const uint8_t* ksrc = kbase + (t0 + (int64_t)ring * ATT_TILE) * KB;
+        const uint8_t* vsrc = vbase + (t0 + (int64_t)ring * ATT_TILE) * VB;
+        const int64_t tok_first = t0 + (int64_t)ring * ATT_TILE;      // first token of tile 0
         // tokens of the last tile that exist in memory (capacity), for the copy size
-        const int64_t t_last = tok_first + (int64_t)(ntiles > 0 ? ntiles - 1 : 0) * WARPS * ATT_TILE;
+        const int64_t t_last = tok_first + (int64_t)(ntiles > 0 ? ntiles - 1 : 0) * RINGS * ATT_TILE;
         const uint32_t last_nt = (uint32_t)(a.cap - t_last < ATT_TILE ? a.cap - t_last : ATT_TILE);
         // tokens of the last tile below the valid length (tiles before it are full)
         const int last_valid = (int)(t1 - t_last < ATT_TILE ? t1 - t_last : ATT_TILE);
@@ -428,10 +456,18 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
             constexpr int S = decltype(stage_c)::value;
             const bool last = issued == ntiles - 1;
             const uint32_t nt = last ? last_nt : (uint32_t)ATT_TILE;
-            bulk_issue(lane == 0 && issued < ntiles, stage0 + S * STAGE, ksrc, nt * KB, stage0 + S * STAGE + KTILE,
-                       vsrc, nt * VB, bar0 + 8 * S);
-            ksrc += (size_t)WARPS * ATT_TILE * KB;
-            vsrc += (size_t)WARPS * ATT_TILE * VB;
+            bool go = lane == 0 && half == 0 && issued < ntiles;
+            if (SPLIT == 2 && go && issued >= ATT_STAGES) {
+                // the partner warp must be done with tile issued - ATT_STAGES in this stage; a
+                // release that never comes leaves the stage unfilled and the full-barrier wait
+                // of both warps then runs out and reports the timeout
+                go = mbar_wait(ebar0 + 8 * S, (ephase_bits >> S) & 1u);
+                ephase_bits ^= 1u << S;
+            }
+            bulk_issue(go, stage0 + S * STAGE, ksrc, nt * KB, stage0 + S * STAGE + KTILE, vsrc, nt * VB,
+                       bar0 + 8 * S);
+            ksrc += (size_t)RINGS * ATT_TILE * KB;
+            vsrc += (size_t)RINGS * ATT_TILE * VB;
             ++issued;
         };
         // Tiles are processed in pairs: tiles 2p and 2p + 1 sit in stages 2p mod 4 and
@@ -470,7 +506,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
             const float* mq = sq + gq * SQS;
 #pragma unroll
             for (int kk = 0; kk < NCH; ++kk) {
-                const int blk = kk >> 1, h = kk & 1;
+                const int blk = half * NBLK + (kk >> 1), h = kk & 1;   // block of the token row
                 if constexpr (KT == 4) {   // k-cols (2t, 2t+1) = elements (j, j+16), (2t+8, 2t+9) = (j+1, j+17)
                     const int e0 = 32 * blk + ((blk & 1) ? 4 * tq + 2 * h : 8 * h + 2 * tq);
                     qf[kk][0] = pack_h2(mq[e0], mq[e0 + 16]);
@@ -634,11 +670,15 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 // every lane waits; the outcome is made warp-uniform before any warp collective
                 bool ok = mbar_wait(bar0 + 8 * SA, (phase_bits >> SA) & 1u);
                 if (has_b) ok = ok && mbar_wait(bar0 + 8 * SB, (phase_bits >> SB) & 1u);
-                if (!__all_sync(0xffffffffu, ok)) {
-                    timed_out = true;
-                    return;
+                ok = __all_sync(0xffffffffu, ok);
+                // a pair leaves together: its partner learns the outcome at the score exchange below
+                if constexpr (SPLIT == 1) {
+                    if (!ok) {
+                        timed_out = true;
+                        return;
+                    }
+                    phase_bits ^= (1u << SA) | (has_b ? (1u << SB) : 0u);
                 }
-                phase_bits ^= (1u << SA) | (has_b ? (1u << SB) : 0u);
                 const int valid_a = ia == ntiles - 1 ? last_valid : ATT_TILE;
                 const int valid_b = !has_b ? 0 : (ia + 1 == ntiles - 1 ? last_valid : ATT_TILE);
                 const uint32_t sta = stage0 + SA * STAGE, stb = stage0 + SB * STAGE;
@@ -648,6 +688,45 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 float sa[4], sb[4];
                 scores(sta, scr, valid_a, sa);
                 scores(stb, scr + SCR, valid_b, sb);
+                if constexpr (SPLIT == 2) {
+                    // add the partner warp's partial scores (the other 4 blocks of every token row),
+                    // in the order half 0 + half 1 in both warps so both hold identical scores.  Slots:
+                    // the upper halves of codebook-table rows 64 .. 191 (unused by both tables),
+                    // 4 rows per (ring, half, tile), lanes 8k .. 8k+7 in row k.
+                    auto slot = [&](int hh, int t) {
+                        return smem_u32(smem) + ((64u + (uint32_t)(((ring * 2 + hh) * 2 + t) * 4) + (lane >> 3)) << 8) +
+                               128u + ((uint32_t)(lane & 7) << 4);
+                    };
+                    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(slot(half, 0)), "f"(sa[0]), "f"(sa[1]),
+                                 "f"(sa[2]), "f"(sa[3]) : "memory");
+                    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(slot(half, 1)), "f"(sb[0]), "f"(sb[1]),
+                                 "f"(sb[2]), "f"(sb[3]) : "memory");
+                    if (lane == 0)   // this warp's wait outcome, beside the slots (row 192, upper half)
+                        asm volatile("st.shared.u32 [%0], %1;" ::"r"(smem_u32(smem) + (192u << 8) + 128u +
+                                                                      (uint32_t)(ring * 2 + half) * 4u),
+                                     "r"((uint32_t)ok) : "memory");
+                    pair_sync(ring);
+                    uint32_t pok;
+                    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(pok) : "r"(smem_u32(smem) + (192u << 8) + 128u +
+                                                                         (uint32_t)(ring * 2 + (half ^ 1)) * 4u)
+                                 : "memory");
+                    float pa[4], pb[4];
+                    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(pa[0]), "=f"(pa[1]), "=f"(pa[2]),
+                                 "=f"(pa[3]) : "r"(slot(half ^ 1, 0)) : "memory");
+                    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(pb[0]), "=f"(pb[1]), "=f"(pb[2]),
+                                 "=f"(pb[3]) : "r"(slot(half ^ 1, 1)) : "memory");
+                    pair_sync(ring);   // both partials read before the slots are written again
+                    if (!(ok && pok != 0)) {
+                        timed_out = true;
+                        return;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        sa[i] = half == 0 ? sa[i] + pa[i] : pa[i] + sa[i];
+                        sb[i] = half == 0 ? sb[i] + pb[i] : pb[i] + sb[i];
+                    }
+                    phase_bits ^= (1u << SA) | (has_b ? (1u << SB) : 0u);
+                }
 
                 // ---- online softmax over the 32 tokens (log2 domain) ----
                 float mx0 = fmaxf(fmaxf(sa[0], sa[2]), fmaxf(sb[0], sb[2]));
@@ -680,6 +759,10 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 accumulate(sta, scr, movmatrix_t(pack_h2(pa0, pa1)), movmatrix_t(pack_h2(pa2, pa3)));
                 accumulate(stb, scr + SCR, movmatrix_t(pack_h2(pb0, pb1)), movmatrix_t(pack_h2(pb2, pb3)));
                 __syncwarp();   // stages SA, SB and the scratch may be overwritten from here on
+                if (SPLIT == 2 && half == 1 && lane == 0) {
+                    mbar_arrive(ebar0 + 8 * SA);
+                    if (has_b) mbar_arrive(ebar0 + 8 * SB);
+                }
             });
         }
         if (timed_out) {
@@ -691,6 +774,18 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
 #pragma unroll
             for (int s2 = 0; s2 < ATT_STAGES; ++s2) mbar_wait(bar0 + 8 * s2, (phase_bits >> s2) & 1u);
         }
+        if (SPLIT == 2 && !timed_out && lane == 0 && half == 0) {
+            // take the releases of the last tiles of the segment, which no refill waited for, so
+            // that every release is waited exactly once and the parities stay in step
+            for (int j = ntiles > ATT_STAGES ? ntiles - ATT_STAGES : 0; j < ntiles; ++j) {
+                const int st = j % ATT_STAGES;
+                if (!mbar_wait(ebar0 + 8 * st, (ephase_bits >> st) & 1u)) {
+                    atomicExch(a.err, (int)TQ_ERROR_TIMEOUT);
+                    *s_abort = 1;
+                }
+                ephase_bits ^= 1u << st;
+            }
+        }
         if (__any_sync(0xffffffffu, bad_scale >= 0x7800u) && lane == 0) atomicExch(a.err, (int)TQ_ERROR_UNSUPPORTED);
 
         // ---- merge the warps, write the (pair, slot) partial ----
@@ -701,9 +796,9 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         }
         __syncthreads();   // all warps done with their stages; reuse them as merge scratch
         if (*s_abort) return;
-        float* red = reinterpret_cast<float*>(stages);   // [warp][ATT_N][D + 2]
-        float* mine = red + warp * ATT_N * (D + 2);
-        if (gq == 0) {
+        float* red = reinterpret_cast<float*>(stages);   // [ring][ATT_N][D + 2]
+        float* mine = red + ring * ATT_N * (D + 2);
+        if (gq == 0 && half == 0) {
             mine[(2 * tq) * (D + 2) + 0] = m_run0;
             mine[(2 * tq + 1) * (D + 2) + 0] = m_run1;
             mine[(2 * tq) * (D + 2) + 1] = l0;
@@ -711,7 +806,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         }
 #pragma unroll
         for (int mt = 0; mt < NMT; ++mt) {
-            const int e0 = 32 * (mt >> 1) + 2 * gq + (mt & 1);
+            const int e0 = 128 * half + 32 * (mt >> 1) + 2 * gq + (mt & 1);
             mine[(2 * tq) * (D + 2) + 2 + e0] = o[mt][0];
             mine[(2 * tq + 1) * (D + 2) + 2 + e0] = o[mt][1];
             mine[(2 * tq) * (D + 2) + 2 + e0 + 16] = o[mt][2];
@@ -720,15 +815,15 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         __syncthreads();
         // per query head: the maximum over the warps, then each warp's weight 2^(m_w - M)
         float* smax = reinterpret_cast<float*>(scratch);   // [ATT_N] (the scale scratch is free here)
-        float* swt = smax + ATT_N;                          // [ATT_N][WARPS]
+        float* swt = smax + ATT_N;                          // [ATT_N][RINGS]
         if (threadIdx.x < ATT_N) {
             float M = M_FLOOR;
-            for (int w = 0; w < WARPS; ++w) M = fmaxf(M, red[w * ATT_N * (D + 2) + threadIdx.x * (D + 2)]);
+            for (int w = 0; w < RINGS; ++w) M = fmaxf(M, red[w * ATT_N * (D + 2) + threadIdx.x * (D + 2)]);
             smax[threadIdx.x] = M;
         }
         __syncthreads();
-        if (threadIdx.x < ATT_N * WARPS) {
-            const int h = threadIdx.x / WARPS, w = threadIdx.x % WARPS;
+        if (threadIdx.x < ATT_N * RINGS) {
+            const int h = threadIdx.x / RINGS, w = threadIdx.x % RINGS;
             swt[threadIdx.x] = ex2(red[w * ATT_N * (D + 2) + h * (D + 2)] - smax[h]);
         }
         __syncthreads();
@@ -739,7 +834,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
             float acc = smax[h];
             if (c > 0) {
                 acc = 0.0f;
-                for (int w = 0; w < WARPS; ++w) acc += swt[h * WARPS + w] * red[w * ATT_N * (D + 2) + idx];
+                for (int w = 0; w < RINGS; ++w) acc += swt[h * RINGS + w] * red[w * ATT_N * (D + 2) + idx];
             }
             dst[idx] = acc;
         }
@@ -828,11 +923,12 @@ template <int D, int KT>
 static size_t decode_smem_bytes() {
     using Cfg = AttnCfg<D, KT>;
     size_t s = LUT_BYTES;
-    const size_t stg = (size_t)Cfg::WARPS * ATT_STAGES * Cfg::STAGE;
-    const size_t red = (size_t)Cfg::WARPS * ATT_N * (D + 2) * 4;   // warp merge scratch reuses the stages
+    const size_t stg = (size_t)Cfg::RINGS * ATT_STAGES * Cfg::STAGE;
+    const size_t red = (size_t)Cfg::RINGS * ATT_N * (D + 2) * 4;   // ring merge scratch reuses the stages
     s += stg > red ? stg : red;
     s += (size_t)Cfg::WARPS * 2 * Cfg::SCR;
-    s += (size_t)Cfg::WARPS * ATT_STAGES * 8;
+    s += (size_t)Cfg::RINGS * ATT_STAGES * 8;
+    s += (size_t)Cfg::EBARS * 8;
     s += 16;
     return s;
 }

@@ -201,7 +201,7 @@ def test_attention_tq3_k_vs_oracle(orc, grp):
 @pytest.mark.parametrize("kt", [4, 3])
 @pytest.mark.parametrize("T,lens", [(2, [2, 1]), (34, [0, 33]), (530, [530, 77]), (3000, [2999, 1500])])
 def test_attention_head_dim_256(orc, kt, T, lens):
-    """head_dim 256 (8 warps per CTA, identity token order), TQ4_0 or TQ3_0 K, ragged lengths."""
+    """head_dim 256 (warp pairs, identity token order), TQ4_0 or TQ3_0 K, ragged lengths."""
     B, Hkv, D, grp = len(lens), 2, 256, 4
     kc = make_cache(B, Hkv, T, D, 70 + kt, qtype=kt)
     vc = make_cache(B, Hkv, T, D, 80 + kt)
@@ -212,6 +212,24 @@ def test_attention_head_dim_256(orc, kt, T, lens):
                                      kv_len=lt.numpy(), nthreads=8)
     rel = check(out.cpu().numpy(), ref, lse.cpu().numpy(), lref)
     print(f"D256 K TQ{kt} T {T}: rel err {rel:.3g}")
+
+
+@pytest.mark.parametrize("kt", [4, 3])
+def test_head_dim_256_many_segments_per_cta(kt):
+    """head_dim 256 with 416 (sequence, KV head) pairs of 590-700 tokens: every CTA runs
+    three or more segments whose rings hold 4-6 tiles each, so stages are refilled inside
+    a segment and across segments (the warp-pair stage-release parities)."""
+    B, Hq, Hkv, T, D = 52, 32, 8, 700, 256
+    g = torch.Generator(device=DEV).manual_seed(256 + kt)
+    kc = ops.quantize(torch.randn(B, Hkv, T, D, device=DEV, generator=g), kt, fwht_head_dim=D)
+    vc = ops.quantize(torch.randn(B, Hkv, T, D, device=DEV, generator=g), 4, fwht_head_dim=D)
+    q = torch.randn(B, Hq, D, device=DEV, generator=g).half()
+    lens = torch.tensor([T - 11 * (b % 11) for b in range(B)], dtype=torch.int32, device=DEV)
+    out, lse = attention.decode_attention(q, kc, vc, kv_len=lens, max_kv_len=T, return_lse=True)
+    for n in sorted(set(lens.tolist())):
+        sel = (lens == n).nonzero().flatten()
+        ref, lref = torch_reference(q[sel], kc[sel][:, :, :n], vc[sel][:, :, :n], D)
+        check(out[sel].cpu().numpy(), ref.cpu().numpy(), lse[sel].cpu().numpy(), lref.cpu().numpy())
 
 
 def test_attention_tq3_k_rotation_flags(orc):

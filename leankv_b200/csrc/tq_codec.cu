@@ -24,6 +24,7 @@
 // the reciprocal is the IEEE division 1.0f / amax; the build uses no fast-math
 // so every fp32 operation is correctly rounded and denormals are kept.
 #include <type_traits>
+#include <utility>
 
 #include "tq_common.cuh"
 #include "tq_kernels.h"
@@ -102,6 +103,30 @@ __device__ __forceinline__ void load_tile_async(uint8_t* __restrict__ smem, cons
     }
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// Programmatic dependent launch.  The quantize and dequantize kernels are launched with
+// programmatic stream serialization: the next such kernel on the stream may start while this
+// one runs (trigger at entry), does its setup, and waits for the whole previous grid to
+// complete, with its memory visible, before its first global access (read or write).  Without
+// the launch attribute both instructions are no-ops.
+__device__ __forceinline__ void grid_dep_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_dependent(void (*kernel)(KArgs...), unsigned grid, unsigned block, cudaStream_t st,
+                                    Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
@@ -565,6 +590,7 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
     __shared__ int64_t s_dst2[2][CODEC_THREADS + 1];
     __shared__ __align__(16) uint2 s_near[NEAR_ROWS * NEAR_REP];
 
+    grid_dep_trigger();
     near_table_init<QT>(s_near);
     const uint32_t near_tb = (uint32_t)__cvta_generic_to_shared(s_near) + 8u * (threadIdx.x & (NEAR_REP - 1));
     if (MODE == 1) {
@@ -592,6 +618,7 @@ quantize_kernel(const IN* __restrict__ x, uint8_t* __restrict__ y, int64_t nbloc
     //    warp stores its own 32 staged blocks.
     constexpr bool ONE_BARRIER = MODE == 1;
     const bool async_tiles = NBUF == 2 && x_vec;
+    grid_dep_wait();
     if (async_tiles && (int64_t)blockIdx.x < ntiles)
         load_tile_async<IN>(s_in2[0], x + (int64_t)blockIdx.x * CODEC_THREADS * QK, rows_of(blockIdx.x));
     cp_async_commit();
@@ -742,7 +769,9 @@ dequantize_kernel(const uint8_t* __restrict__ xq, OUT* __restrict__ y, int64_t n
     constexpr int NL = QT == 4 ? 16 : QT == 3 ? 8 : 4;
     __shared__ __align__(16) uint8_t s_in[DQ_TILE * BB];
     __shared__ float s_lvl[NL];
+    grid_dep_trigger();
     if (threadIdx.x < NL) s_lvl[threadIdx.x] = tq_level<QT>(threadIdx.x);
+    grid_dep_wait();
 
     const int64_t ntiles = (nblocks + DQ_TILE - 1) / DQ_TILE;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
@@ -869,22 +898,21 @@ struct RandRot {
 };
 
 template <int QT, typename IN, int MODE, int L2>
-static void launch_quant_k(const void* x, void* y, int64_t nblocks, int log2_hd, float norm, int n_passes,
-                           const RowMap& map, int grid, int xv, int yv, const RandRot& rr, cudaStream_t st) {
-    quantize_kernel<QT, IN, MODE, L2><<<grid, CODEC_THREADS, 0, st>>>((const IN*)x, (uint8_t*)y, nblocks, log2_hd,
-                                                                      norm, n_passes, xv, yv, map, rr.seed,
-                                                                      rr.heads_per_row);
+static cudaError_t launch_quant_k(const void* x, void* y, int64_t nblocks, int log2_hd, float norm, int n_passes,
+                                  const RowMap& map, int grid, int xv, int yv, const RandRot& rr, cudaStream_t st) {
+    return launch_dependent(quantize_kernel<QT, IN, MODE, L2>, (unsigned)grid, CODEC_THREADS, st, (const IN*)x,
+                            (uint8_t*)y, nblocks, log2_hd, norm, n_passes, xv, yv, map, rr.seed, rr.heads_per_row);
 }
 
 template <int QT, typename IN, int MODE>
-static void launch_quant_l2(const void* x, void* y, int64_t nblocks, int log2_hd, float norm, int n_passes,
-                            const RowMap& map, int grid, int xv, int yv, const RandRot& rr, cudaStream_t st) {
+static cudaError_t launch_quant_l2(const void* x, void* y, int64_t nblocks, int log2_hd, float norm, int n_passes,
+                                   const RowMap& map, int grid, int xv, int yv, const RandRot& rr, cudaStream_t st) {
     // head_dim 128 and 256 (and no rotation) get fully unrolled FWHT stages
     switch (log2_hd) {
-        case -1: launch_quant_k<QT, IN, MODE, -1>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st); break;
-        case 7: launch_quant_k<QT, IN, MODE, 7>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st); break;
-        case 8: launch_quant_k<QT, IN, MODE, 8>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st); break;
-        default: launch_quant_k<QT, IN, MODE, -2>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st); break;
+        case -1: return launch_quant_k<QT, IN, MODE, -1>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st);
+        case 7: return launch_quant_k<QT, IN, MODE, 7>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st);
+        case 8: return launch_quant_k<QT, IN, MODE, 8>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st);
+        default: return launch_quant_k<QT, IN, MODE, -2>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st);
     }
 }
 
@@ -899,13 +927,9 @@ static cudaError_t launch_quant_t(const void* x, void* y, int64_t nblocks, int l
     const int grid = codec_grid(ntiles, n_passes > 0 ? 4 : (sizeof(IN) == 4 ? 3 : 16));
     const int xv = ((uintptr_t)x & 15) == 0, yv = ((uintptr_t)y & 15) == 0;
     if constexpr (QT == 3) {
-        if (n_passes > 0) {
-            launch_quant_l2<QT, IN, 1>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st);
-            return cudaGetLastError();
-        }
+        if (n_passes > 0) return launch_quant_l2<QT, IN, 1>(x, y, nblocks, log2_hd, norm, n_passes, map, grid, xv, yv, rr, st);
     }
-    launch_quant_l2<QT, IN, 0>(x, y, nblocks, log2_hd, norm, 0, map, grid, xv, yv, rr, st);
-    return cudaGetLastError();
+    return launch_quant_l2<QT, IN, 0>(x, y, nblocks, log2_hd, norm, 0, map, grid, xv, yv, rr, st);
 }
 
 cudaError_t launch_quantize(int qtype, int in_dtype, const void* x, void* y, int64_t nblocks, int log2_hd,
@@ -997,9 +1021,9 @@ cudaError_t launch_requantize(int src_type, const void* src, int dst_type, void*
 template <int QT, typename OUT>
 static cudaError_t launch_dq_t(const void* x, void* y, int64_t nblocks, cudaStream_t st) {
     const int64_t ntiles = (nblocks + DQ_TILE - 1) / DQ_TILE;
-    dequantize_kernel<QT, OUT><<<codec_grid(ntiles, 8), DQ_THREADS, 0, st>>>(
-        (const uint8_t*)x, (OUT*)y, nblocks, ((uintptr_t)x & 15) == 0, ((uintptr_t)y & 15) == 0);
-    return cudaGetLastError();
+    return launch_dependent(dequantize_kernel<QT, OUT>, (unsigned)codec_grid(ntiles, 8), DQ_THREADS, st,
+                            (const uint8_t*)x, (OUT*)y, nblocks, (int)(((uintptr_t)x & 15) == 0),
+                            (int)(((uintptr_t)y & 15) == 0));
 }
 
 cudaError_t launch_dequantize(int qtype, int out_dtype, const void* x, void* y, int64_t nblocks, cudaStream_t st) {

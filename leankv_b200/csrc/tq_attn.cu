@@ -316,6 +316,7 @@ struct AttnCfg {
 };
 
 __host__ __device__ constexpr int att_warps(int) { return 16; }
+__host__ __device__ constexpr int att_rings(int D) { return att_warps(D) / (D / 128); }   // tile streams per CTA
 
 // TQ3 code pairs -> byte address in the codebook table: pair i of a 24-bit group word
 // (codes 2i, 2i+1) indexes row ((w >> 6i) & 63), TQ3 half of the row (byte 128 + 4 * lane).
@@ -341,6 +342,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
     using Cfg = AttnCfg<D, KT>;
     constexpr int WARPS = Cfg::WARPS, THREADS = Cfg::THREADS;
     constexpr int SPLIT = Cfg::SPLIT, RINGS = Cfg::RINGS, NBLK = Cfg::NBW;   // NBLK: this warp's blocks
+    static_assert(att_rings(D) == RINGS && att_warps(D) == WARPS, "host plan and kernel disagree");
     constexpr int KBB = Cfg::KBB, KB = Cfg::KB, VB = Cfg::VB;
     constexpr int KTILE = Cfg::KTILE, STAGE = Cfg::STAGE;
     constexpr int NCH = Cfg::NCH, NMT = Cfg::NMT, SCR = Cfg::SCR;
@@ -940,7 +942,7 @@ AttnPlan attn_plan(int B, int Hkv, int D, int64_t cap, int64_t max_len) {
     p.lnom = (len + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
     if (p.lnom == 0) p.lnom = ATT_TILE;
     const int64_t total = pairs * p.lnom;
-    const int64_t unit = (int64_t)att_warps(D) * ATT_TILE;
+    const int64_t unit = (int64_t)att_rings(D) * ATT_TILE;   // one tile per ring
     const int sms = sm_count();
     int64_t chunk = (total + sms - 1) / sms;
     chunk = (chunk + unit - 1) / unit * unit;

@@ -214,6 +214,23 @@ def test_attention_head_dim_256(orc, kt, T, lens):
     print(f"D256 K TQ{kt} T {T}: rel err {rel:.3g}")
 
 
+@pytest.mark.parametrize("grp", [1, 2, 8])
+@pytest.mark.parametrize("kt", [4, 3])
+def test_attention_head_dim_256_grp(orc, kt, grp):
+    """head_dim 256 with GQA groups 1, 2 and 8 (group 4 above), f32 q, no rotation of q."""
+    B, Hkv, T, D = 2, 2, 700, 256
+    kc = make_cache(B, Hkv, T, D, 110 + grp, qtype=kt)
+    vc = make_cache(B, Hkv, T, D, 120 + grp)
+    q = torch.randn(B, Hkv * grp, D, generator=torch.Generator().manual_seed(130 + grp))
+    lt = torch.tensor([T, 333], dtype=torch.int32)
+    for rotate in (True, False):
+        out, lse = attention.decode_attention(q.to(DEV), kc, vc, kv_len=lt.to(DEV), return_lse=True,
+                                              rotate_q=rotate)
+        ref, lref = orc.decode_attention(q.numpy(), kc.cpu().numpy(), kt, vc.cpu().numpy(), 4, Hkv,
+                                         kv_len=lt.numpy(), rotate_q=rotate, nthreads=8)
+        check(out.cpu().numpy(), ref, lse.cpu().numpy(), lref)
+
+
 @pytest.mark.parametrize("kt", [4, 3])
 def test_head_dim_256_many_segments_per_cta(kt):
     """head_dim 256 with 416 (sequence, KV head) pairs of 590-700 tokens: every CTA runs

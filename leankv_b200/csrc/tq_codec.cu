@@ -380,10 +380,15 @@ __device__ __forceinline__ double tq3_opt_refine(const float (&v)[QK], uint32_t 
             const double xd = (double)v[j];
             const double Cd = fma(xd, e.x, C), Ad = A + e.y;
             const double Cu = fma(xd, e.z, C), Au = A + e.w;
-            const bool acc_dn = i > 0 && Cd * Cd * A > E * Ad;          // lower neighbour first
-            const bool acc_up = !acc_dn && i < 7 && Cu * Cu * A > E * Au;
-            if (acc_dn) { C = Cd; A = Ad; E = Cd * Cd; idx[j] = i - 1; improved = true; }
-            if (acc_up) { C = Cu; A = Au; E = Cu * Cu; idx[j] = i + 1; improved = true; }
+            // A missing neighbour (code 0 down, code 7 up) has dL = dLL = 0, so its test reads
+            // (C * C) * A > E * A with E == C * C bit for bit, which is false: no range check.
+            const bool acc_dn = Cd * Cd * A > E * Ad;          // lower neighbour first
+            const bool acc_up = !acc_dn && Cu * Cu * A > E * Au;
+            C = acc_dn ? Cd : (acc_up ? Cu : C);
+            A = acc_dn ? Ad : (acc_up ? Au : A);
+            E = C * C;   // the accepted Cd * Cd (or Cu * Cu), or the unchanged C * C
+            idx[j] = i + (int)acc_up - (int)acc_dn;
+            improved |= acc_dn | acc_up;
         }
         if (!improved) break;
     }

@@ -318,7 +318,7 @@ class Attn:
     Both keep the total work fixed as ranks are added ("strong" scaling).
     """
 
-    def __init__(self, name, rank, ws, tokens=None):
+    def __init__(self, name, rank, ws, tokens=None, transport="nccl"):
         import torch
         from leankv_b200 import attention, distributed, ops
         self.attention = attention
@@ -348,7 +348,7 @@ class Attn:
         self.L = L
         self.split = name == "c4" and ws > 1
         if self.split:
-            self.att = distributed.SplitSequenceAttention()
+            self.att = distributed.SplitSequenceAttention(transport=transport)
             self.lens = torch.full((Bl,), L, dtype=torch.int32, device="cuda")
         kv_bytes = kc.numel() + vc.numel()
         self.bytes_per_step = kv_bytes + self.q.numel() * 2 + self.out.numel() * 2          # this rank
@@ -365,8 +365,10 @@ class Attn:
         else:
             self.config = {"workload": WORKLOAD["c4"],
                            "shape": f"B={B} Hq={Hq} Hkv={Hkv} D={D} ctx={T}, fp16 q/out", "kv_bytes": kv_total}
-            self.parallelism = (f"token shards x{ws} ({L} tokens per rank); all_gather of packed (O, lse) over NCCL "
-                                "+ LSE merge on every rank" if ws > 1 else "one GPU holds the whole context")
+            self.parallelism = (f"token shards x{ws} ({L} tokens per rank); " + (
+                "all_gather of packed (O, lse) over NCCL + LSE merge on every rank" if transport == "nccl" else
+                "one kernel per rank: (O, lse) stored into every rank's buffer over NVLink (CUDA IPC peer stores), "
+                "system-scope arrival counts, LSE merge") if ws > 1 else "one GPU holds the whole context")
         self.dtype = "TQ blocks -> f16 MMA, f32 accumulate"
         self.e2e_path = "leankv_b200 decode attention, q H2D and out D2H from pinned host memory"
 
@@ -553,9 +555,9 @@ class Stream:
                 "append's quantize is the reference hadamard_transform_row + quantize_row_tq4_0 (timed in tq4)")
 
 
-def make_workload(name, rank, tokens, ws=1, layers=None):
+def make_workload(name, rank, tokens, ws=1, layers=None, transport="nccl"):
     if name in ("attn", "c4"):
-        return Attn(name, rank, ws, tokens)
+        return Attn(name, rank, ws, tokens, transport)
     if name == "c5":
         return Stream(rank, ws, tokens, layers)
     return Codec(name, rank, tokens)
@@ -563,7 +565,7 @@ def make_workload(name, rank, tokens, ws=1, layers=None):
 
 def run_ours(args, ws, rank, local):
     import torch
-    wl = make_workload(args.workload, rank, args.tokens, ws, args.layers)
+    wl = make_workload(args.workload, rank, args.tokens, ws, args.layers, args.transport)
     if isinstance(wl, Stream):
         budget = wl.remaining() - (0 if args.no_e2e else min(args.steps, 20) + 1)
         if args.warmup + args.steps > budget:
@@ -660,6 +662,8 @@ def run_ours(args, ws, rank, local):
             "wall_s_timed_region": round(wall, 4),
             "cpu_baseline": cpu,
         }
+    if getattr(wl, "att", None) is not None and hasattr(wl.att, "close"):
+        wl.att.close()   # peer exchange buffers (collective; a no-op for the NCCL transport)
     return out
 
 
@@ -759,6 +763,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-API measurement (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the token count (profiling runs)")
+    ap.add_argument("--transport", choices=["peer", "nccl"], default="nccl",
+                    help="c4 on N > 1 GPUs: rank exchange through NVLink peer memory or NCCL all_gather")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 3 if args.impl == "reference" else {"attn": 200, "c4": 50, "c5": 40}.get(args.workload, 2000)

@@ -309,6 +309,43 @@ tq_status tq_lse_merge_cuda(int n_parts, int64_t n_rows, int head_dim, const flo
                             const float *lse, int64_t lse_part_stride, void *out, tq_dtype out_dtype,
                             float *lse_out, void *stream);
 
+/* ── split-sequence merge over peer memory (one process per GPU, one node) ──
+ *
+ * The exchange step of the multi-GPU split-KV decode as one kernel, without a
+ * collective library.  Every rank's kernel stores its packed partial
+ * [o (n_rows x head_dim floats) | lse (n_rows floats)] into its slot of every
+ * rank's exchange buffer (peer stores over NVLink), publishes it with a
+ * system-scope fence and one 64-bit atomic increment per CTA on every rank's
+ * arrival counter, waits (bounded) until its own counter shows the partials
+ * of all ranks for this step, and merges them in rank order with the
+ * arithmetic of tq_lse_merge_cuda.  No counterpart in the reference.
+ *
+ * Setup: every rank calls tq_peer_exchange_create with the same world,
+ * n_rows and head_dim, shares the TQ_PEER_HANDLE_BYTES handle it returns with
+ * all ranks (any host channel), then calls tq_peer_exchange_connect with the
+ * handles of all ranks in rank order.  Steps: every rank calls
+ * tq_peer_exchange_merge once per step, in the same order; the ranks run on
+ * distinct GPUs of one node (the kernel of one rank waits for the kernels of
+ * the others).  The exchange buffer holds two steps (alternating), so a rank
+ * can run one step ahead of another.  A step whose wait runs out (about two
+ * seconds) records TQ_ERROR_TIMEOUT, read by tq_peer_exchange_status, and
+ * leaves the exchange unusable.  Teardown: tq_peer_exchange_disconnect on
+ * every rank, a host barrier, then tq_peer_exchange_destroy.  Not for CUDA
+ * graph capture: each call passes its step number to the kernel.
+ */
+typedef struct tq_peer_exchange tq_peer_exchange;
+#define TQ_PEER_HANDLE_BYTES 64
+#define TQ_PEER_MAX_WORLD 64
+tq_status tq_peer_exchange_create(int world, int rank, int64_t n_rows, int head_dim, tq_peer_exchange **ex,
+                                  void *handle_out);
+tq_status tq_peer_exchange_connect(tq_peer_exchange *ex, const void *handles);
+tq_status tq_peer_exchange_merge(tq_peer_exchange *ex, const float *part, void *out, tq_dtype out_dtype,
+                                 float *lse_out, void *stream);
+/* synchronizes the stream, then returns the kernel-side status of the steps so far */
+tq_status tq_peer_exchange_status(tq_peer_exchange *ex, void *stream);
+tq_status tq_peer_exchange_disconnect(tq_peer_exchange *ex);
+tq_status tq_peer_exchange_destroy(tq_peer_exchange *ex);
+
 #ifdef __cplusplus
 }
 #endif

@@ -19,6 +19,7 @@ STATUS_NAMES = {0: "TQ_SUCCESS", 1: "TQ_ERROR_INVALID_VALUE", 2: "TQ_ERROR_UNSUP
                 4: "TQ_ERROR_CUDA", 5: "TQ_ERROR_OUT_OF_MEMORY", 6: "TQ_ERROR_NO_DEVICE", 7: "TQ_ERROR_TIMEOUT"}
 # tq_dtype / tq_type
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+TQ_PEER_HANDLE_BYTES = 64   # bytes of a tq_peer_exchange_create handle
 TYPE_TQ2_0, TYPE_TQ3_0, TYPE_TQ4_0 = 2, 3, 4
 BLOCK_BYTES = {TYPE_TQ2_0: 10, TYPE_TQ3_0: 14, TYPE_TQ4_0: 18}
 QK = 32
@@ -96,6 +97,13 @@ SIGNATURES = {
     "tq_proto_decode_cuda": (_i32, [_v, _v, _i64, _i32, _i32, _v, _v, _i32, _v, _i32, _v, _v, _v]),
     # KV-cache append
     "tq_kv_append_cuda": (_i32, [_i32, _v, _i32, _v, _i32, _i32, _i32, _i64, _i64, _v, _i32, _i32, _v, _v]),
+    # split-sequence merge over peer memory (exchange handles are opaque pointers)
+    "tq_peer_exchange_create": (_i32, [_i32, _i32, _i64, _i32, _v, _v]),
+    "tq_peer_exchange_connect": (_i32, [_v, _v]),
+    "tq_peer_exchange_merge": (_i32, [_v, _v, _v, _i32, _v, _v]),
+    "tq_peer_exchange_status": (_i32, [_v, _v]),
+    "tq_peer_exchange_disconnect": (_i32, [_v]),
+    "tq_peer_exchange_destroy": (_i32, [_v]),
 }
 
 

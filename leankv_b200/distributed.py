@@ -18,17 +18,27 @@ The decode attention divides two ways:
   which is NCCL over NVLink on a B200 node.  Each rank then merges the P partials
   itself (tq_lse_merge_cuda), so every rank ends up holding the full output.
 
+  ``transport="peer"`` replaces the all_gather and the merge by one kernel per
+  rank (tq_peer_exchange_merge): it stores the rank's partial into every rank's
+  exchange buffer over NVLink (CUDA IPC mappings, plain peer stores), counts
+  its arrival with system-scope atomics, waits (bounded) for all ranks' partials
+  and merges them with the same arithmetic, so both transports give identical
+  outputs.  It needs one GPU per rank on one node.
+
 The output rotation (FWHT) is linear and is applied inside each rank's partial;
 the merge is a convex combination, so it commutes with the rotation.
 """
 from __future__ import annotations
 
+import ctypes as C
 from typing import Callable
 
 import torch
 import torch.distributed as dist
 
+from . import _lib as L
 from . import attention
+from .ops import _DTYPES, _stream
 
 
 def batch_shard(batch: int, rank: int, world: int) -> tuple[int, int]:
@@ -60,6 +70,66 @@ def local_lengths(kv_len: torch.Tensor, start: int, stop: int) -> torch.Tensor:
     return (kv_len.to(torch.int64) - start).clamp_(0, stop - start).to(torch.int32)
 
 
+class PeerExchange:
+    """Exchange buffers of one rank for tq_peer_exchange_merge (CUDA IPC over NVLink).
+
+    Created collectively: every rank of `group` allocates its buffer, the IPC
+    handles are all-gathered over the process group (host objects), and every
+    rank maps the others'.  `merge(part, out, lse_out)` then runs one step on the
+    current stream; every rank must call it the same number of times, in order.
+    `close()` unmaps, waits for all ranks, and frees (collective as well).
+    """
+
+    def __init__(self, n_rows: int, head_dim: int, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.n_rows, self.head_dim = n_rows, head_dim
+        dev = torch.cuda.current_device()
+        if self.world > 1:
+            # the kernel of one rank waits for the kernels of the others: one GPU per rank
+            ids = [None] * self.world
+            dist.all_gather_object(ids, (str(torch.cuda.get_device_properties(dev).uuid), dev), group=group)
+            if len({i[0] for i in ids}) != self.world:
+                raise ValueError("the peer exchange needs a distinct GPU for every rank")
+        lib = L.load()
+        self._ex = C.c_void_p()
+        handle = C.create_string_buffer(L.TQ_PEER_HANDLE_BYTES)
+        L.check(lib.tq_peer_exchange_create(self.world, self.rank, n_rows, head_dim, C.byref(self._ex), handle))
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, handle.raw, group=group)
+        else:
+            handles[0] = handle.raw
+        L.check(lib.tq_peer_exchange_connect(self._ex, b"".join(handles)))
+
+    def merge(self, part: torch.Tensor, out: torch.Tensor, lse_out: torch.Tensor | None = None) -> torch.Tensor:
+        n, D = self.n_rows, self.head_dim
+        if part.dtype != torch.float32 or part.numel() != n * (D + 1) or not part.is_contiguous():
+            raise ValueError("part must be a contiguous float32 [n_rows * (head_dim + 1)] tensor")
+        if out.numel() != n * D or not out.is_contiguous() or out.dtype not in _DTYPES:
+            raise ValueError("out must be a contiguous [n_rows, head_dim] float32 / float16 / bfloat16 tensor")
+        L.check(L.load().tq_peer_exchange_merge(self._ex, part.data_ptr(), out.data_ptr(), _DTYPES[out.dtype],
+                                                lse_out.data_ptr() if lse_out is not None else None,
+                                                _stream(part)))
+        return out
+
+    def status(self) -> None:
+        """Synchronize the current stream and raise if a step's wait ran out."""
+        L.check(L.load().tq_peer_exchange_status(self._ex, torch.cuda.current_stream().cuda_stream))
+
+    def close(self) -> None:
+        if not self._ex:
+            return
+        lib = L.load()
+        torch.cuda.synchronize()
+        L.check(lib.tq_peer_exchange_disconnect(self._ex))
+        if self.world > 1:
+            dist.barrier(group=self.group)   # no rank frees its buffer while another still maps it
+        L.check(lib.tq_peer_exchange_destroy(self._ex))
+        self._ex = C.c_void_p()
+
+
 class SplitSequenceAttention:
     """Decode attention over contexts split across ranks by token position.
 
@@ -71,10 +141,17 @@ class SplitSequenceAttention:
     ``attend(q, k, v, kv_len, max_kv_len, o_out, lse_out)`` and
     ``merge(parts, n_parts, n_rows, head_dim, out)`` default to the CUDA
     kernels; they are parameters so that the exchange logic can run on CPU ranks
-    (gloo) with CPU stand-ins.
+    (gloo) with CPU stand-ins.  ``transport``: "nccl" (all_gather over the
+    process group, then the merge kernel) or "peer" (PeerExchange: one kernel
+    over NVLink peer memory; call ``close()`` on every rank when done).
     """
 
-    def __init__(self, group=None, attend: Callable | None = None, merge: Callable | None = None):
+    def __init__(self, group=None, attend: Callable | None = None, merge: Callable | None = None,
+                 transport: str = "nccl"):
+        if transport not in ("nccl", "peer"):
+            raise ValueError("transport must be 'nccl' or 'peer'")
+        self.transport = transport
+        self._peers: dict = {}
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
@@ -108,9 +185,27 @@ class SplitSequenceAttention:
         self._attend(q, k_shard, v_shard, kv_len_local, max_kv_len, o_local, lse_local, **kw)
         if out is None:
             out = torch.empty((B, Hq, D), dtype=out_dtype, device=q.device)
+        if self.transport == "peer":
+            key = (n, D, str(q.device))
+            ex = self._peers.get(key)
+            if ex is None:
+                ex = self._peers[key] = PeerExchange(n, D, self.group)
+            ex.merge(send, out.view(n, D))
+            return out
         if self.world == 1:
             self._merge(send, 1, n, D, out.view(n, D))
             return out
         dist.all_gather_into_tensor(recv, send, group=self.group)
         self._merge(recv, self.world, n, D, out.view(n, D))
         return out
+
+    def status(self) -> None:
+        """Peer transport: synchronize and raise if a step's wait ran out."""
+        for ex in self._peers.values():
+            ex.status()
+
+    def close(self) -> None:
+        """Release the peer exchanges (collective: every rank calls it)."""
+        for key in sorted(self._peers):
+            self._peers[key].close()
+        self._peers.clear()

@@ -145,3 +145,24 @@ def ctypes_sizeof_matches_c(tmp=None):
         sz, off_ws, off_sc = map(int, subprocess.run([exe], capture_output=True, text=True).stdout.split())
     return (sz == C.sizeof(A.AttnArgs) and off_ws == A.AttnArgs.workspace_bytes.offset
             and off_sc == A.AttnArgs.sm_scale.offset)
+
+
+@pytest.mark.parametrize("args", [(0, 0, 8, 128), (65, 0, 8, 128), (2, 2, 8, 128), (2, -1, 8, 128),
+                                  (2, 0, 0, 128), (2, 0, 8, 0)])
+def test_peer_exchange_argument_errors(args):
+    """Bad world / rank / sizes are rejected before any CUDA call (runs without a GPU)."""
+    import ctypes
+    lib = L.load()
+    ex = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(L.TQ_PEER_HANDLE_BYTES)
+    assert lib.tq_peer_exchange_create(*args, ctypes.byref(ex), handle) == 1
+    assert not ex.value
+    assert lib.tq_peer_exchange_merge(None, None, None, 0, None, None) == 1
+    assert lib.tq_peer_exchange_connect(None, None) == 1
+    assert lib.tq_peer_exchange_destroy(None) == 0
+
+
+def test_split_sequence_transport_name():
+    from leankv_b200.distributed import SplitSequenceAttention
+    with pytest.raises(ValueError, match="transport"):
+        SplitSequenceAttention(transport="mpi")

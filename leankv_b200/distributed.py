@@ -96,12 +96,17 @@ class PeerExchange:
         self._ex = C.c_void_p()
         handle = C.create_string_buffer(L.TQ_PEER_HANDLE_BYTES)
         L.check(lib.tq_peer_exchange_create(self.world, self.rank, n_rows, head_dim, C.byref(self._ex), handle))
-        handles = [None] * self.world
-        if self.world > 1:
-            dist.all_gather_object(handles, handle.raw, group=group)
-        else:
-            handles[0] = handle.raw
-        L.check(lib.tq_peer_exchange_connect(self._ex, b"".join(handles)))
+        try:
+            handles = [None] * self.world
+            if self.world > 1:
+                dist.all_gather_object(handles, handle.raw, group=group)
+            else:
+                handles[0] = handle.raw
+            L.check(lib.tq_peer_exchange_connect(self._ex, b"".join(handles)))
+        except BaseException:
+            lib.tq_peer_exchange_destroy(self._ex)   # unmaps what was mapped, frees this rank's buffer
+            self._ex = C.c_void_p()
+            raise
 
     def merge(self, part: torch.Tensor, out: torch.Tensor, lse_out: torch.Tensor | None = None) -> torch.Tensor:
         n, D = self.n_rows, self.head_dim

@@ -175,7 +175,9 @@ class SplitSequenceAttention:
         if b is None:
             per = n_rows * (head_dim + 1)
             send = torch.empty(per, dtype=torch.float32, device=device)
-            recv = torch.empty(self.world * per, dtype=torch.float32, device=device)
+            # the all_gather destination; the peer transport gathers into its own exchange buffers
+            recv = (torch.empty(self.world * per, dtype=torch.float32, device=device)
+                    if self.transport == "nccl" and self.world > 1 else None)
             b = self._bufs[key] = (send, recv)
         return b
 

@@ -763,7 +763,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-API measurement (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the token count (profiling runs)")
-    ap.add_argument("--transport", choices=["peer", "nccl"], default="nccl",
+    ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="c4 on N > 1 GPUs: rank exchange through NVLink peer memory or NCCL all_gather")
     args = ap.parse_args()
     if args.steps is None:

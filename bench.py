@@ -4,17 +4,20 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
 Workloads (synthetic, seeded; shapes and distributions of the LeanKV configs):
-  tq3opt  (default) TQ3_0 + optimal rounding (2 CD passes + LS scale), FWHT fused,
+  c4      (default) fused decode attention over a TQ3_0 K / TQ4_0 V cache, B64 Hq64 Hkv8 D128,
+          context 131072; N > 1 ranks split every context by token position and merge the
+          (O, lse) partials over NVLink (peer-memory kernel up to 4 GPUs, NCCL all_gather above)
+  tq3opt  TQ3_0 + optimal rounding (2 CD passes + LS scale), FWHT fused,
           bf16 [32768 tokens, 8 KV heads, 128]: Student-t(4) x per-channel log-normal scales
   tq4     TQ4_0 quantize (FWHT fused) + dequantize of fp32 [4096, 8, 128], N(0,1) with
           4 outlier channels per head x20
-  attn    fused TQ4/TQ4 decode attention, B16 Hq32 Hkv8 D128 ctx 32768 (see leankv_b200.attention)
+  attn    fused TQ4/TQ4 decode attention, B16 Hq32 Hkv8 D128 ctx 32768 (ranks split the batch)
+  c5      streaming append + decode, 80 layers, head_dim 256, 256 decode steps (ranks split the batch)
 
-A step is one launch of the hot path over one batch that is resident in HBM.
-`value` is whole-job throughput (all ranks); `e2e` is the same metric through the
-C-ABI host-pointer API (pinned host buffers, H2D + D2H inside the timed region).
-One process per GPU (torchrun for N > 1); the codec shards by token rows with
-no collective ("weak" scaling).
+A step is one pass of the hot path over one batch that is resident in HBM.
+`value` is whole-job throughput (all ranks, GB/s of packed KV read for the attention
+workloads); `e2e` is the same metric through the public API with host buffers (H2D + D2H
+inside the timed region).  One process per GPU (torchrun for N > 1).
 """
 from __future__ import annotations
 
@@ -278,23 +281,6 @@ class Codec:
             h2d, d2h = h2d + self.hy.numel(), d2h + self.hxr.numel() * 4
         return h2d, d2h
 
-    # CPU baseline on a bounded sample of the same workload
-    def cpu_run(self, frac_tokens: int, nthreads: int, impl: str):
-        import numpy as np
-        from oracle import oracle as O
-        tokens = self.x.shape[0] // frac_tokens
-        xs = self.x[:tokens].reshape(tokens, -1)
-        if self.x.dtype == __import__("torch").bfloat16:
-            arr = xs.view(__import__("torch").int16).cpu().numpy().view(np.uint16)
-        else:
-            arr = xs.cpu().numpy()
-        t0 = time.perf_counter()
-        blocks = O.parallel_quantize(arr, self.qtype, self.hd, nthreads, impl=impl, opt_passes=self.passes)
-        if self.round_trip:
-            O.parallel_dequantize(blocks, self.qtype, arr.shape[1], nthreads)
-        dt = time.perf_counter() - t0
-        sample_bytes = self.bytes_per_step / frac_tokens
-        return sample_bytes / dt / 1e9, tokens
 
 
 def _outlier_rows(g, shape, hd):
@@ -392,19 +378,6 @@ class Attn:
     def e2e_bytes(self):
         return self.hq.numel() * 2, self.hout.numel() * 2
 
-    def cpu_run(self, frac, nthreads, impl):
-        from oracle import oracle as O
-        n = 1
-        q = self.q[:n].float().cpu().numpy()
-        kc, vc = self.kc[:n].cpu().numpy(), self.vc[:n].cpu().numpy()
-        t0 = time.perf_counter()
-        O.decode_attention(q, kc, 4 if kc.shape[-1] == 18 else 3, vc, 4, self.kc.shape[1], nthreads=nthreads)
-        dt = time.perf_counter() - t0
-        return self.bytes_per_step * n / self.q.shape[0] / dt / 1e9, n
-
-    def cpu_sample_note(self, n, nthreads):
-        return (f"{n} of {self.q.shape[0]} sequences, {nthreads} threads; float64 restatement: reference "
-                "dequantize_row_tq*_0 + hadamard_transform + exact softmax (no reference CPU attention exists)")
 
 
 class Stream:
@@ -417,7 +390,8 @@ class Stream:
     and replayed; the append slots and lengths live on the device and advance inside the graph.
     Ranks split the batch of 32 ("strong" scaling, no collective).
     """
-    LAYERS, HKV, HQ, D, BATCH, GROWTH = 80, 8, 32, 256, 32, 256
+    LAYERS, HKV, HQ, D, BATCH, DECODE_STEPS = 80, 8, 32, 256, 32, 256
+    GROWTH = DECODE_STEPS + 32            # + warm-up and end-to-end steps; capacity stays even
 
     def __init__(self, rank, ws, tokens=None, layers=None):
         import torch
@@ -537,22 +511,6 @@ class Stream:
     def e2e_bytes(self):
         return (self.hk.numel() + self.hv.numel() + self.hq.numel()) * 2, self.hout.numel() * 2
 
-    def cpu_run(self, frac, nthreads, impl):
-        """One layer of one sequence of the decode step on the host (float64 restatement), scaled per byte."""
-        from oracle import oracle as O
-        ctx = int(self.len1[0].item())
-        kc = self.kc[0][:1, :, :ctx].cpu().numpy()
-        vc = self.vc[0][:1, :, :ctx].cpu().numpy()
-        q = self.q[0][:1].float().cpu().numpy()
-        t0 = time.perf_counter()
-        O.decode_attention(q, kc, 4, vc, 4, self.HKV, nthreads=nthreads)
-        dt = time.perf_counter() - t0
-        return (kc.size + vc.size) / dt / 1e9, 1
-
-    def cpu_sample_note(self, n, nthreads):
-        return (f"attention of 1 layer x 1 sequence at the current context, {nthreads} threads, GB/s of cache read; "
-                "float64 restatement (reference dequantize_row_tq4_0 + hadamard_transform + exact softmax); the "
-                "append's quantize is the reference hadamard_transform_row + quantize_row_tq4_0 (timed in tq4)")
 
 
 def make_workload(name, rank, tokens, ws=1, layers=None, transport="nccl"):
@@ -561,6 +519,90 @@ def make_workload(name, rank, tokens, ws=1, layers=None, transport="nccl"):
     if name == "c5":
         return Stream(rank, ws, tokens, layers)
     return Codec(name, rank, tokens)
+
+
+# ── CPU baselines: one host-side sample per workload, used by both the cpu_baseline leg of
+# this arm and the --impl reference arm, so the two report the same work ─────────────────
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+NOTE_ATT = ("float64 restatement (reference dequantize_row_tq*_0 + hadamard_transform + exact softmax); "
+            "no reference CPU attention exists in-tree")
+
+
+def _ref_cache(rng, O, qtype, hkv, ctx, d):
+    """K or V of one sequence as the reference C writes it: N(0,1) with 4 outlier channels x20,
+    hadamard_transform_row over head_dim, quantize_row_tq*_0; [1, hkv, ctx, d/32, block bytes]."""
+    import numpy as np
+    x = rng.standard_normal((hkv, ctx, d), dtype=np.float32)
+    for h in range(hkv):
+        x[h, :, rng.permutation(d)[:4]] *= 20.0
+    bb = O.BLOCK_BYTES[qtype]
+    return O.ref_quantize(qtype, O.ref_fwht(x, d)).reshape(1, hkv, ctx, d // 32, bb)
+
+
+def cpu_sample(wl: str, nthreads: int):
+    """(fn, bytes, kind, sample note) of a bounded host sample of workload `wl`: the inputs are made on
+    the host by a seeded generator with the workload's shape and distribution, and fn() runs the
+    reference's CPU path (or its C restatement where the reference has none) on `nthreads` threads."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    rng = np.random.default_rng(3)
+    if wl in ("attn", "c4", "c5"):
+        # one sequence (of one layer for C5); the C4 context is cut to 1/8 to keep a step bounded
+        Hq, Hkv, D, T, kt = {"attn": (32, 8, 128, 32768, 4), "c4": (64, 8, 128, 131072 // 8, 3),
+                             "c5": (32, 8, 256, 16384, 4)}[wl]
+        kc, vc = _ref_cache(rng, O, kt, Hkv, T, D), _ref_cache(rng, O, 4, Hkv, T, D)
+        q = rng.standard_normal((1, Hq, D), dtype=np.float32)
+        nbytes = kc.size + vc.size + (q.size * 2 * 2 if wl != "c5" else 0)
+        fn = lambda: O.decode_attention(q, kc, kt, vc, 4, Hkv, nthreads=nthreads)  # noqa: E731
+        sample = {"attn": "1 of the 16 sequences per step; ",
+                  "c4": "1 of the 64 sequences at 1/8 of the context per step; ",
+                  "c5": "1 layer x 1 sequence of the decode step at context 16384, GB/s of cache read; "}[wl] + NOTE_ATT
+        return fn, nbytes, "port", sample
+    if wl == "tq3opt":
+        tokens = 32768 // 16
+        g = torch.Generator().manual_seed(2)
+        # the workload's distribution: Student-t(4) = N / sqrt(chi2_4 / 4) x log-normal channel scales
+        nrm = torch.randn(tokens, 8, 128, generator=g)
+        chi = sum(torch.randn(tokens, 8, 128, generator=g) ** 2 for _ in range(4))
+        x = (nrm / torch.sqrt(chi / 4.0)) * torch.exp(torch.randn(1, 8, 128, generator=g))
+        arr = x.reshape(tokens, -1).to(torch.bfloat16).view(torch.int16).numpy().view("uint16")
+        nbytes = arr.size * 2 + arr.size // 32 * 14
+        fn = lambda: O.parallel_quantize(arr, 3, 128, nthreads, impl="port", opt_passes=2)  # noqa: E731
+        return fn, nbytes, "port", (f"{tokens} of 32768 tokens per step; C restatement of "
+                                    "scripts/tq3_rounding.py (no reference C exists) + reference hadamard_transform_row")
+    tokens = 4096
+    x = rng.standard_normal((tokens, 8, 128), dtype=np.float32)
+    for h in range(8):
+        x[:, h, rng.permutation(128)[:4]] *= 20.0
+    arr = np.ascontiguousarray(x.reshape(tokens, -1))
+    nbytes = 2 * (arr.size * 4 + arr.size // 32 * 18)
+    fn = lambda: O.parallel_dequantize(O.parallel_quantize(arr, 4, 128, nthreads, impl="reference"),  # noqa: E731
+                                       4, arr.shape[1], nthreads)
+    return fn, nbytes, "reference", ("full [4096, 8, 128] per step; src/ggml-tq.c hadamard_transform_row + "
+                                     "quantize_row_tq4_0 + dequantize_row_tq4_0")
+
+
+def time_cpu_sample(wl: str, nthreads: int, warmup: int = 1, steps: int = 1):
+    fn, nbytes, kind, sample = cpu_sample(wl, nthreads)
+    for _ in range(warmup):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        fn()
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": round(nbytes / dt / 1e9, 4), "unit": "GB/s", "cores": nthreads, "cpu_model": cpu_model(),
+            "kind": kind, "sample": sample, "ms_per_sample": round(dt * 1e3, 3)}
 
 
 def run_ours(args, ws, rank, local):
@@ -619,24 +661,23 @@ def run_ours(args, ws, rank, local):
                "path": getattr(wl, "e2e_path", "tq_quantize_host (C ABI, pinned host buffers)"),
                "steps": n_e2e}
 
+    # a peer-transport step whose wait ran out leaves its output unmerged: check every rank's status
+    # (it synchronizes) before any number is reported, and fail the line on an error
+    peer_error = None
+    if getattr(wl, "att", None) is not None and hasattr(wl.att, "status"):
+        try:
+            wl.att.status()
+        except Exception as e:   # TQError
+            peer_error = str(e)
+    # every rank learns whether any rank failed, so all take the same exit path
+    if max_over_ranks(1.0 if peer_error is not None else 0.0, ws) > 0 and peer_error is None:
+        peer_error = "another rank's peer exchange wait ran out"
+
     out = None
-    if rank == 0:
+    if rank == 0 and peer_error is None:
         cpu = None
         if ws == 1 and not args.no_cpu_baseline:
-            n = os.cpu_count() or 1
-            if isinstance(wl, (Attn, Stream)):
-                v, nseq = wl.cpu_run(16, n, "port")
-                cpu = {"value": round(v, 4), "unit": "GB/s", "cores": n, "kind": "port",
-                       "sample": wl.cpu_sample_note(nseq, n)}
-            else:
-                impl = "port" if wl.passes else "reference"
-                v, tokens = wl.cpu_run(16, n, impl)
-                cpu = {"value": round(v, 4), "unit": "GB/s", "cores": n,
-                       "kind": "port" if wl.passes else "reference",
-                       "sample": f"{tokens} of {wl.x.shape[0]} tokens (1/16 of the workload), {n} threads; "
-                                 + ("C restatement of scripts/tq3_rounding.py + reference hadamard_transform_row"
-                                    if wl.passes else "reference src/ggml-tq.c hadamard_transform_row + quantize_row"
-                                    + (" + dequantize_row" if getattr(wl, "round_trip", False) else ""))}
+            cpu = time_cpu_sample(args.workload, os.cpu_count() or 1)
         is_codec = isinstance(wl, Codec)
         out = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
@@ -664,91 +705,44 @@ def run_ours(args, ws, rank, local):
         }
     if getattr(wl, "att", None) is not None and hasattr(wl.att, "close"):
         wl.att.close()   # peer exchange buffers (collective; a no-op for the NCCL transport)
+    if peer_error is not None:
+        raise SystemExit(f"peer exchange failed during the timed or e2e steps: {peer_error}")
     return out
-
-
-def _ref_cache(rng, O, qtype, hkv, ctx, d):
-    """K or V of one sequence as the reference C writes it: N(0,1) with 4 outlier channels x20,
-    hadamard_transform_row over head_dim, quantize_row_tq*_0; [1, hkv, ctx, d/32, block bytes]."""
-    import numpy as np
-    x = rng.standard_normal((hkv, ctx, d), dtype=np.float32)
-    for h in range(hkv):
-        x[h, :, rng.permutation(d)[:4]] *= 20.0
-    bb = O.BLOCK_BYTES[qtype]
-    return O.ref_quantize(qtype, O.ref_fwht(x, d)).reshape(1, hkv, ctx, d // 32, bb)
 
 
 def run_reference(args, ws, rank):
     """The reference's CPU implementation of the path on this host's cores, on a bounded sample of
-    the same workload (same config, metric and unit as this repository's arm; inputs made on the
-    host by the reference C, nothing of this repository's GPU path involved)."""
+    the same workload (same config, metric and unit as this repository's arm; the same host sample
+    as this arm's cpu_baseline leg; nothing of this repository's GPU path involved)."""
     if rank != 0:
         return None
-    import numpy as np
-    import torch
-    from oracle import oracle as O
     n = os.cpu_count() or 1
-    torch.manual_seed(0)
-    rng = np.random.default_rng(3)
     wl = args.workload
+    fn, nbytes, kind, sample = cpu_sample(wl, n)
     config = {"workload": WORKLOAD[wl]}
-    scaling = "weak" if wl in ("tq3opt", "tq4") else "strong"
-    note_att = ("float64 restatement (reference dequantize_row_tq*_0 + hadamard_transform + exact softmax); "
-                "no reference CPU attention exists in-tree")
     if wl in ("attn", "c4", "c5"):
-        # one sequence (of one layer for C5), context shortened for C4 to keep a step bounded
-        Hq, Hkv, D, T, kt, seqs = {"attn": (32, 8, 128, 32768, 4, 16), "c4": (64, 8, 128, 131072 // 8, 3, 64),
-                                   "c5": (32, 8, 256, 16384, 4, 32)}[wl]
-        kc, vc = _ref_cache(rng, O, kt, Hkv, T, D), _ref_cache(rng, O, 4, Hkv, T, D)
-        q = rng.standard_normal((1, Hq, D), dtype=np.float32)
-        bytes_ = kc.size + vc.size + (q.size * 2 * 2 if wl != "c5" else 0)
-        fn = lambda: O.decode_attention(q, kc, kt, vc, 4, Hkv, nthreads=n)  # noqa: E731
         config["shape"] = {"attn": "B=16 Hq=32 Hkv=8 D=128 ctx=32768, fp16 q/out",
                            "c4": "B=64 Hq=64 Hkv=8 D=128 ctx=131072, fp16 q/out",
                            "c5": "batch 32 (x1 ranks: 32 each) Hkv=8 Hq=32 D=256 prefill 16384 + up to 256 "
                                  "appended tokens, bf16 inputs/outputs"}[wl]
-        sample = {"attn": "1 of the 16 sequences per step; ",
-                  "c4": "1 of the 64 sequences at 1/8 of the context per step; ",
-                  "c5": "1 layer x 1 sequence of the decode step at context 16384, GB/s of cache read; "}[wl] + note_att
-        kind = "port"
-    elif wl == "tq3opt":
-        tokens = 32768 // 16
-        # the workload's generator on the host: Student-t(4) = N / sqrt(chi2_4 / 4), log-normal channel scales
-        nrm = torch.randn(tokens, 8, 128)
-        chi = sum(torch.randn(tokens, 8, 128) ** 2 for _ in range(4))
-        x = (nrm / torch.sqrt(chi / 4.0)) * torch.exp(torch.randn(1, 8, 128))
-        arr = x.reshape(tokens, -1).to(torch.bfloat16).view(torch.int16).numpy().view("uint16")
-        bytes_ = arr.size * 2 + arr.size // 32 * 14
-        fn = lambda: O.parallel_quantize(arr, 3, 128, n, impl="port", opt_passes=2)  # noqa: E731
-        config["input"] = INPUT[wl]
-        kind, sample = "port", (f"{tokens} of 32768 tokens per step; C restatement of scripts/tq3_rounding.py "
-                                "(no reference C exists) + reference hadamard_transform_row")
     else:
-        tokens = 4096
-        x = rng.standard_normal((tokens, 8, 128), dtype=np.float32)
-        for h in range(8):
-            x[:, h, rng.permutation(128)[:4]] *= 20.0
-        arr = np.ascontiguousarray(x.reshape(tokens, -1))
-        bytes_ = 2 * (arr.size * 4 + arr.size // 32 * 18)
-        fn = lambda: O.parallel_dequantize(O.parallel_quantize(arr, 4, 128, n, impl="reference"),  # noqa: E731
-                                           4, arr.shape[1], n)
         config["input"] = INPUT[wl]
-        kind, sample = "reference", ("full [4096, 8, 128] per step; src/ggml-tq.c hadamard_transform_row + "
-                                     "quantize_row_tq4_0 + dequantize_row_tq4_0")
     config["parallelism"] = f"{n} host threads"
+    scaling = "weak" if wl in ("tq3opt", "tq4") else "strong"
     for _ in range(args.warmup):
         fn()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         fn()
     dt = (time.perf_counter() - t0) / args.steps
-    v = bytes_ / dt / 1e9
+    v = nbytes / dt / 1e9
     return {"metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None,
             "dtype": {"tq3opt": "bf16->u8", "tq4": "f32->u8->f32"}.get(wl, "f64"),
             "data": "synthetic (seeded)", "impl": "reference", "config": config,
-            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": n, "kind": kind, "sample": sample},
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": n, "cpu_model": cpu_model(),
+                             "kind": kind, "sample": sample},
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -758,19 +752,23 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["tq3opt", "tq4", "attn", "c4", "c5"], default="tq3opt")
+    ap.add_argument("--workload", choices=["tq3opt", "tq4", "attn", "c4", "c5"], default="c4")
     ap.add_argument("--layers", type=int, default=None, help="c5: override the layer count (profiling runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-API measurement (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the token count (profiling runs)")
-    ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
-                    help="c4 on N > 1 GPUs: rank exchange through NVLink peer memory or NCCL all_gather")
+    ap.add_argument("--transport", choices=["peer", "nccl"], default=None,
+                    help="c4 on N > 1 GPUs: rank exchange through NVLink peer memory or NCCL all_gather "
+                         "(default: peer up to 4 GPUs, where its parity and timeout tests ran; nccl above)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 3 if args.impl == "reference" else {"attn": 200, "c4": 50, "c5": 40}.get(args.workload, 2000)
+        args.steps = 3 if args.impl == "reference" else {"attn": 200, "c4": 50, "c5": Stream.DECODE_STEPS}.get(
+            args.workload, 2000)
     if args.warmup is None:
         args.warmup = 3 if args.impl == "reference" else {"c4": 5, "c5": 5}.get(args.workload, 20)
     args.warmup = max(args.warmup, 3)
+    if args.transport is None:
+        args.transport = "peer" if int(os.environ.get("WORLD_SIZE", "1")) <= 4 else "nccl"
 
     if args.impl == "reference":
         ws = int(os.environ.get("WORLD_SIZE", "1"))

@@ -327,17 +327,23 @@ tq_status tq_lse_merge_cuda(int n_parts, int64_t n_rows, int head_dim, const flo
  * tq_peer_exchange_merge once per step, in the same order; the ranks run on
  * distinct GPUs of one node (the kernel of one rank waits for the kernels of
  * the others).  The exchange buffer holds two steps (alternating), so a rank
- * can run one step ahead of another.  A step whose wait runs out (about two
- * seconds) records TQ_ERROR_TIMEOUT, read by tq_peer_exchange_status, and
- * leaves the exchange unusable.  Teardown: tq_peer_exchange_disconnect on
- * every rank, a host barrier, then tq_peer_exchange_destroy.  Not for CUDA
- * graph capture: each call passes its step number to the kernel.
+ * can run one step ahead of another.  wait_ms bounds each step's wait for the
+ * other ranks (0: 2000 ms); choose it above the longest delay expected between
+ * ranks (module loading, host work on one rank, SMs held by other streams).  A
+ * step whose wait runs out records TQ_ERROR_TIMEOUT, read by
+ * tq_peer_exchange_status, and leaves the exchange unusable: recovery is
+ * teardown plus a new exchange on every rank.  The kernel's grid is capped at
+ * the device's SM count, so all its CTAs are resident while they wait.
+ * Callers must check tq_peer_exchange_status before trusting an output.
+ * Teardown: tq_peer_exchange_disconnect on every rank, a host barrier, then
+ * tq_peer_exchange_destroy.  Not for CUDA graph capture: each call passes its
+ * step number to the kernel.
  */
 typedef struct tq_peer_exchange tq_peer_exchange;
 #define TQ_PEER_HANDLE_BYTES 64
 #define TQ_PEER_MAX_WORLD 64
-tq_status tq_peer_exchange_create(int world, int rank, int64_t n_rows, int head_dim, tq_peer_exchange **ex,
-                                  void *handle_out);
+tq_status tq_peer_exchange_create(int world, int rank, int64_t n_rows, int head_dim, uint32_t wait_ms,
+                                  tq_peer_exchange **ex, void *handle_out);
 tq_status tq_peer_exchange_connect(tq_peer_exchange *ex, const void *handles);
 tq_status tq_peer_exchange_merge(tq_peer_exchange *ex, const float *part, void *out, tq_dtype out_dtype,
                                  float *lse_out, void *stream);

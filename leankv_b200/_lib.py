@@ -98,7 +98,7 @@ SIGNATURES = {
     # KV-cache append
     "tq_kv_append_cuda": (_i32, [_i32, _v, _i32, _v, _i32, _i32, _i32, _i64, _i64, _v, _i32, _i32, _v, _v]),
     # split-sequence merge over peer memory (exchange handles are opaque pointers)
-    "tq_peer_exchange_create": (_i32, [_i32, _i32, _i64, _i32, _v, _v]),
+    "tq_peer_exchange_create": (_i32, [_i32, _i32, _i64, _i32, C.c_uint32, _v, _v]),
     "tq_peer_exchange_connect": (_i32, [_v, _v]),
     "tq_peer_exchange_merge": (_i32, [_v, _v, _v, _i32, _v, _v]),
     "tq_peer_exchange_status": (_i32, [_v, _v]),

@@ -35,6 +35,12 @@
 //   O^T = V^T P: M = 16 rows of one V block per m-tile (mt -> block mt/2),
 //     row r of m-tile mt is element 32*(mt/2) + 2*(r%8) + (mt%2) + 16*(r/8);
 //     K-chunk = the warp's 16 tokens.  The V block scales multiply P (fp16).
+//
+// Precision: the codebook tables hold alpha * level in fp16, with alpha chosen per codebook so
+// that every level rounds almost exactly (largest relative error 6.1e-5 for TQ4, 9.8e-6 for
+// TQ3, against 3.1e-4 and 6.4e-5 unscaled); 1 / alpha folds into the fp32 K block scales and
+// the final normalisation.  q~ is split into fp16 hi + lo parts and every score chunk runs two
+// MMAs (qh and ql against the same codebook fragments), so the query is exact to about 2^-22.
 #include <cstdint>
 #include <cstdio>
 #include <type_traits>
@@ -132,6 +138,19 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 #define LUT_SEL1 0x5514u
 #define LUT_SEL2 0x5524u
 #define LUT_SEL3 0x5534u
+
+// Codebook scales (fp32 constants found by search over [1, 2)): alpha * L rounds to fp16 with a
+// relative error of at most 6.05e-5 (TQ4) and 9.75e-6 (TQ3).
+constexpr float TQ4_ALPHA = 1.5976254940032959f;
+constexpr float TQ3_ALPHA = 1.7372877597808838f;
+
+// hi + lo fp16 parts of two floats: hi = fp16(a), lo = fp16(a - hi)
+__device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 f = __half22float2(h);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = pack_h2(a - f.x, b - f.y);
+}
 
 // ── query rotation and output merge helpers ──────────────────────────────────
 
@@ -369,9 +388,11 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
     }
     for (int i = threadIdx.x; i < 256 * 32; i += THREADS) {
         const int k = i >> 5, l = i & 31;
-        *reinterpret_cast<uint32_t*>(smem + (k << 8) + (l << 2)) = pack_h2(tq4_level(k & 15), tq4_level(k >> 4));
+        *reinterpret_cast<uint32_t*>(smem + (k << 8) + (l << 2)) =
+            pack_h2(TQ4_ALPHA * tq4_level(k & 15), TQ4_ALPHA * tq4_level(k >> 4));
         if (KT == 3 && k < 64)
-            *reinterpret_cast<uint32_t*>(smem + (k << 8) + 128 + (l << 2)) = pack_h2(tq3_level(k & 7), tq3_level(k >> 3));
+            *reinterpret_cast<uint32_t*>(smem + (k << 8) + 128 + (l << 2)) =
+                pack_h2(TQ3_ALPHA * tq3_level(k & 7), TQ3_ALPHA * tq3_level(k >> 3));
     }
     if (lane == 0 && half == 0)
         for (int s = 0; s < ATT_STAGES; ++s) {
@@ -481,7 +502,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         // q~ of this pair while the first tiles are in flight: warp h < 8 loads query head h of
         // the group (zeros past grp), rotates it and scales it into the (still unused) scale
         // scratch; every warp then builds its fp16 mma B fragments from there.
-        uint32_t qf[NCH][2];
+        uint32_t qf[NCH][2], qfl[NCH][2];   // fp16 hi and lo parts of q~ (mma B fragments)
         {
             constexpr int SQS = D + 4;   // row pitch: the fragment reads below are at most 2-way conflicted
             static_assert(ATT_N * SQS * 4 <= WARPS * 2 * SCR, "q~ must fit the scale scratch");
@@ -511,12 +532,12 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 const int blk = half * NBLK + (kk >> 1), h = kk & 1;   // block of the token row
                 if constexpr (KT == 4) {   // k-cols (2t, 2t+1) = elements (j, j+16), (2t+8, 2t+9) = (j+1, j+17)
                     const int e0 = 32 * blk + ((blk & 1) ? 4 * tq + 2 * h : 8 * h + 2 * tq);
-                    qf[kk][0] = pack_h2(mq[e0], mq[e0 + 16]);
-                    qf[kk][1] = pack_h2(mq[e0 + 1], mq[e0 + 17]);
+                    split_h2(mq[e0], mq[e0 + 16], qf[kk][0], qfl[kk][0]);
+                    split_h2(mq[e0 + 1], mq[e0 + 17], qf[kk][1], qfl[kk][1]);
                 } else {                   // TQ3 group t: codes 4h, 4h+1 | 4h+2, 4h+3 of group t
                     const int e0 = 32 * blk + 8 * tq + 4 * h;
-                    qf[kk][0] = pack_h2(mq[e0], mq[e0 + 1]);
-                    qf[kk][1] = pack_h2(mq[e0 + 2], mq[e0 + 3]);
+                    split_h2(mq[e0], mq[e0 + 1], qf[kk][0], qfl[kk][0]);
+                    split_h2(mq[e0 + 2], mq[e0 + 3], qf[kk][1], qfl[kk][1]);
                 }
             }
             __syncthreads();   // q~ read by all warps before the scale scratch is reused
@@ -539,7 +560,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 // as inf/nan in IEEE fp16, and P * d could overflow fp16: reported once per segment
                 bad_scale = max(bad_scale, (uint32_t)(h & 0x7FFFu));
                 if (!IS_V) {
-                    const float f = __half2float(__ushort_as_half(h));
+                    const float f = __half2float(__ushort_as_half(h)) * (1.0f / (KT == 4 ? TQ4_ALPHA : TQ3_ALPHA));
                     asm volatile("st.shared.f32 [%0], %1;" ::"r"(xs + xkd + rr * ROWSTEP * NBLK * 4), "f"(f));
                 } else {
                     constexpr int VDELTA = (((rr * ROWSTEP) & 7) >> 1) * NBLK * 8 + ((rr * ROWSTEP) >> 3) * 4;
@@ -570,11 +591,13 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
                     mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
+                    mma16816(acc, af, qfl[2 * blk][0], qfl[2 * blk][1]);
                     af[0] = lut_ld<RES>(w0, lane4, LUT_SEL2);
                     af[1] = lut_ld<RES>(w1, lane4, LUT_SEL2);
                     af[2] = lut_ld<RES>(w0, lane4, LUT_SEL3);
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL3);
                     mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
+                    mma16816(acc, af, qfl[2 * blk + 1][0], qfl[2 * blk + 1][1]);
                 } else if constexpr (KT == 4) {
                     const uint32_t kr = st + k_off;
                     uint32_t w0 = ld16<blk * TQ4_BYTES>(kr), w1 = ld16<blk * TQ4_BYTES + KROW8>(kr);
@@ -583,6 +606,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
                     mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
+                    mma16816(acc, af, qfl[2 * blk][0], qfl[2 * blk][1]);
                     w0 = ld16<blk * TQ4_BYTES + 8>(kr);
                     w1 = ld16<blk * TQ4_BYTES + 8 + KROW8>(kr);
                     af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
@@ -590,6 +614,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
                     mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
+                    mma16816(acc, af, qfl[2 * blk + 1][0], qfl[2 * blk + 1][1]);
                 } else {
                     constexpr int IMM = blk * TQ3_BYTES - 2 * (blk & 1);
                     const uint32_t kr = st + ((blk & 1) ? k3_off_o : k3_off_e);
@@ -601,11 +626,13 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[2] = lut_ld_addr<RES>(tq3_lut_addr<1>(wg, lane4x));
                     af[3] = lut_ld_addr<RES>(tq3_lut_addr<1>(wh, lane4x));
                     mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
+                    mma16816(acc, af, qfl[2 * blk][0], qfl[2 * blk][1]);
                     af[0] = lut_ld_addr<RES>(tq3_lut_addr<2>(wg, lane4x));
                     af[1] = lut_ld_addr<RES>(tq3_lut_addr<2>(wh, lane4x));
                     af[2] = lut_ld_addr<RES>(tq3_lut_addr<3>(wg, lane4x));
                     af[3] = lut_ld_addr<RES>(tq3_lut_addr<3>(wh, lane4x));
                     mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
+                    mma16816(acc, af, qfl[2 * blk + 1][0], qfl[2 * blk + 1][1]);
                 }
                 sc[0] = fmaf(dka[blk], acc[0], sc[0]);
                 sc[1] = fmaf(dka[blk], acc[1], sc[1]);
@@ -869,7 +896,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
             const bool empty = !(L > 0.0f);
             if (!empty) {
 #pragma unroll
-                for (int i = 0; i < EPL; ++i) ov[i] /= L;
+                for (int i = 0; i < EPL; ++i) ov[i] = ov[i] / L * (1.0f / TQ4_ALPHA);   // the V codebook's alpha
             }
             if (a.v_rotated) {
                 fwht_warp_row<EPL>(ov, lane);

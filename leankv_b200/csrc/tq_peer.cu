@@ -18,7 +18,11 @@
 //          all_gather + merge path bit for bit.
 //
 // The counters never reset: step s of an exchange expects s * world * ctas
-// arrivals (a wait is bounded by 2 s of %globaltimer).  Slots alternate
+// arrivals.  A wait is bounded by the exchange's wait limit (%globaltimer,
+// 2 s unless the creator chose another); after a wait runs out the exchange
+// stays unusable, and recovery is close() plus a new exchange on every rank.
+// The grid never exceeds the SM count, so all its CTAs are resident and a
+// waiting CTA cannot keep one that still has to push from running.  Slots alternate
 // between two buffers by step parity: a rank stores
 // step s + 2 into a slot only after its own step s + 1 completed, which needed
 // every rank's step s + 1 stores, which every rank issues only after its
@@ -43,7 +47,7 @@ constexpr int PX_ROWS_PER_CTA = PX_THREADS / 32;       // one warp per row in th
 constexpr int PX_MAX_CTAS = 128;                       // <= SMs: every CTA of the grid is resident
 constexpr size_t PX_HEAD = 256;
 constexpr size_t PX_STATUS = 64;
-constexpr uint64_t PX_WAIT_NS = 2000000000ull;         // bound of the arrival wait (2 s of %globaltimer)
+constexpr uint32_t PX_DEFAULT_WAIT_MS = 2000;          // bound of the arrival wait when the creator passes 0
 
 struct PeerBases {
     uint8_t* base[TQ_PEER_MAX_WORLD];
@@ -72,8 +76,8 @@ template <typename OT>
 __global__ void __launch_bounds__(PX_THREADS) peer_merge_kernel(const float* __restrict__ part, const PeerBases peers,
                                                                 int world, int rank, int64_t n_rows, int D,
                                                                 int64_t slot_floats, int par, uint64_t target,
-                                                                OT* __restrict__ out, float* __restrict__ lse_out,
-                                                                int vec) {
+                                                                uint64_t wait_ns, OT* __restrict__ out,
+                                                                float* __restrict__ lse_out, int vec) {
     // ---- push: this CTA's slice [c0, c1) of the packed partial into every rank's slot ----
     const int64_t F = n_rows * (int64_t)(D + 1);
     const int64_t per = ((F + gridDim.x - 1) / gridDim.x + 3) & ~int64_t(3);   // multiple of 4 floats
@@ -100,7 +104,7 @@ __global__ void __launch_bounds__(PX_THREADS) peer_merge_kernel(const float* __r
         // ---- wait for every CTA of every rank (bounded) ----
         const uint64_t* cnt = reinterpret_cast<const uint64_t*>(peers.base[rank]);
         const uint64_t t0 = global_ns();
-        while (ld_acquire_sys(cnt) < target && global_ns() - t0 < PX_WAIT_NS) __nanosleep(64);
+        while (ld_acquire_sys(cnt) < target && global_ns() - t0 < wait_ns) __nanosleep(64);
         s_ok = ld_acquire_sys(cnt) >= target;
         if (!s_ok) atomicExch(reinterpret_cast<int*>(peers.base[rank] + PX_STATUS), (int)TQ_ERROR_TIMEOUT);
     }
@@ -136,6 +140,7 @@ __global__ void __launch_bounds__(PX_THREADS) peer_merge_kernel(const float* __r
 struct tq_peer_exchange {
     int world = 0, rank = 0, dev = 0, ctas = 0, D = 0;
     int64_t n_rows = 0, slot_floats = 0;
+    uint64_t wait_ns = 0;
     uint64_t step = 0;
     bool connected = false;
     uint8_t* local = nullptr;
@@ -155,7 +160,7 @@ static tq_status px_device(const tq_peer_exchange* ex) {
     return TQ_SUCCESS;
 }
 
-extern "C" tq_status tq_peer_exchange_create(int world, int rank, int64_t n_rows, int head_dim,
+extern "C" tq_status tq_peer_exchange_create(int world, int rank, int64_t n_rows, int head_dim, uint32_t wait_ms,
                                              tq_peer_exchange** ex, void* handle_out) {
     if (!ex || !handle_out) return set_error(TQ_ERROR_INVALID_VALUE, "null argument");
     *ex = nullptr;
@@ -170,9 +175,14 @@ extern "C" tq_status tq_peer_exchange_create(int world, int rank, int64_t n_rows
     e->n_rows = n_rows;
     e->D = head_dim;
     e->slot_floats = (n_rows * (int64_t)(head_dim + 1) + 63) / 64 * 64;   // slots start 256-byte aligned
-    const int64_t ctas = (n_rows + PX_ROWS_PER_CTA - 1) / PX_ROWS_PER_CTA;
-    e->ctas = (int)(ctas < PX_MAX_CTAS ? ctas : PX_MAX_CTAS);
+    e->wait_ns = (uint64_t)(wait_ms ? wait_ms : PX_DEFAULT_WAIT_MS) * 1000000ull;
     tq_status s = cuda_status(cudaGetDevice(&e->dev), "cudaGetDevice");
+    int sms = 0;
+    if (!s) s = cuda_status(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, e->dev), "SM count");
+    int64_t ctas = (n_rows + PX_ROWS_PER_CTA - 1) / PX_ROWS_PER_CTA;
+    if (ctas > PX_MAX_CTAS) ctas = PX_MAX_CTAS;
+    if (sms > 0 && ctas > sms) ctas = sms;   // every CTA of the grid resident: no waiting CTA starves a pusher
+    e->ctas = (int)ctas;
     const size_t bytes = PX_HEAD + (size_t)2 * world * e->slot_floats * sizeof(float);
     if (!s) s = cuda_status(cudaMalloc(&e->local, bytes), "cudaMalloc(exchange buffer)");
     if (!s) s = cuda_status(cudaMemset(e->local, 0, PX_HEAD), "cudaMemset(exchange counters)");
@@ -233,17 +243,17 @@ extern "C" tq_status tq_peer_exchange_merge(tq_peer_exchange* ex, const float* p
     switch (out_dtype) {
         case TQ_DTYPE_F32:
             peer_merge_kernel<float><<<ex->ctas, PX_THREADS, 0, st>>>(part, pb, ex->world, ex->rank, ex->n_rows, ex->D,
-                                                                      ex->slot_floats, par, target, (float*)out,
+                                                                      ex->slot_floats, par, target, ex->wait_ns, (float*)out,
                                                                       lse_out, vec);
             break;
         case TQ_DTYPE_F16:
             peer_merge_kernel<__half><<<ex->ctas, PX_THREADS, 0, st>>>(part, pb, ex->world, ex->rank, ex->n_rows, ex->D,
-                                                                       ex->slot_floats, par, target, (__half*)out,
+                                                                       ex->slot_floats, par, target, ex->wait_ns, (__half*)out,
                                                                        lse_out, vec);
             break;
         default:
             peer_merge_kernel<__nv_bfloat16><<<ex->ctas, PX_THREADS, 0, st>>>(
-                part, pb, ex->world, ex->rank, ex->n_rows, ex->D, ex->slot_floats, par, target,
+                part, pb, ex->world, ex->rank, ex->n_rows, ex->D, ex->slot_floats, par, target, ex->wait_ns,
                 (__nv_bfloat16*)out, lse_out, vec);
             break;
     }

@@ -77,10 +77,13 @@ class PeerExchange:
     handles are all-gathered over the process group (host objects), and every
     rank maps the others'.  `merge(part, out, lse_out)` then runs one step on the
     current stream; every rank must call it the same number of times, in order.
+    `wait_ms` bounds each step's wait for the other ranks (0: 2000 ms).  A wait
+    that runs out leaves `out` unmerged and the exchange unusable; `status()`
+    reports it, and recovery is `close()` plus a new PeerExchange on every rank.
     `close()` unmaps, waits for all ranks, and frees (collective as well).
     """
 
-    def __init__(self, n_rows: int, head_dim: int, group=None):
+    def __init__(self, n_rows: int, head_dim: int, group=None, wait_ms: int = 0):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -95,7 +98,8 @@ class PeerExchange:
         lib = L.load()
         self._ex = C.c_void_p()
         handle = C.create_string_buffer(L.TQ_PEER_HANDLE_BYTES)
-        L.check(lib.tq_peer_exchange_create(self.world, self.rank, n_rows, head_dim, C.byref(self._ex), handle))
+        L.check(lib.tq_peer_exchange_create(self.world, self.rank, n_rows, head_dim, int(wait_ms), C.byref(self._ex),
+                                            handle))
         try:
             handles = [None] * self.world
             if self.world > 1:
@@ -149,13 +153,19 @@ class SplitSequenceAttention:
     (gloo) with CPU stand-ins.  ``transport``: "nccl" (all_gather over the
     process group, then the merge kernel) or "peer" (PeerExchange: one kernel
     over NVLink peer memory; call ``close()`` on every rank when done).
+
+    With the peer transport a step whose wait for the other ranks runs out
+    (``wait_ms``, 0: 2000 ms) leaves its output unmerged and only records the
+    failure on the device: callers must call ``status()``, which synchronizes
+    and raises TQError, before trusting any output of the steps so far.
     """
 
     def __init__(self, group=None, attend: Callable | None = None, merge: Callable | None = None,
-                 transport: str = "nccl"):
+                 transport: str = "nccl", wait_ms: int = 0):
         if transport not in ("nccl", "peer"):
             raise ValueError("transport must be 'nccl' or 'peer'")
         self.transport = transport
+        self.wait_ms = wait_ms
         self._peers: dict = {}
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -196,7 +206,7 @@ class SplitSequenceAttention:
             key = (n, D, str(q.device))
             ex = self._peers.get(key)
             if ex is None:
-                ex = self._peers[key] = PeerExchange(n, D, self.group)
+                ex = self._peers[key] = PeerExchange(n, D, self.group, self.wait_ms)
             ex.merge(send, out.view(n, D))
             return out
         if self.world == 1:

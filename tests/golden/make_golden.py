@@ -2,7 +2,7 @@
 
 Run where the reference tree is available (it is read, never modified):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 Sources of truth:
   * the reference C (src/ggml-tq.c) compiled unchanged by oracle/Makefile into
@@ -183,11 +183,11 @@ def make_testtq(out: str) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of the reference checkout (read only)")
     a = ap.parse_args()
     if not os.path.isdir(a.reference):
         sys.exit("reference tree not found; fixtures are generated where it is mounted")
-    O.build()
+    O.build(os.path.join(a.reference, "src"))
     make_codec(os.path.join(HERE, "codec.npz"))
     make_fwht(os.path.join(HERE, "fwht.npz"))
     make_tq3_opt(os.path.join(HERE, "tq3_opt.npz"), a.reference)

@@ -2,13 +2,14 @@
 
 Reference: the float64 oracle (reference dequantization + FWHT + exact softmax),
 and at full size a torch float32 evaluation on caches dequantized by the
-bit-exact dequantizer.  Tolerance (floating-point kernel, fp16 tensor-core
-operands, fp32 accumulation): max |out - ref| <= 2e-3 * max |ref| + 1e-5, and
-|lse - lse_ref| <= 2e-3 * max(1, |lse_ref|).  The bound is set by the fp16
-rounding of the softmax weights folded with the V block scales (P * d, about
-2.5 * 2^-11 relative per term): a 2-token context, where nothing averages out,
-reaches 1.1e-3; contexts of hundreds of tokens and more measure 2e-4 .. 5e-4
-(printed by the tests).
+bit-exact dequantizer.  Every cache is generated as the configs specify: N(0,1)
+rows with 4 outlier channels per KV head scaled x20, rotated and quantized.
+Tolerance (floating-point kernel, fp16 tensor-core operands, fp32
+accumulation): max |out - ref| <= 1e-3 * max |ref| + 1e-5, and
+|lse - lse_ref| <= 1e-3 * max(1, |lse_ref|).  The kernel splits both score
+operands into fp16 hi + lo parts (q~ and the K codebook) and forms P * d_V in
+fp32 before one fp16 rounding, so what remains is the fp16 rounding of the V
+codebook (at most 3.1e-4 relative) and of P * d_V (2^-11).
 """
 import numpy as np
 import pytest
@@ -18,7 +19,17 @@ from leankv_b200 import attention, ops
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
-RTOL = 2e-3
+RTOL = 1e-3
+
+
+def outlier_normal(shape, generator, device=DEV):
+    """N(0,1) [..., Hkv, T, D] with 4 outlier channels per KV head scaled x20 (the config-1 generator)."""
+    x = torch.randn(*shape, generator=generator, device=device)
+    H, D = shape[-3], shape[-1]
+    for h in range(H):
+        ch = torch.randperm(D, generator=generator, device=device)[:4]
+        x[..., h, :, ch] *= 20.0
+    return x
 
 
 def make_cache(B, Hkv, T, D, seed, qtype=4, outliers=True):
@@ -140,8 +151,8 @@ def test_c3_full_size_tq4(orc):
     """B16 Hq32 Hkv8 D128 ctx 32768, TQ4_0 K/V, fp16 queries: torch fp32 for all, oracle for 2 sequences."""
     B, Hq, Hkv, T, D = 16, 32, 8, 32768, 128
     g = torch.Generator(device=DEV).manual_seed(3)
-    kc = ops.quantize(torch.randn(B, Hkv, T, D, device=DEV, generator=g), 4, fwht_head_dim=D)
-    vc = ops.quantize(torch.randn(B, Hkv, T, D, device=DEV, generator=g), 4, fwht_head_dim=D)
+    kc = ops.quantize(outlier_normal((B, Hkv, T, D), g), 4, fwht_head_dim=D)
+    vc = ops.quantize(outlier_normal((B, Hkv, T, D), g), 4, fwht_head_dim=D)
     q = torch.randn(B, Hq, D, device=DEV, generator=g).half()
     out, lse = attention.decode_attention(q, kc, vc, return_lse=True)
     ref, lref = torch_reference(q, kc, vc, D)
@@ -238,8 +249,8 @@ def test_head_dim_256_many_segments_per_cta(kt):
     a segment and across segments (the warp-pair stage-release parities)."""
     B, Hq, Hkv, T, D = 52, 32, 8, 700, 256
     g = torch.Generator(device=DEV).manual_seed(256 + kt)
-    kc = ops.quantize(torch.randn(B, Hkv, T, D, device=DEV, generator=g), kt, fwht_head_dim=D)
-    vc = ops.quantize(torch.randn(B, Hkv, T, D, device=DEV, generator=g), 4, fwht_head_dim=D)
+    kc = ops.quantize(outlier_normal((B, Hkv, T, D), g), kt, fwht_head_dim=D)
+    vc = ops.quantize(outlier_normal((B, Hkv, T, D), g), 4, fwht_head_dim=D)
     q = torch.randn(B, Hq, D, device=DEV, generator=g).half()
     lens = torch.tensor([T - 11 * (b % 11) for b in range(B)], dtype=torch.int32, device=DEV)
     out, lse = attention.decode_attention(q, kc, vc, kv_len=lens, max_kv_len=T, return_lse=True)
@@ -264,8 +275,8 @@ def test_c4_shape_tq3k_long_context(orc):
     """64 query / 8 KV heads, head_dim 128, context 131072, TQ3_0 K / TQ4_0 V (batch 2 of the 64)."""
     B, Hq, Hkv, T, D = 2, 64, 8, 131072, 128
     g = torch.Generator(device=DEV).manual_seed(4)
-    kc = ops.quantize(torch.randn(B, Hkv, T, D, device=DEV, generator=g), 3, fwht_head_dim=D)
-    vc = ops.quantize(torch.randn(B, Hkv, T, D, device=DEV, generator=g), 4, fwht_head_dim=D)
+    kc = ops.quantize(outlier_normal((B, Hkv, T, D), g), 3, fwht_head_dim=D)
+    vc = ops.quantize(outlier_normal((B, Hkv, T, D), g), 4, fwht_head_dim=D)
     q = torch.randn(B, Hq, D, device=DEV, generator=g).half()
     lens = torch.tensor([T, T - 12345], dtype=torch.int32, device=DEV)
     out, lse = attention.decode_attention(q, kc, vc, kv_len=lens, return_lse=True)
@@ -280,8 +291,8 @@ def test_c5_shape_head_dim_256(orc):
     """8 KV heads, head_dim 256, context 16384 + 1, TQ4_0 K/V (one layer, batch 4 of the 32)."""
     B, Hq, Hkv, T, D = 4, 32, 8, 16385, 256
     g = torch.Generator(device=DEV).manual_seed(5)
-    kc = ops.quantize(torch.randn(B, Hkv, T + 1, D, device=DEV, generator=g), 4, fwht_head_dim=D)
-    vc = ops.quantize(torch.randn(B, Hkv, T + 1, D, device=DEV, generator=g), 4, fwht_head_dim=D)
+    kc = ops.quantize(outlier_normal((B, Hkv, T + 1, D), g), 4, fwht_head_dim=D)
+    vc = ops.quantize(outlier_normal((B, Hkv, T + 1, D), g), 4, fwht_head_dim=D)
     q = torch.randn(B, Hq, D, device=DEV, generator=g).to(torch.bfloat16)
     lens = torch.full((B,), T, dtype=torch.int32, device=DEV)
     out, lse = attention.decode_attention(q, kc, vc, kv_len=lens, max_kv_len=T, return_lse=True)

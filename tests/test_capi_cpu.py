@@ -155,7 +155,7 @@ def test_peer_exchange_argument_errors(args):
     lib = L.load()
     ex = ctypes.c_void_p()
     handle = ctypes.create_string_buffer(L.TQ_PEER_HANDLE_BYTES)
-    assert lib.tq_peer_exchange_create(*args, ctypes.byref(ex), handle) == 1
+    assert lib.tq_peer_exchange_create(*args, 0, ctypes.byref(ex), handle) == 1
     assert not ex.value
     assert lib.tq_peer_exchange_merge(None, None, None, 0, None, None) == 1
     assert lib.tq_peer_exchange_connect(None, None) == 1

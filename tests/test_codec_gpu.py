@@ -5,6 +5,7 @@ Bar: bit-exact codes, fp16 scales, dequantized floats and FWHT outputs (integer
 identical codes and fp16 scales to the restated coordinate descent.
 """
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -121,7 +122,7 @@ def test_tq3_opt_golden_python(golden, orc):
     ref_h = np.array([orc.half_from_float(np.float32(d)) for d in g["scales"]], np.uint16)
     hm = int((halves != ref_h).sum())
     print(f"tq3-opt vs Python: {mism} code-mismatch blocks, {hm} scale mismatches of {len(halves)}")
-    assert mism <= 2 and hm <= 2
+    assert mism == 0 and hm == 0
 
 
 # ── dtypes, shapes, alignment ──────────────────────────────────────────────────
@@ -298,16 +299,26 @@ def make_c2_input(seed, tokens=32768, heads=8, hd=128):
 
 
 def test_c2_tq3_opt_full_size(orc):
-    """TQ3_0 + optimal rounding of [32768, 8, 128] bf16 Student-t(4) x lognormal channel scales."""
+    """TQ3_0 + optimal rounding of [32768, 8, 128] bf16 Student-t(4) x lognormal channel scales:
+    every one of the 1,048,576 blocks equals the C restatement (threaded, the reference's
+    hadamard_transform_row + the coordinate descent of scripts/tq3_rounding.py)."""
     x = make_c2_input(2)
     q = blocks_np(ops.quantize(x.to(DEV), 3, fwht_head_dim=128, opt_passes=2))
+    rows = x.reshape(32768, -1).view(torch.int16).numpy().view(np.uint16)
+    ref = orc.parallel_quantize(rows, 3, 128, os.cpu_count() or 1, impl="port", opt_passes=2).reshape(-1, 14)
+    mism = int((q != ref).any(axis=1).sum())
+    print(f"C2 full size: {mism} of {ref.shape[0]} blocks differ from the restatement")
+    assert mism == 0
+    # the Python prototype starts from x / amax in float64 instead of the C float32 x * (1 / amax):
+    # report how many blocks that starting point changes (not a parity failure)
     xr = orc.fwht(x.float().numpy(), 128).reshape(-1, 32)
-    sel = np.arange(0, xr.shape[0], 61)          # ~17k blocks checked against the restatement
-    ref, moves = orc.quantize_tq3_opt(xr[sel], 2)
-    assert np.array_equal(q[sel], ref)
+    sel = np.arange(0, xr.shape[0], 16)
+    q64, _ = orc.quantize_tq3_opt(xr[sel], 2, init_f64=True)
+    print(f"C2: {int((q[sel] != q64).any(axis=1).sum())} of {len(sel)} sampled blocks differ with the "
+          "float64 starting assignment of scripts/tq3_rounding.py")
     # optimal rounding beats plain nearest-level TQ3 on the whole tensor
     plain = orc.quantize(3, xr)
     e_opt = ((orc.dequantize(3, q).reshape(xr.shape) - xr) ** 2).mean()
     e_pl = ((orc.dequantize(3, plain).reshape(xr.shape) - xr) ** 2).mean()
     assert e_opt < e_pl
-    print(f"C2 MSE opt {e_opt:.6g} vs plain {e_pl:.6g}; sampled moves {moves}")
+    print(f"C2 MSE opt {e_opt:.6g} vs plain {e_pl:.6g}")

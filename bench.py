@@ -353,8 +353,12 @@ class Attn:
                            "shape": f"B={B} Hq={Hq} Hkv={Hkv} D={D} ctx={T}, fp16 q/out", "kv_bytes": kv_total}
             self.parallelism = (f"token shards x{ws} ({L} tokens per rank); " + (
                 "all_gather of packed (O, lse) over NCCL + LSE merge on every rank" if transport == "nccl" else
-                "one kernel per rank: (O, lse) stored into every rank's buffer over NVLink (CUDA IPC peer stores), "
-                "system-scope arrival counts, LSE merge") if ws > 1 else "one GPU holds the whole context")
+                "exchange fused into the decode kernel: each pair's (O, lse) stored into every rank's buffer over "
+                "NVLink (CUDA IPC peer stores) as soon as the pair is done, system-scope arrival counts, then an "
+                "LSE merge kernel" if transport == "peer" else
+                "after the decode kernel, one kernel per rank: (O, lse) stored into every rank's buffer over NVLink "
+                "(CUDA IPC peer stores), system-scope arrival counts, LSE merge") if ws > 1 else
+                "one GPU holds the whole context")
         self.dtype = "TQ blocks -> f16 MMA, f32 accumulate"
         self.e2e_path = "leankv_b200 decode attention, q H2D and out D2H from pinned host memory"
 
@@ -757,8 +761,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-API measurement (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the token count (profiling runs)")
-    ap.add_argument("--transport", choices=["peer", "nccl"], default=None,
-                    help="c4 on N > 1 GPUs: rank exchange through NVLink peer memory or NCCL all_gather "
+    ap.add_argument("--transport", choices=["peer", "peer_merge", "nccl"], default=None,
+                    help="c4 on N > 1 GPUs: rank exchange fused into the attention over NVLink peer memory (peer), "
+                         "a separate peer push + merge kernel (peer_merge) or NCCL all_gather + merge kernel "
                          "(default: peer up to 4 GPUs, where its parity and timeout tests ran; nccl above)")
     args = ap.parse_args()
     if args.steps is None:

@@ -347,6 +347,18 @@ tq_status tq_peer_exchange_create(int world, int rank, int64_t n_rows, int head_
 tq_status tq_peer_exchange_connect(tq_peer_exchange *ex, const void *handles);
 tq_status tq_peer_exchange_merge(tq_peer_exchange *ex, const float *part, void *out, tq_dtype out_dtype,
                                  float *lse_out, void *stream);
+/* One split-sequence step with the exchange fused into the attention: the decode attention of
+ * `args` (this rank's token shard of every context; args->out and args->lse are not written)
+ * stores each (sequence, KV head) pair's rows [o | lse] into this step's slot of every rank's
+ * exchange buffer as soon as the pair is complete, and counts the pair in every rank's arrival
+ * counter; a merge kernel then waits (bounded) for the pairs of all ranks and writes the merged
+ * output to `out` (and lse_out).  The transfers of early pairs overlap the attention of later
+ * ones.  Requires batch * n_q_heads == n_rows and head_dim of the exchange; the result equals
+ * tq_decode_attention_cuda + tq_peer_exchange_merge bit for bit.  Every rank calls the same
+ * sequence of tq_peer_exchange_merge / tq_peer_exchange_attention steps.  No counterpart in the
+ * reference. */
+tq_status tq_peer_exchange_attention(tq_peer_exchange *ex, const tq_decode_attention_args *args, void *out,
+                                     tq_dtype out_dtype, float *lse_out, void *stream);
 /* synchronizes the stream, then returns the kernel-side status of the steps so far */
 tq_status tq_peer_exchange_status(tq_peer_exchange *ex, void *stream);
 tq_status tq_peer_exchange_disconnect(tq_peer_exchange *ex);

@@ -101,6 +101,7 @@ SIGNATURES = {
     "tq_peer_exchange_create": (_i32, [_i32, _i32, _i64, _i32, C.c_uint32, _v, _v]),
     "tq_peer_exchange_connect": (_i32, [_v, _v]),
     "tq_peer_exchange_merge": (_i32, [_v, _v, _v, _i32, _v, _v]),
+    "tq_peer_exchange_attention": (_i32, [_v, _v, _v, _i32, _v, _v]),
     "tq_peer_exchange_status": (_i32, [_v, _v]),
     "tq_peer_exchange_disconnect": (_i32, [_v]),
     "tq_peer_exchange_destroy": (_i32, [_v]),

@@ -221,6 +221,7 @@ struct AttnKernelArgs {
     float onorm;                // 1/sqrt(D) of the output FWHT
     int B, Hq, Hkv, grp, slots;
     int q_dtype, out_dtype, rotate_q, v_rotated;
+    PeerOut peer;               // world 0: write out / lse; else store rows into every rank's slot
 };
 
 template <int RES>
@@ -443,6 +444,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
     const int64_t pairs = (int64_t)a.B * a.Hkv;
     const int64_t total = pairs * a.lnom;
     int64_t gpos = (int64_t)blockIdx.x * a.chunk;
+    uint32_t pairs_done = 0;   // pairs this CTA completed (thread 0), counted at the end for the exchange
     const int64_t gend = gpos + a.chunk < total ? gpos + a.chunk : total;
 
     while (gpos < gend) {
@@ -905,9 +907,38 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
             }
             const int64_t b = pair / a.Hkv, g = pair - b * a.Hkv;
             const size_t bh = (size_t)b * a.Hq + (size_t)g * a.grp + warp;
+            const float lse_v = empty ? -INFINITY : (M + __log2f(L)) * 0.6931471805599453f;
+            if (a.peer.world == 0) {
 #pragma unroll
-            for (int i = 0; i < EPL; ++i) store_out_rt(a.out, a.out_dtype, bh * D + lane * EPL + i, ov[i]);
-            if (a.lse && lane == 0) a.lse[bh] = empty ? -INFINITY : (M + __log2f(L)) * 0.6931471805599453f;
+                for (int i = 0; i < EPL; ++i) store_out_rt(a.out, a.out_dtype, bh * D + lane * EPL + i, ov[i]);
+                if (a.lse && lane == 0) a.lse[bh] = lse_v;
+            } else {
+                // split-sequence exchange: this rank's (o, lse) row goes into its slot of every rank's
+                // exchange buffer (peer stores over NVLink), made visible system-wide before the count
+                const int64_t slot = ((int64_t)a.peer.par * a.peer.world + a.peer.rank) * a.peer.slot_floats;
+                for (int t = 0; t < a.peer.world; ++t) {
+                    float* dst = reinterpret_cast<float*>(a.peer.base[t] + PEER_HEAD_BYTES) + slot;
+                    static_assert(EPL % 4 == 0, "16-byte row stores");
+#pragma unroll
+                    for (int i = 0; i < EPL; i += 4)
+                        *reinterpret_cast<float4*>(dst + bh * D + lane * EPL + i) =
+                            make_float4(ov[i], ov[i + 1], ov[i + 2], ov[i + 3]);
+                    if (lane == 0) dst[a.peer.n_rows * D + bh] = lse_v;
+                }
+            }
+        }
+        if (threadIdx.x == 0 && s_abort[1]) ++pairs_done;
+    }
+    if (a.peer.world != 0) {
+        // Count this CTA's completed pairs once, at its end, in every rank's counter.  The rows of
+        // early pairs have been travelling over NVLink since those pairs finished; the barrier and
+        // the cumulative system-scope fence of thread 0 order every thread's row stores before the
+        // counts, so a rank that sees all counts reads complete rows.
+        __syncthreads();
+        if (threadIdx.x == 0 && pairs_done) {
+            __threadfence_system();
+            for (int t = 0; t < a.peer.world; ++t)
+                atomicAdd_system(reinterpret_cast<unsigned long long*>(a.peer.base[t]), (unsigned long long)pairs_done);
         }
     }
 }
@@ -1059,6 +1090,7 @@ static cudaError_t run_decode(const AttnRun& r, const AttnPlan& p, uint8_t* ws, 
     a.out_dtype = r.out_dtype;
     a.rotate_q = r.rotate_q;
     a.v_rotated = r.v_rotated;
+    a.peer = r.peer;
     const int res = reserved_smem();
     if (res == 0) return launch_decode_kt<D, 0>(a, r.k_type, p.grid, st);
     if (res == 1024) return launch_decode_kt<D, 1024>(a, r.k_type, p.grid, st);

@@ -14,6 +14,19 @@ struct AttnPlan {
     int slots = 0;               // partial slots per (sequence, KV head)
 };
 
+// Destination of the split-sequence exchange (world 0: the kernel writes out / lse instead).  The
+// last CTA of a (sequence, KV head) pair stores the pair's rows [o (D floats) | lse] into slot
+// (par, rank) of every rank's exchange buffer, then counts the pair in every rank's arrival
+// counter (the buffer's first 8 bytes).  Buffer layout: counter | status | slots [2][world][slot_floats]
+// from PEER_HEAD_BYTES on, each slot [o (n_rows x D) | lse (n_rows)].
+constexpr size_t PEER_HEAD_BYTES = 256;
+constexpr int PEER_OUT_MAX_WORLD = 64;
+struct PeerOut {
+    uint8_t* base[PEER_OUT_MAX_WORLD] = {};
+    int world = 0, rank = 0, par = 0;
+    int64_t slot_floats = 0, n_rows = 0;
+};
+
 struct AttnRun {
     int B = 0, Hq = 0, Hkv = 0, grp = 0, D = 0;
     const void* q = nullptr;
@@ -28,6 +41,7 @@ struct AttnRun {
     void* out = nullptr;
     int out_dtype = 0;
     float* lse = nullptr;
+    PeerOut peer;
 };
 
 AttnPlan attn_plan(int B, int Hkv, int D, int64_t cap, int64_t max_len);

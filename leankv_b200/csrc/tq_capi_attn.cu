@@ -9,7 +9,7 @@
 
 using namespace tq;
 
-static tq_status attn_check(const tq_decode_attention_args* a, AttnRun* r, AttnPlan* p) {
+tq_status tq::attn_check(const tq_decode_attention_args* a, AttnRun* r, AttnPlan* p) {
     if (!a) return set_error(TQ_ERROR_INVALID_VALUE, "null argument block");
     if (a->batch < 0 || a->n_q_heads <= 0 || a->n_kv_heads <= 0)
         return set_error(TQ_ERROR_INVALID_VALUE, "bad batch / head counts");

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include "leankv_tq.h"
+#include "tq_attn.h"
 
 namespace tq {
 
@@ -18,5 +19,7 @@ size_t block_bytes(int type);
 size_t dtype_bytes(int dt);
 bool dtype_ok(int dt);
 bool type_ok(int t);
+// checks a decode-attention argument block and fills the kernel's run description and work plan
+tq_status attn_check(const tq_decode_attention_args* a, AttnRun* r, AttnPlan* p);
 
 }  // namespace tq

@@ -38,6 +38,7 @@
 #include <cuda_runtime.h>
 
 #include "leankv_tq.h"
+#include "tq_attn.h"
 #include "tq_capi_internal.h"
 
 namespace {
@@ -72,12 +73,17 @@ __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
     return v;
 }
 
-template <typename OT>
+// PUSH: store this rank's partial `part` and count every CTA (tq_peer_exchange_merge).  Without it
+// the partials were stored and counted by the decode-attention kernel itself
+// (tq_peer_exchange_attention): this kernel only waits for the target and merges.
+template <typename OT, bool PUSH>
 __global__ void __launch_bounds__(PX_THREADS) peer_merge_kernel(const float* __restrict__ part, const PeerBases peers,
                                                                 int world, int rank, int64_t n_rows, int D,
                                                                 int64_t slot_floats, int par, uint64_t target,
                                                                 uint64_t wait_ns, OT* __restrict__ out,
                                                                 float* __restrict__ lse_out, int vec) {
+    __shared__ int s_ok;
+    if (PUSH) {
     // ---- push: this CTA's slice [c0, c1) of the packed partial into every rank's slot ----
     const int64_t F = n_rows * (int64_t)(D + 1);
     const int64_t per = ((F + gridDim.x - 1) / gridDim.x + 3) & ~int64_t(3);   // multiple of 4 floats
@@ -97,11 +103,12 @@ __global__ void __launch_bounds__(PX_THREADS) peer_merge_kernel(const float* __r
     }
     __threadfence_system();   // this thread's stores reach every rank before the counts below
     __syncthreads();
-    __shared__ int s_ok;
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0)
         for (int t = 0; t < world; ++t)
             atomicAdd_system(reinterpret_cast<unsigned long long*>(peers.base[t]), 1ull);
-        // ---- wait for every CTA of every rank (bounded) ----
+    }
+    if (threadIdx.x == 0) {
+        // ---- wait for every count of every rank (bounded) ----
         const uint64_t* cnt = reinterpret_cast<const uint64_t*>(peers.base[rank]);
         const uint64_t t0 = global_ns();
         while (ld_acquire_sys(cnt) < target && global_ns() - t0 < wait_ns) __nanosleep(64);
@@ -142,6 +149,7 @@ struct tq_peer_exchange {
     int64_t n_rows = 0, slot_floats = 0;
     uint64_t wait_ns = 0;
     uint64_t step = 0;
+    uint64_t expected = 0;   // arrivals counted into this rank's counter by the end of the last step
     bool connected = false;
     uint8_t* local = nullptr;
     uint8_t* peer[TQ_PEER_MAX_WORLD] = {};
@@ -224,6 +232,72 @@ extern "C" tq_status tq_peer_exchange_connect(tq_peer_exchange* ex, const void* 
     return TQ_SUCCESS;
 }
 
+template <bool PUSH>
+static tq_status launch_merge(tq_peer_exchange* ex, const float* part, void* out, tq_dtype out_dtype, float* lse_out,
+                              uint64_t target, cudaStream_t st) {
+    PeerBases pb;
+    for (int t = 0; t < TQ_PEER_MAX_WORLD; ++t) pb.base[t] = t < ex->world ? ex->peer[t] : nullptr;
+    const uint64_t step = ex->step + 1;
+    const int par = (int)(step & 1);
+    const int vec = part && (((uintptr_t)part) & 15) == 0;
+    switch (out_dtype) {
+        case TQ_DTYPE_F32:
+            peer_merge_kernel<float, PUSH><<<ex->ctas, PX_THREADS, 0, st>>>(
+                part, pb, ex->world, ex->rank, ex->n_rows, ex->D, ex->slot_floats, par, target, ex->wait_ns,
+                (float*)out, lse_out, vec);
+            break;
+        case TQ_DTYPE_F16:
+            peer_merge_kernel<__half, PUSH><<<ex->ctas, PX_THREADS, 0, st>>>(
+                part, pb, ex->world, ex->rank, ex->n_rows, ex->D, ex->slot_floats, par, target, ex->wait_ns,
+                (__half*)out, lse_out, vec);
+            break;
+        default:
+            peer_merge_kernel<__nv_bfloat16, PUSH><<<ex->ctas, PX_THREADS, 0, st>>>(
+                part, pb, ex->world, ex->rank, ex->n_rows, ex->D, ex->slot_floats, par, target, ex->wait_ns,
+                (__nv_bfloat16*)out, lse_out, vec);
+            break;
+    }
+    const tq_status s = cuda_status(cudaGetLastError(), "peer merge launch");
+    if (!s) ex->step = step;
+    return s;
+}
+
+extern "C" tq_status tq_peer_exchange_attention(tq_peer_exchange* ex, const tq_decode_attention_args* a, void* out,
+                                                tq_dtype out_dtype, float* lse_out, void* stream) {
+    if (!ex || !a || !out) return set_error(TQ_ERROR_INVALID_VALUE, "null argument");
+    if (!ex->connected) return set_error(TQ_ERROR_INVALID_VALUE, "exchange not connected");
+    if (!tq::dtype_ok(out_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "bad output dtype");
+    if (((uintptr_t)out) % tq::dtype_bytes(out_dtype)) return set_error(TQ_ERROR_MISALIGNED, "out not aligned");
+    tq_status s = px_device(ex);
+    if (s) return s;
+    tq::AttnRun r;
+    tq::AttnPlan p;
+    if ((s = tq::attn_check(a, &r, &p))) return s;
+    if ((int64_t)r.B * r.Hq != ex->n_rows || r.D != ex->D)
+        return set_error(TQ_ERROR_INVALID_VALUE, "batch * n_q_heads = %lld and head_dim %d do not match the exchange "
+                         "(%lld rows of %d)", (long long)r.B * r.Hq, r.D, (long long)ex->n_rows, ex->D);
+    const size_t need = tq::attn_workspace_bytes(r.B, r.Hkv, r.D, p);
+    if (!a->workspace || a->workspace_bytes < need)
+        return set_error(TQ_ERROR_INVALID_VALUE, "workspace of %zu bytes needed", need);
+    if (((uintptr_t)a->workspace) & 255) return set_error(TQ_ERROR_MISALIGNED, "workspace must be 256-byte aligned");
+    if (r.D % 4) return set_error(TQ_ERROR_UNSUPPORTED, "head_dim must be a multiple of 4");
+    // the decode kernel stores its (o, lse) rows into step (ex->step + 1)'s slot of every rank and
+    // counts each (sequence, KV head) pair there; the merge kernel waits for all ranks' pairs
+    r.peer.world = ex->world;
+    r.peer.rank = ex->rank;
+    r.peer.par = (int)((ex->step + 1) & 1);
+    r.peer.slot_floats = ex->slot_floats;
+    r.peer.n_rows = ex->n_rows;
+    for (int t = 0; t < ex->world; ++t) r.peer.base[t] = ex->peer[t];
+    const cudaStream_t st = (cudaStream_t)stream;
+    s = cuda_status(tq::launch_decode_attention(r, p, a->workspace, st), "decode attention launch");
+    if (s) return s;   // nothing was counted: the step and the targets stay where the peers expect them
+    const uint64_t target = ex->expected + (uint64_t)ex->world * (uint64_t)r.B * (uint64_t)r.Hkv;
+    s = launch_merge<false>(ex, nullptr, out, out_dtype, lse_out, target, st);
+    if (!s) ex->expected = target;
+    return s;
+}
+
 extern "C" tq_status tq_peer_exchange_merge(tq_peer_exchange* ex, const float* part, void* out, tq_dtype out_dtype,
                                             float* lse_out, void* stream) {
     if (!ex || !part || !out) return set_error(TQ_ERROR_INVALID_VALUE, "null argument");
@@ -233,32 +307,9 @@ extern "C" tq_status tq_peer_exchange_merge(tq_peer_exchange* ex, const float* p
     if (((uintptr_t)out) % tq::dtype_bytes(out_dtype)) return set_error(TQ_ERROR_MISALIGNED, "out not aligned");
     tq_status s = px_device(ex);
     if (s) return s;
-    PeerBases pb;
-    for (int t = 0; t < TQ_PEER_MAX_WORLD; ++t) pb.base[t] = t < ex->world ? ex->peer[t] : nullptr;
-    const uint64_t step = ex->step + 1;
-    const uint64_t target = step * (uint64_t)ex->world * (uint64_t)ex->ctas;
-    const int par = (int)(step & 1);
-    const int vec = (((uintptr_t)part) & 15) == 0;
-    cudaStream_t st = (cudaStream_t)stream;
-    switch (out_dtype) {
-        case TQ_DTYPE_F32:
-            peer_merge_kernel<float><<<ex->ctas, PX_THREADS, 0, st>>>(part, pb, ex->world, ex->rank, ex->n_rows, ex->D,
-                                                                      ex->slot_floats, par, target, ex->wait_ns, (float*)out,
-                                                                      lse_out, vec);
-            break;
-        case TQ_DTYPE_F16:
-            peer_merge_kernel<__half><<<ex->ctas, PX_THREADS, 0, st>>>(part, pb, ex->world, ex->rank, ex->n_rows, ex->D,
-                                                                       ex->slot_floats, par, target, ex->wait_ns, (__half*)out,
-                                                                       lse_out, vec);
-            break;
-        default:
-            peer_merge_kernel<__nv_bfloat16><<<ex->ctas, PX_THREADS, 0, st>>>(
-                part, pb, ex->world, ex->rank, ex->n_rows, ex->D, ex->slot_floats, par, target, ex->wait_ns,
-                (__nv_bfloat16*)out, lse_out, vec);
-            break;
-    }
-    s = cuda_status(cudaGetLastError(), "peer merge launch");
-    if (!s) ex->step = step;   // a launch that failed leaves the step count where the peers expect it
+    const uint64_t target = ex->expected + (uint64_t)ex->world * (uint64_t)ex->ctas;
+    s = launch_merge<true>(ex, part, out, out_dtype, lse_out, target, (cudaStream_t)stream);
+    if (!s) ex->expected = target;   // a launch that failed leaves the counts where the peers expect them
     return s;
 }
 

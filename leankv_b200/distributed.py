@@ -18,12 +18,17 @@ The decode attention divides two ways:
   which is NCCL over NVLink on a B200 node.  Each rank then merges the P partials
   itself (tq_lse_merge_cuda), so every rank ends up holding the full output.
 
-  ``transport="peer"`` replaces the all_gather and the merge by one kernel per
-  rank (tq_peer_exchange_merge): it stores the rank's partial into every rank's
-  exchange buffer over NVLink (CUDA IPC mappings, plain peer stores), counts
-  its arrival with system-scope atomics, waits (bounded) for all ranks' partials
-  and merges them with the same arithmetic, so both transports give identical
-  outputs.  It needs one GPU per rank on one node.
+  ``transport="peer"`` fuses the exchange into the attention
+  (tq_peer_exchange_attention): the decode kernel's CTA that completes a
+  (sequence, KV head) pair stores that pair's rows straight into its slot of
+  every rank's exchange buffer over NVLink (CUDA IPC mappings, plain peer
+  stores) and counts the pair in every rank's arrival counter (system-scope
+  atomics), so the transfers of early pairs overlap the attention of later
+  ones; a merge kernel then waits (bounded) for all ranks' pairs and merges
+  them with the arithmetic of tq_lse_merge_cuda.  ``transport="peer_merge"``
+  runs the attention first and then one push + merge kernel per rank
+  (tq_peer_exchange_merge).  All transports give bit-identical outputs.  The
+  peer transports need one GPU per rank on one node.
 
 The output rotation (FWHT) is linear and is applied inside each rank's partial;
 the merge is a convex combination, so it commutes with the rotation.
@@ -123,6 +128,34 @@ class PeerExchange:
                                                 _stream(part)))
         return out
 
+    def attention(self, q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor, out: torch.Tensor,
+                  kv_len: torch.Tensor | None = None, max_kv_len: int | None = None, sm_scale: float | None = None,
+                  lse_out: torch.Tensor | None = None, rotate_q: bool = True, v_rotated: bool = True) -> torch.Tensor:
+        """One step with the exchange fused into the decode attention (tq_peer_exchange_attention): the
+        attention over this rank's token shard stores every (sequence, KV head) pair's rows into all
+        ranks' slots as soon as the pair is done; a merge kernel waits for every rank and writes the
+        merged [B, Hq, D] output to `out`."""
+        B, Hq, D = q.shape
+        if B * Hq != self.n_rows or D != self.head_dim:
+            raise ValueError("q does not match the exchange's rows / head_dim")
+        if out.numel() != self.n_rows * D or not out.is_contiguous() or out.dtype not in _DTYPES:
+            raise ValueError("out must be a contiguous [B, Hq, D] float32 / float16 / bfloat16 tensor")
+        attention._need_cuda(q, k_shard, v_shard, out)
+        if kv_len is not None:
+            kv_len = kv_len.contiguous()
+        k_type = 4 if k_shard.shape[-1] == 18 else 3
+        a = attention.make_args(q.contiguous(), k_shard, v_shard, kv_len, max_kv_len or 0, sm_scale or 0.0, rotate_q,
+                                v_rotated, out, None, k_type, 4)
+        lib = attention._bind()
+        need = lib.tq_decode_attention_workspace_size(C.byref(a))
+        if need == 0:
+            L.check(lib.tq_decode_attention_cuda(C.byref(a), _stream(q)))   # reports the argument error
+        ws = attention._workspace(q.device, need)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        L.check(L.load().tq_peer_exchange_attention(self._ex, C.byref(a), out.data_ptr(), _DTYPES[out.dtype],
+                                                    lse_out.data_ptr() if lse_out is not None else None, _stream(q)))
+        return out
+
     def status(self) -> None:
         """Synchronize the current stream and raise if a step's wait ran out."""
         L.check(L.load().tq_peer_exchange_status(self._ex, torch.cuda.current_stream().cuda_stream))
@@ -151,8 +184,12 @@ class SplitSequenceAttention:
     ``merge(parts, n_parts, n_rows, head_dim, out)`` default to the CUDA
     kernels; they are parameters so that the exchange logic can run on CPU ranks
     (gloo) with CPU stand-ins.  ``transport``: "nccl" (all_gather over the
-    process group, then the merge kernel) or "peer" (PeerExchange: one kernel
-    over NVLink peer memory; call ``close()`` on every rank when done).
+    process group, then the merge kernel), "peer" (PeerExchange with the
+    exchange fused into the decode attention: each pair's rows go to every rank
+    over NVLink as soon as the pair is done, then a merge kernel) or
+    "peer_merge" (PeerExchange: the attention, then one push + merge kernel over
+    NVLink peer memory).  For both peer transports call ``close()`` on every
+    rank when done.
 
     With the peer transport a step whose wait for the other ranks runs out
     (``wait_ms``, 0: 2000 ms) leaves its output unmerged and only records the
@@ -162,8 +199,10 @@ class SplitSequenceAttention:
 
     def __init__(self, group=None, attend: Callable | None = None, merge: Callable | None = None,
                  transport: str = "nccl", wait_ms: int = 0):
-        if transport not in ("nccl", "peer"):
-            raise ValueError("transport must be 'nccl' or 'peer'")
+        if transport not in ("nccl", "peer", "peer_merge"):
+            raise ValueError("transport must be 'nccl', 'peer' or 'peer_merge'")
+        if transport == "peer" and attend is not None:
+            raise ValueError("the fused peer transport runs the CUDA attention itself; use 'peer_merge' with attend")
         self.transport = transport
         self.wait_ms = wait_ms
         self._peers: dict = {}
@@ -196,13 +235,19 @@ class SplitSequenceAttention:
                  out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float32, **kw) -> torch.Tensor:
         B, Hq, D = q.shape
         n = B * Hq
+        if out is None:
+            out = torch.empty((B, Hq, D), dtype=out_dtype, device=q.device)
+        if self.transport == "peer":
+            key = (n, D, str(q.device))
+            ex = self._peers.get(key)
+            if ex is None:
+                ex = self._peers[key] = PeerExchange(n, D, self.group, self.wait_ms)
+            return ex.attention(q, k_shard, v_shard, out, kv_len_local, max_kv_len, **kw)
         send, recv = self._buffers(n, D, q.device)
         o_local = send[: n * D].view(B, Hq, D)
         lse_local = send[n * D:].view(B, Hq)
         self._attend(q, k_shard, v_shard, kv_len_local, max_kv_len, o_local, lse_local, **kw)
-        if out is None:
-            out = torch.empty((B, Hq, D), dtype=out_dtype, device=q.device)
-        if self.transport == "peer":
+        if self.transport == "peer_merge":
             key = (n, D, str(q.device))
             ex = self._peers.get(key)
             if ex is None:

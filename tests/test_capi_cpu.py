@@ -159,6 +159,7 @@ def test_peer_exchange_argument_errors(args):
     assert not ex.value
     assert lib.tq_peer_exchange_merge(None, None, None, 0, None, None) == 1
     assert lib.tq_peer_exchange_connect(None, None) == 1
+    assert lib.tq_peer_exchange_attention(None, None, None, 0, None, None) == 1
     assert lib.tq_peer_exchange_destroy(None) == 0
 
 

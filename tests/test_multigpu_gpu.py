@@ -55,12 +55,13 @@ def _rank(rank, world, port, outdir):
         att = SplitSequenceAttention()
         out = att(q, ks, vs, ll, s1 - s0, out_dtype=torch.float32)
         full = attention.decode_attention(q, kc, vc, kv_len=lens)
-        peer = SplitSequenceAttention(transport="peer")
         outs = []
-        for _ in range(3):   # both slot buffers, the arrival counter over several steps
-            outs.append(peer(q, ks, vs, ll, s1 - s0, out_dtype=torch.float32).cpu().numpy())
-        peer.status()
-        peer.close()
+        for transport in ("peer", "peer_merge"):
+            peer = SplitSequenceAttention(transport=transport)
+            for _ in range(3):   # both slot buffers, the arrival counter over several steps
+                outs.append(peer(q, ks, vs, ll, s1 - s0, out_dtype=torch.float32).cpu().numpy())
+            peer.status()
+            peer.close()
         np.save(os.path.join(outdir, f"r{rank}.npy"), np.stack([out.cpu().numpy(), full.cpu().numpy()] + outs))
         dist.barrier()
     finally:

@@ -287,6 +287,9 @@ __device__ __forceinline__ void bulk_issue(bool pred, uint32_t dst_k, const void
 
 constexpr float M_FLOOR = -1.0e30f;   // finite "minus infinity" for the running max
 
+// a partial's value: through L2 when other CTAs wrote it, from shared memory when this CTA did
+__device__ __forceinline__ float part_ld(bool in_smem, const float* p) { return in_smem ? *p : __ldcg(p); }
+
 // compile-time loop: f(std::integral_constant<int, I>) for I in [B, E)
 template <int B, int E, typename F>
 __device__ __forceinline__ void static_for(F&& f) {
@@ -376,7 +379,10 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
     uint8_t* scratch = stages + RINGS * ATT_STAGES * STAGE;
     uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + WARPS * 2 * SCR);
     uint64_t* ebars = bars + RINGS * ATT_STAGES;
-    int* s_abort = reinterpret_cast<int*>(ebars + Cfg::EBARS);
+    int* s_abort = reinterpret_cast<int*>(ebars + Cfg::EBARS);   // [0] abort, [1] last CTA of the pair
+    // head_dim 256: the lo parts of q~'s B fragments, [half][chunk][lane], one copy per half of the
+    // dimensions (every warp of a half holds the same ones), read per chunk instead of held in registers
+    uint2* s_qfl = reinterpret_cast<uint2*>(s_abort + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ring = warp / SPLIT, half = warp % SPLIT;   // tile stream, half of the dimensions
@@ -541,6 +547,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     split_h2(mq[e0], mq[e0 + 1], qf[kk][0], qfl[kk][0]);
                     split_h2(mq[e0 + 2], mq[e0 + 3], qf[kk][1], qfl[kk][1]);
                 }
+                if (SPLIT == 2 && ring == 0) s_qfl[(half * NCH + kk) * 32 + lane] = make_uint2(qfl[kk][0], qfl[kk][1]);
             }
             __syncthreads();   // q~ read by all warps before the scale scratch is reused
         }
@@ -581,6 +588,17 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 dka[4 * c] = x.x; dka[4 * c + 1] = x.y; dka[4 * c + 2] = x.z; dka[4 * c + 3] = x.w;
                 dkb[4 * c] = y.x; dkb[4 * c + 1] = y.y; dkb[4 * c + 2] = y.z; dkb[4 * c + 3] = y.w;
             });
+            // lo part of q~'s fragment for chunk kk: registers at head_dim 128, shared memory at 256
+            auto qlo = [&](int kk) -> uint2 {
+                if constexpr (SPLIT == 2) {
+                    uint2 v;
+                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y)
+                                 : "r"(smem_u32(s_qfl + (half * NCH + kk) * 32 + lane)));
+                    return v;
+                } else {
+                    return make_uint2(qfl[kk][0], qfl[kk][1]);
+                }
+            };
             static_for<0, NBLK>([&](auto blk_c) {
                 constexpr int blk = decltype(blk_c)::value;
                 float acc[4];
@@ -593,13 +611,13 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
                     mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
-                    mma16816(acc, af, qfl[2 * blk][0], qfl[2 * blk][1]);
+                    { const uint2 ql = qlo(2 * blk); mma16816(acc, af, ql.x, ql.y); }
                     af[0] = lut_ld<RES>(w0, lane4, LUT_SEL2);
                     af[1] = lut_ld<RES>(w1, lane4, LUT_SEL2);
                     af[2] = lut_ld<RES>(w0, lane4, LUT_SEL3);
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL3);
                     mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
-                    mma16816(acc, af, qfl[2 * blk + 1][0], qfl[2 * blk + 1][1]);
+                    { const uint2 ql = qlo(2 * blk + 1); mma16816(acc, af, ql.x, ql.y); }
                 } else if constexpr (KT == 4) {
                     const uint32_t kr = st + k_off;
                     uint32_t w0 = ld16<blk * TQ4_BYTES>(kr), w1 = ld16<blk * TQ4_BYTES + KROW8>(kr);
@@ -608,7 +626,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
                     mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
-                    mma16816(acc, af, qfl[2 * blk][0], qfl[2 * blk][1]);
+                    { const uint2 ql = qlo(2 * blk); mma16816(acc, af, ql.x, ql.y); }
                     w0 = ld16<blk * TQ4_BYTES + 8>(kr);
                     w1 = ld16<blk * TQ4_BYTES + 8 + KROW8>(kr);
                     af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
@@ -616,7 +634,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
                     mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
-                    mma16816(acc, af, qfl[2 * blk + 1][0], qfl[2 * blk + 1][1]);
+                    { const uint2 ql = qlo(2 * blk + 1); mma16816(acc, af, ql.x, ql.y); }
                 } else {
                     constexpr int IMM = blk * TQ3_BYTES - 2 * (blk & 1);
                     const uint32_t kr = st + ((blk & 1) ? k3_off_o : k3_off_e);
@@ -628,13 +646,13 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[2] = lut_ld_addr<RES>(tq3_lut_addr<1>(wg, lane4x));
                     af[3] = lut_ld_addr<RES>(tq3_lut_addr<1>(wh, lane4x));
                     mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
-                    mma16816(acc, af, qfl[2 * blk][0], qfl[2 * blk][1]);
+                    { const uint2 ql = qlo(2 * blk); mma16816(acc, af, ql.x, ql.y); }
                     af[0] = lut_ld_addr<RES>(tq3_lut_addr<2>(wg, lane4x));
                     af[1] = lut_ld_addr<RES>(tq3_lut_addr<2>(wh, lane4x));
                     af[2] = lut_ld_addr<RES>(tq3_lut_addr<3>(wg, lane4x));
                     af[3] = lut_ld_addr<RES>(tq3_lut_addr<3>(wh, lane4x));
                     mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
-                    mma16816(acc, af, qfl[2 * blk + 1][0], qfl[2 * blk + 1][1]);
+                    { const uint2 ql = qlo(2 * blk + 1); mma16816(acc, af, ql.x, ql.y); }
                 }
                 sc[0] = fmaf(dka[blk], acc[0], sc[0]);
                 sc[1] = fmaf(dka[blk], acc[1], sc[1]);
@@ -859,7 +877,16 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         }
         __syncthreads();
         const size_t sstride = (size_t)ATT_N * (D + 2);
-        float* dst = a.part + ((size_t)pair * a.slots + slot) * sstride;
+        const int64_t c_first = (pair * a.lnom) / a.chunk, c_last = ((pair + 1) * a.lnom - 1) / a.chunk;
+        const int nslot = (int)(c_last - c_first + 1);
+        // A pair inside this CTA's chunk (one slot) is finished from shared memory: no partial
+        // through L2, no fence, no count.  The partial sits past the next segment's q~ staging in
+        // the scale scratch, which nothing writes before the next segment's first barrier.
+        // (head_dim 128: the scratch holds both; head_dim 256 pairs always go through L2.)
+        constexpr int SOLO_OFF = ((ATT_N * (D + 4) * 4 + 127) / 128) * 128;
+        constexpr bool SOLO_OK = SOLO_OFF + ATT_N * (D + 2) * 4 <= WARPS * 2 * SCR;
+        const bool solo = SOLO_OK && nslot == 1;
+        float* dst = solo ? reinterpret_cast<float*>(scratch + SOLO_OFF) : a.part + ((size_t)pair * a.slots + slot) * sstride;
         for (int idx = threadIdx.x; idx < ATT_N * (D + 2); idx += THREADS) {
             const int h = idx / (D + 2), c = idx % (D + 2);
             float acc = smax[h];
@@ -871,29 +898,27 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         }
         // publish the partial, count this CTA in the pair; the stages are free for the next
         // segment's copies after this barrier
-        __threadfence();
+        if (!solo) __threadfence();
         __syncthreads();
-        const int64_t c_first = (pair * a.lnom) / a.chunk, c_last = ((pair + 1) * a.lnom - 1) / a.chunk;
-        const int nslot = (int)(c_last - c_first + 1);
-        if (threadIdx.x == 0) s_abort[1] = atomicAdd(a.cnt + pair, 1) == nslot - 1;
+        if (threadIdx.x == 0) s_abort[1] = solo ? 1 : atomicAdd(a.cnt + pair, 1) == nslot - 1;
         __syncthreads();
         if (s_abort[1] && warp < a.grp) {
             // last CTA of the pair: log-sum-exp merge of the nslot partials of query head
             // hh = warp, inverse FWHT, cast; lse in natural log
-            __threadfence();
+            if (!solo) __threadfence();
             constexpr int EPL = D / 32;
-            const float* p0 = a.part + (size_t)pair * a.slots * sstride + warp * (D + 2);
+            const float* p0 = solo ? dst + warp * (D + 2) : a.part + (size_t)pair * a.slots * sstride + warp * (D + 2);
             float M = M_FLOOR, L = 0.0f;
             float ov[EPL];
 #pragma unroll
             for (int i = 0; i < EPL; ++i) ov[i] = 0.0f;
-            for (int s = 0; s < nslot; ++s) M = fmaxf(M, __ldcg(p0 + s * sstride));
-            for (int s = 0; s < nslot; ++s) L += ex2(__ldcg(p0 + s * sstride) - M) * __ldcg(p0 + s * sstride + 1);
+            for (int s = 0; s < nslot; ++s) M = fmaxf(M, part_ld(solo, p0 + s * sstride));
+            for (int s = 0; s < nslot; ++s) L += ex2(part_ld(solo, p0 + s * sstride) - M) * part_ld(solo, p0 + s * sstride + 1);
             if (L > 0.0f)
                 for (int s = 0; s < nslot; ++s) {
-                    const float w = ex2(__ldcg(p0 + s * sstride) - M);
+                    const float w = ex2(part_ld(solo, p0 + s * sstride) - M);
 #pragma unroll
-                    for (int i = 0; i < EPL; ++i) ov[i] += w * __ldcg(p0 + s * sstride + 2 + lane * EPL + i);
+                    for (int i = 0; i < EPL; ++i) ov[i] += w * part_ld(solo, p0 + s * sstride + 2 + lane * EPL + i);
                 }
             const bool empty = !(L > 0.0f);
             if (!empty) {
@@ -989,7 +1014,8 @@ static size_t decode_smem_bytes() {
     s += (size_t)Cfg::WARPS * 2 * Cfg::SCR;
     s += (size_t)Cfg::RINGS * ATT_STAGES * 8;
     s += (size_t)Cfg::EBARS * 8;
-    s += 16;
+    s += 16;                                                        // s_abort
+    if (Cfg::SPLIT == 2) s += (size_t)2 * Cfg::NCH * 32 * 8;        // s_qfl
     return s;
 }
 

@@ -50,6 +50,7 @@
 #include "tq_capi_internal.h"
 #include "tq_common.cuh"
 #include "tq_kernels.h"
+#include "tq_merge.cuh"
 
 namespace tq {
 
@@ -968,38 +969,18 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
     }
 }
 
-// ── output stores, multi-rank log-sum-exp merge ──────────────────────────────
+// ── multi-rank log-sum-exp merge ───────────────────────────────────────────────
 
-template <typename OT> __device__ __forceinline__ void store_out(OT* p, float v);
-template <> __device__ __forceinline__ void store_out<float>(float* p, float v) { *p = v; }
-template <> __device__ __forceinline__ void store_out<__half>(__half* p, float v) { *p = __float2half_rn(v); }
-template <> __device__ __forceinline__ void store_out<__nv_bfloat16>(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
-
-// log-sum-exp merge of P partial results (natural-log lse), e.g. from several ranks;
-// part p at o + p * o_stride, lse + p * lse_stride
+// merge of P partial results (natural-log lse), e.g. from several ranks; part p at o + p * o_stride,
+// lse + p * lse_stride; one warp per row (merge_row, shared with the peer-memory merge kernels)
+constexpr int COMBINE_WARPS = 8;
 template <typename OT>
-__global__ void __launch_bounds__(128) lse_combine_kernel(const float* __restrict__ o, int64_t o_stride,
-                                                          const float* __restrict__ lse, int64_t lse_stride,
-                                                          OT* __restrict__ out, float* __restrict__ lse_out, int P,
-                                                          int64_t n, int D) {
-    const int64_t i = blockIdx.x;
-    float M = -INFINITY;
-    for (int p = 0; p < P; ++p) M = fmaxf(M, lse[(int64_t)p * lse_stride + i]);
-    float W = 0.0f;
-    for (int p = 0; p < P; ++p) {
-        const float l = lse[(int64_t)p * lse_stride + i];
-        if (l != -INFINITY) W += __expf(l - M);
-    }
-    for (int e = threadIdx.x; e < D; e += 128) {
-        float acc = 0.0f;
-        if (M != -INFINITY)
-            for (int p = 0; p < P; ++p) {
-                const float l = lse[(int64_t)p * lse_stride + i];
-                if (l != -INFINITY) acc += __expf(l - M) * o[(int64_t)p * o_stride + i * D + e];
-            }
-        store_out<OT>(out + i * D + e, M == -INFINITY ? 0.0f : acc / W);
-    }
-    if (lse_out && threadIdx.x == 0) lse_out[i] = M == -INFINITY ? -INFINITY : M + __logf(W);
+__global__ void __launch_bounds__(COMBINE_WARPS * 32) lse_combine_kernel(const float* __restrict__ o, int64_t o_stride,
+                                                                        const float* __restrict__ lse, int64_t lse_stride,
+                                                                        OT* __restrict__ out, float* __restrict__ lse_out,
+                                                                        int P, int64_t n, int D) {
+    const int64_t i = (int64_t)blockIdx.x * COMBINE_WARPS + (threadIdx.x >> 5);
+    if (i < n) merge_row<OT>(o, o_stride, lse, lse_stride, P, i, D, out, lse_out, threadIdx.x & 31);
 }
 
 // ── host side ───────────────────────────────────────────────────────────────
@@ -1132,20 +1113,25 @@ cudaError_t launch_decode_attention(const AttnRun& r, const AttnPlan& p, void* w
 
 cudaError_t launch_lse_combine(const float* o, int64_t o_stride, const float* lse, int64_t lse_stride, void* out,
                                int out_dtype, float* lse_out, int P, int64_t n, int D, cudaStream_t st) {
-    for (int64_t r0 = 0; r0 < n; r0 += 1 << 30) {   // grid.x limit
-        const int64_t nr = n - r0 < (1 << 30) ? n - r0 : (1 << 30);
+    const int64_t rows_per_launch = (int64_t(1) << 30) * COMBINE_WARPS;   // grid.x limit
+    for (int64_t r0 = 0; r0 < n; r0 += rows_per_launch) {
+        const int64_t nr = n - r0 < rows_per_launch ? n - r0 : rows_per_launch;
+        const unsigned grid = (unsigned)((nr + COMBINE_WARPS - 1) / COMBINE_WARPS);
         const float* oo = o + r0 * D;
         const float* ll = lse + r0;
         float* lo = lse_out ? lse_out + r0 : nullptr;
         switch (out_dtype) {
             case DT_F32:
-                lse_combine_kernel<float><<<(unsigned)nr, 128, 0, st>>>(oo, o_stride, ll, lse_stride, (float*)out + r0 * D, lo, P, nr, D);
+                lse_combine_kernel<float><<<grid, COMBINE_WARPS * 32, 0, st>>>(oo, o_stride, ll, lse_stride,
+                                                                               (float*)out + r0 * D, lo, P, nr, D);
                 break;
             case DT_F16:
-                lse_combine_kernel<__half><<<(unsigned)nr, 128, 0, st>>>(oo, o_stride, ll, lse_stride, (__half*)out + r0 * D, lo, P, nr, D);
+                lse_combine_kernel<__half><<<grid, COMBINE_WARPS * 32, 0, st>>>(oo, o_stride, ll, lse_stride,
+                                                                                (__half*)out + r0 * D, lo, P, nr, D);
                 break;
             default:
-                lse_combine_kernel<__nv_bfloat16><<<(unsigned)nr, 128, 0, st>>>(oo, o_stride, ll, lse_stride, (__nv_bfloat16*)out + r0 * D, lo, P, nr, D);
+                lse_combine_kernel<__nv_bfloat16><<<grid, COMBINE_WARPS * 32, 0, st>>>(
+                    oo, o_stride, ll, lse_stride, (__nv_bfloat16*)out + r0 * D, lo, P, nr, D);
                 break;
         }
         const cudaError_t e = cudaGetLastError();

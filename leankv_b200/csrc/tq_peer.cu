@@ -40,6 +40,7 @@
 #include "leankv_tq.h"
 #include "tq_attn.h"
 #include "tq_capi_internal.h"
+#include "tq_merge.cuh"
 
 namespace {
 
@@ -53,13 +54,6 @@ constexpr uint32_t PX_DEFAULT_WAIT_MS = 2000;          // bound of the arrival w
 struct PeerBases {
     uint8_t* base[TQ_PEER_MAX_WORLD];
 };
-
-template <typename OT> __device__ __forceinline__ void px_store(OT* p, float v);
-template <> __device__ __forceinline__ void px_store<float>(float* p, float v) { *p = v; }
-template <> __device__ __forceinline__ void px_store<__half>(__half* p, float v) { *p = __float2half_rn(v); }
-template <> __device__ __forceinline__ void px_store<__nv_bfloat16>(__nv_bfloat16* p, float v) {
-    *p = __float2bfloat16_rn(v);
-}
 
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
@@ -118,28 +112,11 @@ __global__ void __launch_bounds__(PX_THREADS) peer_merge_kernel(const float* __r
     __syncthreads();
     if (!s_ok) return;
 
-    // ---- merge: one warp per row, ranks in order (the arithmetic of lse_combine_kernel) ----
+    // ---- merge: one warp per row, ranks in order (merge_row, as lse_combine_kernel) ----
     const float* slots = reinterpret_cast<const float*>(peers.base[rank] + PX_HEAD) + (int64_t)par * world * slot_floats;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int64_t i = (int64_t)blockIdx.x * PX_ROWS_PER_CTA + warp; i < n_rows; i += (int64_t)gridDim.x * PX_ROWS_PER_CTA) {
-        float M = -INFINITY;
-        for (int p = 0; p < world; ++p) M = fmaxf(M, __ldcg(slots + p * slot_floats + n_rows * D + i));
-        float W = 0.0f;
-        for (int p = 0; p < world; ++p) {
-            const float l = __ldcg(slots + p * slot_floats + n_rows * D + i);
-            if (l != -INFINITY) W += __expf(l - M);
-        }
-        for (int e = lane; e < D; e += 32) {
-            float acc = 0.0f;
-            if (M != -INFINITY)
-                for (int p = 0; p < world; ++p) {
-                    const float l = __ldcg(slots + p * slot_floats + n_rows * D + i);
-                    if (l != -INFINITY) acc += __expf(l - M) * __ldcg(slots + p * slot_floats + i * D + e);
-                }
-            px_store<OT>(out + i * D + e, M == -INFINITY ? 0.0f : acc / W);
-        }
-        if (lse_out && lane == 0) lse_out[i] = M == -INFINITY ? -INFINITY : M + __logf(W);
-    }
+    for (int64_t i = (int64_t)blockIdx.x * PX_ROWS_PER_CTA + warp; i < n_rows; i += (int64_t)gridDim.x * PX_ROWS_PER_CTA)
+        tq::merge_row<OT>(slots, slot_floats, slots + n_rows * D, slot_floats, world, i, D, out, lse_out, lane);
 }
 
 }  // namespace

@@ -5,8 +5,8 @@
 
 Workloads (synthetic, seeded; shapes and distributions of the LeanKV configs):
   c4      (default) fused decode attention over a TQ3_0 K / TQ4_0 V cache, B64 Hq64 Hkv8 D128,
-          context 131072; N > 1 ranks split every context by token position and merge the
-          (O, lse) partials over NVLink (peer-memory kernel up to 4 GPUs, NCCL all_gather above)
+          context 131072; N > 1 ranks split every context by token position; the decode kernel
+          stores each finished pair's (O, lse) into every rank's buffer over NVLink, then a merge
   tq3opt  TQ3_0 + optimal rounding (2 CD passes + LS scale), FWHT fused,
           bf16 [32768 tokens, 8 KV heads, 128]: Student-t(4) x per-channel log-normal scales
   tq4     TQ4_0 quantize (FWHT fused) + dequantize of fp32 [4096, 8, 128], N(0,1) with
@@ -762,9 +762,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-API measurement (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the token count (profiling runs)")
     ap.add_argument("--transport", choices=["peer", "peer_merge", "nccl"], default=None,
-                    help="c4 on N > 1 GPUs: rank exchange fused into the attention over NVLink peer memory (peer), "
-                         "a separate peer push + merge kernel (peer_merge) or NCCL all_gather + merge kernel "
-                         "(default: peer up to 4 GPUs, where its parity and timeout tests ran; nccl above)")
+                    help="c4 on N > 1 GPUs: rank exchange fused into the attention over NVLink peer memory (peer, "
+                         "the default; its parity and timeout tests ran on 2, 4 and 8 B200s), a separate peer "
+                         "push + merge kernel (peer_merge) or NCCL all_gather + merge kernel (nccl)")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 3 if args.impl == "reference" else {"attn": 200, "c4": 50, "c5": Stream.DECODE_STEPS}.get(
@@ -773,7 +773,7 @@ def main():
         args.warmup = 3 if args.impl == "reference" else {"c4": 5, "c5": 5}.get(args.workload, 20)
     args.warmup = max(args.warmup, 3)
     if args.transport is None:
-        args.transport = "peer" if int(os.environ.get("WORLD_SIZE", "1")) <= 4 else "nccl"
+        args.transport = "peer"
 
     if args.impl == "reference":
         ws = int(os.environ.get("WORLD_SIZE", "1"))

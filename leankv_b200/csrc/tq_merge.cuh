@@ -42,9 +42,10 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ o, int64_t o
     }
 #pragma unroll
     for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
-    // W in part order; acc of each of this lane's elements in part order.  Rows longer than 256
-    // elements go in chunks of 256 (W is recomputed per chunk, the same value every time).
-    constexpr int MAXE = 8;   // elements per lane and chunk
+    // W in part order; acc of each of this lane's elements in part order.  Rows go in chunks of
+    // 128 elements (4 per lane; W is recomputed per chunk, the same value every time), parts in
+    // groups of 8 whose loads are all issued before the ordered accumulation.
+    constexpr int MAXE = 4, PG = 8;
     float W = 0.0f;
     for (int e0 = 0; e0 < D; e0 += 32 * MAXE) {
         float acc[MAXE];
@@ -55,15 +56,25 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ o, int64_t o
             const float l = p0 + lane < P ? __ldcg(lse + (int64_t)(p0 + lane) * lse_stride + i) : -INFINITY;
             const float w = l != -INFINITY ? __expf(l - M) : 0.0f;
             const int np = P - p0 < 32 ? P - p0 : 32;
-            for (int q = 0; q < np; ++q) {
-                const float wq = __shfl_sync(0xffffffffu, w, q);
-                const float lq = __shfl_sync(0xffffffffu, l, q);
-                if (lq == -INFINITY) continue;   // warp-uniform
-                W += wq;
-                const float* op = o + (int64_t)(p0 + q) * o_stride + i * D + e0;
+            for (int g0 = 0; g0 < np; g0 += PG) {
+                float v[PG][MAXE];
 #pragma unroll
-                for (int k = 0; k < MAXE; ++k)
-                    if (e0 + lane + 32 * k < D) acc[k] = fmaf(wq, __ldcg(op + lane + 32 * k), acc[k]);
+                for (int g = 0; g < PG; ++g) {
+                    const float* op = o + (int64_t)(p0 + g0 + g) * o_stride + i * D + e0;
+#pragma unroll
+                    for (int k = 0; k < MAXE; ++k)
+                        v[g][k] = (g0 + g < np && e0 + lane + 32 * k < D) ? __ldcg(op + lane + 32 * k) : 0.0f;
+                }
+#pragma unroll
+                for (int g = 0; g < PG; ++g) {
+                    if (g0 + g >= np) break;
+                    const float wq = __shfl_sync(0xffffffffu, w, g0 + g);
+                    const float lq = __shfl_sync(0xffffffffu, l, g0 + g);
+                    if (lq == -INFINITY) continue;   // warp-uniform
+                    W += wq;
+#pragma unroll
+                    for (int k = 0; k < MAXE; ++k) acc[k] = fmaf(wq, v[g][k], acc[k]);
+                }
             }
         }
 #pragma unroll

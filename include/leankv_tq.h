@@ -250,7 +250,7 @@ tq_status tq_proto_decode_cuda(const uint8_t *indices, const float *scales, int6
  * (or block_tq3_0), i.e. every token's head row is head_dim/32 consecutive blocks.
  * q / out: [batch][n_q_heads][head_dim].  lse (optional): [batch][n_q_heads],
  * natural log of sum_t exp(s_t); -inf and a zero output for kv_len == 0.
- * Requirements: head_dim 128 or 256; n_q_heads / n_kv_heads in {1, 2, 4, 8};
+ * Requirements: head_dim 128 or 256; n_q_heads / n_kv_heads in 1 .. 8;
  * kv_capacity even; cache pointers 16-byte aligned.  Block types: K TQ4_0 or
  * TQ3_0, V TQ4_0.  Work memory: tq_decode_attention_workspace_size() bytes of
  * device memory; its first int32 receives the kernel-side status (TQ_SUCCESS,

@@ -361,7 +361,10 @@ __device__ __forceinline__ void pair_sync(int ring) {
     asm volatile("bar.sync %0, 64;" ::"r"(ring + 1) : "memory");
 }
 
-template <int D, int KT, int RES>
+// PK (GQA group of at most 4 query heads): the score mma's 8 columns hold the group's q~ hi parts
+// in columns 0-3 and its lo parts in columns 4-7, so one mma per chunk forms both products and one
+// shuffle per score adds them; larger groups run a second mma per chunk with the lo parts.
+template <int D, int KT, int RES, bool PK>
 __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const AttnKernelArgs a) {
     using Cfg = AttnCfg<D, KT>;
     constexpr int WARPS = Cfg::WARPS, THREADS = Cfg::THREADS;
@@ -535,7 +538,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                         make_float4(qv[i] * a.qscale, qv[i + 1] * a.qscale, qv[i + 2] * a.qscale, qv[i + 3] * a.qscale);
             }
             __syncthreads();
-            const float* mq = sq + gq * SQS;
+            const float* mq = sq + (PK ? (gq & 3) : gq) * SQS;
 #pragma unroll
             for (int kk = 0; kk < NCH; ++kk) {
                 const int blk = half * NBLK + (kk >> 1), h = kk & 1;   // block of the token row
@@ -548,7 +551,14 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     split_h2(mq[e0], mq[e0 + 1], qf[kk][0], qfl[kk][0]);
                     split_h2(mq[e0 + 2], mq[e0 + 3], qf[kk][1], qfl[kk][1]);
                 }
-                if (SPLIT == 2 && ring == 0) s_qfl[(half * NCH + kk) * 32 + lane] = make_uint2(qfl[kk][0], qfl[kk][1]);
+                if constexpr (PK) {        // columns 4-7 carry the lo parts of heads 0-3
+                    if (gq >= 4) {
+                        qf[kk][0] = qfl[kk][0];
+                        qf[kk][1] = qfl[kk][1];
+                    }
+                } else {
+                    if (SPLIT == 2 && ring == 0) s_qfl[(half * NCH + kk) * 32 + lane] = make_uint2(qfl[kk][0], qfl[kk][1]);
+                }
             }
             __syncthreads();   // q~ read by all warps before the scale scratch is reused
         }
@@ -600,6 +610,13 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     return make_uint2(qfl[kk][0], qfl[kk][1]);
                 }
             };
+            // the second mma of a chunk, with q~'s lo parts (groups above 4 only)
+            auto lo_mma = [&](float (&acc)[4], const uint32_t (&af)[4], int kk) {
+                if constexpr (!PK) {
+                    const uint2 ql = qlo(kk);
+                    mma16816(acc, af, ql.x, ql.y);
+                }
+            };
             static_for<0, NBLK>([&](auto blk_c) {
                 constexpr int blk = decltype(blk_c)::value;
                 float acc[4];
@@ -612,13 +629,13 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
                     mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
-                    { const uint2 ql = qlo(2 * blk); mma16816(acc, af, ql.x, ql.y); }
+                    lo_mma(acc, af, 2 * blk);
                     af[0] = lut_ld<RES>(w0, lane4, LUT_SEL2);
                     af[1] = lut_ld<RES>(w1, lane4, LUT_SEL2);
                     af[2] = lut_ld<RES>(w0, lane4, LUT_SEL3);
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL3);
                     mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
-                    { const uint2 ql = qlo(2 * blk + 1); mma16816(acc, af, ql.x, ql.y); }
+                    lo_mma(acc, af, 2 * blk + 1);
                 } else if constexpr (KT == 4) {
                     const uint32_t kr = st + k_off;
                     uint32_t w0 = ld16<blk * TQ4_BYTES>(kr), w1 = ld16<blk * TQ4_BYTES + KROW8>(kr);
@@ -627,7 +644,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
                     mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
-                    { const uint2 ql = qlo(2 * blk); mma16816(acc, af, ql.x, ql.y); }
+                    lo_mma(acc, af, 2 * blk);
                     w0 = ld16<blk * TQ4_BYTES + 8>(kr);
                     w1 = ld16<blk * TQ4_BYTES + 8 + KROW8>(kr);
                     af[0] = lut_ld<RES>(w0, lane4, LUT_SEL0);
@@ -635,7 +652,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[2] = lut_ld<RES>(w0, lane4, LUT_SEL1);
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
                     mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
-                    { const uint2 ql = qlo(2 * blk + 1); mma16816(acc, af, ql.x, ql.y); }
+                    lo_mma(acc, af, 2 * blk + 1);
                 } else {
                     constexpr int IMM = blk * TQ3_BYTES - 2 * (blk & 1);
                     const uint32_t kr = st + ((blk & 1) ? k3_off_o : k3_off_e);
@@ -647,19 +664,23 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[2] = lut_ld_addr<RES>(tq3_lut_addr<1>(wg, lane4x));
                     af[3] = lut_ld_addr<RES>(tq3_lut_addr<1>(wh, lane4x));
                     mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
-                    { const uint2 ql = qlo(2 * blk); mma16816(acc, af, ql.x, ql.y); }
+                    lo_mma(acc, af, 2 * blk);
                     af[0] = lut_ld_addr<RES>(tq3_lut_addr<2>(wg, lane4x));
                     af[1] = lut_ld_addr<RES>(tq3_lut_addr<2>(wh, lane4x));
                     af[2] = lut_ld_addr<RES>(tq3_lut_addr<3>(wg, lane4x));
                     af[3] = lut_ld_addr<RES>(tq3_lut_addr<3>(wh, lane4x));
                     mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
-                    { const uint2 ql = qlo(2 * blk + 1); mma16816(acc, af, ql.x, ql.y); }
+                    lo_mma(acc, af, 2 * blk + 1);
                 }
                 sc[0] = fmaf(dka[blk], acc[0], sc[0]);
                 sc[1] = fmaf(dka[blk], acc[1], sc[1]);
                 sc[2] = fmaf(dkb[blk], acc[2], sc[2]);
                 sc[3] = fmaf(dkb[blk], acc[3], sc[3]);
             });
+            if constexpr (PK) {   // head h's score = column h (hi) + column h + 4 (lo): lanes t and t ^ 2
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], 2);
+            }
             if (valid < ATT_TILE) {
                 if (Cfg::tok_of_row(gq) >= valid) { sc[0] = -INFINITY; sc[1] = -INFINITY; }
                 if (Cfg::tok_of_row(gq + 8) >= valid) { sc[2] = -INFINITY; sc[3] = -INFINITY; }
@@ -1043,27 +1064,32 @@ static int reserved_smem() {
     return cached[dev];
 }
 
-template <int D, int KT, int RES>
+template <int D, int KT, int RES, bool PK>
 static cudaError_t launch_decode_kernel(const AttnKernelArgs& a, int grid, cudaStream_t st) {
     const size_t smem = decode_smem_bytes<D, KT>();
     // the shared-memory opt-in is set once per device, so that later calls (for example
     // inside a CUDA graph capture) issue only stream work
-    static bool attr_set[64] = {};
+    static bool attr_set[64] = {};   // one per instantiation
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(attn_decode_kernel<D, KT, RES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        e = cudaFuncSetAttribute(attn_decode_kernel<D, KT, RES, PK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    attn_decode_kernel<D, KT, RES><<<grid, AttnCfg<D, KT>::THREADS, smem, st>>>(a);
+    attn_decode_kernel<D, KT, RES, PK><<<grid, AttnCfg<D, KT>::THREADS, smem, st>>>(a);
     return cudaGetLastError();
 }
 
 template <int D, int RES>
 static cudaError_t launch_decode_kt(const AttnKernelArgs& a, int k_type, int grid, cudaStream_t st) {
-    return k_type == 4 ? launch_decode_kernel<D, 4, RES>(a, grid, st) : launch_decode_kernel<D, 3, RES>(a, grid, st);
+    if (a.grp <= 4)
+        return k_type == 4 ? launch_decode_kernel<D, 4, RES, true>(a, grid, st)
+                           : launch_decode_kernel<D, 3, RES, true>(a, grid, st);
+    return k_type == 4 ? launch_decode_kernel<D, 4, RES, false>(a, grid, st)
+                       : launch_decode_kernel<D, 3, RES, false>(a, grid, st);
 }
 
 template <int D>

@@ -15,8 +15,7 @@ tq_status tq::attn_check(const tq_decode_attention_args* a, AttnRun* r, AttnPlan
         return set_error(TQ_ERROR_INVALID_VALUE, "bad batch / head counts");
     if (a->n_q_heads % a->n_kv_heads) return set_error(TQ_ERROR_INVALID_VALUE, "n_q_heads %% n_kv_heads != 0");
     const int grp = a->n_q_heads / a->n_kv_heads;
-    if (grp != 1 && grp != 2 && grp != 4 && grp != 8)
-        return set_error(TQ_ERROR_UNSUPPORTED, "GQA group size %d (supported: 1, 2, 4, 8)", grp);
+    if (grp > 8) return set_error(TQ_ERROR_UNSUPPORTED, "GQA group size %d (supported: 1 .. 8)", grp);
     if (a->head_dim != 128 && a->head_dim != 256)
         return set_error(TQ_ERROR_UNSUPPORTED, "head_dim %d (supported: 128, 256)", a->head_dim);
     if ((a->k_type != TQ_TYPE_TQ4_0 && a->k_type != TQ_TYPE_TQ3_0) || a->v_type != TQ_TYPE_TQ4_0)

@@ -57,7 +57,7 @@ def check(out, ref, lse=None, lse_ref=None):
     return err / max(np.abs(ref).max(), 1e-30)
 
 
-@pytest.mark.parametrize("grp", [1, 2, 4, 8])
+@pytest.mark.parametrize("grp", [1, 2, 3, 4, 6, 8])
 def test_attention_vs_oracle_grp(orc, grp):
     B, Hkv, T, D = 2, 2, 700, 128
     Hq = Hkv * grp
@@ -194,7 +194,7 @@ def test_split_by_sequence_combine_equals_full(orc):
     check(comb.cpu().numpy(), full.cpu().numpy())
 
 
-@pytest.mark.parametrize("grp", [1, 2, 4, 8])
+@pytest.mark.parametrize("grp", [1, 2, 3, 4, 8])
 def test_attention_tq3_k_vs_oracle(orc, grp):
     """Mixed TQ3_0 K / TQ4_0 V caches (the long-context split-sequence layout)."""
     B, Hkv, T, D = 2, 2, 900, 128
@@ -225,7 +225,7 @@ def test_attention_head_dim_256(orc, kt, T, lens):
     print(f"D256 K TQ{kt} T {T}: rel err {rel:.3g}")
 
 
-@pytest.mark.parametrize("grp", [1, 2, 8])
+@pytest.mark.parametrize("grp", [1, 2, 3, 8])
 @pytest.mark.parametrize("kt", [4, 3])
 def test_attention_head_dim_256_grp(orc, kt, grp):
     """head_dim 256 with GQA groups 1, 2 and 8 (group 4 above), f32 q, no rotation of q."""

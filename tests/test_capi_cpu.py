@@ -113,6 +113,8 @@ def test_attention_argument_errors():
     a.k_type = a.v_type = 4
     a.kv_capacity = 64
     assert lib.tq_decode_attention_cuda(C.byref(a), None) == 1
+    a.n_q_heads = 72                                                         # group 9
+    assert lib.tq_decode_attention_cuda(C.byref(a), None) == 2
     a.n_q_heads = 64                                                         # group 8 ok, head_dim 64 not
     a.head_dim = 64
     assert lib.tq_decode_attention_cuda(C.byref(a), None) == 2

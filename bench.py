@@ -304,7 +304,7 @@ class Attn:
     Both keep the total work fixed as ranks are added ("strong" scaling).
     """
 
-    def __init__(self, name, rank, ws, tokens=None, transport="nccl"):
+    def __init__(self, name, rank, ws, tokens=None, transport="nccl", page_size=0, page_order="shuffled"):
         import torch
         from leankv_b200 import attention, distributed, ops
         self.attention = attention
@@ -327,6 +327,24 @@ class Attn:
             for b in range(Bl):
                 ops.quantize(_outlier_rows(g, (Hkv, L, D), D), qt, fwht_head_dim=D, out=cache[b])
         self.kc, self.vc = kc, vc
+        self.page_size = page_size
+        if page_size:
+            # paged layout: the same token rows moved into page pools in a shuffled page order
+            if L % page_size or (name == "c4" and ws > 1):
+                raise SystemExit("--page-size needs a context that is a multiple of it (and one rank for c4)")
+            npp = L // page_size
+            perm = (torch.randperm(Bl * npp, generator=torch.Generator().manual_seed(6)) if page_order == "shuffled"
+                    else torch.arange(Bl * npp)).cuda()
+            self.table = perm.view(Bl, npp).to(torch.int32).contiguous()
+            pools = []
+            for c in (kc, vc):
+                pool = torch.empty((Bl * npp, Hkv, page_size) + tuple(c.shape[3:]), dtype=torch.uint8, device="cuda")
+                pool[perm] = c.view(Bl, Hkv, npp, page_size, *c.shape[3:]).transpose(1, 2).reshape(pool.shape)
+                pools.append(pool)
+            del kc, vc
+            self.kc, self.vc = pools
+            self.plens = torch.full((Bl,), L, dtype=torch.int32, device="cuda")
+            torch.cuda.empty_cache()
         gq = torch.Generator(device="cuda").manual_seed(5)           # the same queries on every rank
         qfull = torch.randn(B, Hq, D, generator=gq, device="cuda").half()
         self.q = qfull[b0:b1].contiguous()
@@ -336,7 +354,7 @@ class Attn:
         if self.split:
             self.att = distributed.SplitSequenceAttention(transport=transport)
             self.lens = torch.full((Bl,), L, dtype=torch.int32, device="cuda")
-        kv_bytes = kc.numel() + vc.numel()
+        kv_bytes = self.kc.numel() + self.vc.numel()
         self.bytes_per_step = kv_bytes + self.q.numel() * 2 + self.out.numel() * 2          # this rank
         kv_total = B * Hkv * T * (D // 32) * (kb + 18)
         self.job_bytes = kv_total + B * Hq * D * 2 * 2                                       # all ranks
@@ -351,6 +369,9 @@ class Attn:
         else:
             self.config = {"workload": WORKLOAD["c4"],
                            "shape": f"B={B} Hq={Hq} Hkv={Hkv} D={D} ctx={T}, fp16 q/out", "kv_bytes": kv_total}
+        if page_size:
+            self.config["cache_layout"] = (f"paged: {page_size}-token pages of every KV head in page pools, "
+                                           f"pages in {page_order} order through a page table")
             self.parallelism = (f"token shards x{ws} ({L} tokens per rank); " + (
                 "all_gather of packed (O, lse) over NCCL + LSE merge on every rank" if transport == "nccl" else
                 "exchange fused into the decode kernel: each pair's (O, lse) stored into every rank's buffer over "
@@ -365,6 +386,9 @@ class Attn:
     def step(self):
         if self.split:
             self.att(self.q, self.kc, self.vc, self.lens, self.L, out=self.out)
+        elif self.page_size:
+            self.attention.decode_attention_paged(self.q, self.kc, self.vc, self.table, kv_len=self.plens,
+                                                  max_kv_len=self.L, out=self.out)
         else:
             self.attention.decode_attention(self.q, self.kc, self.vc, out=self.out)
 
@@ -517,9 +541,9 @@ class Stream:
 
 
 
-def make_workload(name, rank, tokens, ws=1, layers=None, transport="nccl"):
+def make_workload(name, rank, tokens, ws=1, layers=None, transport="nccl", page_size=0, page_order="shuffled"):
     if name in ("attn", "c4"):
-        return Attn(name, rank, ws, tokens, transport)
+        return Attn(name, rank, ws, tokens, transport, page_size, page_order)
     if name == "c5":
         return Stream(rank, ws, tokens, layers)
     return Codec(name, rank, tokens)
@@ -611,7 +635,8 @@ def time_cpu_sample(wl: str, nthreads: int, warmup: int = 1, steps: int = 1):
 
 def run_ours(args, ws, rank, local):
     import torch
-    wl = make_workload(args.workload, rank, args.tokens, ws, args.layers, args.transport)
+    wl = make_workload(args.workload, rank, args.tokens, ws, args.layers, args.transport, args.page_size,
+                       args.page_order)
     if isinstance(wl, Stream):
         budget = wl.remaining() - (0 if args.no_e2e else min(args.steps, 20) + 1)
         if args.warmup + args.steps > budget:
@@ -765,6 +790,11 @@ def main():
                     help="c4 on N > 1 GPUs: rank exchange fused into the attention over NVLink peer memory (peer, "
                          "the default; its parity and timeout tests ran on 2, 4 and 8 B200s), a separate peer "
                          "push + merge kernel (peer_merge) or NCCL all_gather + merge kernel (nccl)")
+    ap.add_argument("--page-size", type=int, default=0,
+                    help="attn / c4 on one GPU: run the paged decode attention over the same cache stored as "
+                         "pages of this many tokens (a power of two, >= 16)")
+    ap.add_argument("--page-order", choices=["shuffled", "sequential"], default="shuffled",
+                    help="with --page-size: pool pages in a random order, or in sequence order (a fresh pool)")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 3 if args.impl == "reference" else {"attn": 200, "c4": 50, "c5": Stream.DECODE_STEPS}.get(

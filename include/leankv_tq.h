@@ -296,6 +296,43 @@ tq_status tq_decode_attention_cuda(const tq_decode_attention_args *a, void *stre
 #define TQ_STATIC_SCRATCH_BYTES (16u << 20)
 tq_status tq_decode_attention_static_cuda(const tq_decode_attention_args *a, void *stream);
 
+/*
+ * Paged KV caches (no counterpart in the reference; the page-table layout of
+ * paged serving caches).  K and V each live in a pool of pages; a page holds
+ * page_size consecutive token rows of every KV head of one sequence:
+ *   pool [num_pages][n_kv_heads][page_size][head_dim/32 blocks]
+ * and page_table[b * max_pages_per_seq + i] is the pool page holding tokens
+ * [i * page_size, (i + 1) * page_size) of sequence b.  page_size is a power of
+ * two, 16 .. 65536 tokens (a 16-token tile of the kernel never crosses a page).
+ * A page id outside [0, num_pages) met by the attention kernel is reported as
+ * TQ_ERROR_INVALID_VALUE in its status word (that tile reads page 0 instead);
+ * the append kernel does not write a row whose page id is outside the pool and
+ * counts it as an overflow.  The page table is device memory.
+ */
+typedef struct {
+    const int32_t *page_table;   /* device [batch][max_pages_per_seq] */
+    int64_t max_pages_per_seq;
+    int64_t num_pages;           /* pages in each pool, at most 2^31 - 1 */
+    int page_size;               /* tokens per page */
+} tq_kv_pages;
+
+/* Decode attention over paged K/V pools: the arguments of tq_decode_attention_cuda
+ * with a->k_cache / a->v_cache pointing at the pools and a->kv_capacity equal to
+ * max_pages_per_seq * page_size (tq_decode_attention_workspace_size then sizes
+ * the work memory).  Results are bit-identical to tq_decode_attention_cuda on the
+ * same tokens stored contiguously. */
+tq_status tq_decode_attention_paged_cuda(const tq_decode_attention_args *a, const tq_kv_pages *pages, void *stream);
+
+/* Quantize-on-write into a paged cache: tq_kv_append_cuda with the token slot
+ * pos[b] + t of row t of (b, h) placed through the page table (capacity =
+ * max_pages_per_seq * page_size).  Rows whose slot is outside the capacity or
+ * whose page id is outside the pool are not written and are counted in
+ * *overflow when overflow is not NULL. */
+tq_status tq_kv_append_paged_cuda(tq_type type, const void *src, tq_dtype src_dtype, void *pool, int batch,
+                                  int n_kv_heads, int head_dim, const tq_kv_pages *pages, int64_t n_new,
+                                  const int32_t *pos, int rotate, int opt_passes, int32_t *overflow,
+                                  void *stream);
+
 /* log-sum-exp merge of n_parts partial results o[n_parts][n_rows][head_dim] with
  * natural-log lse[n_parts][n_rows] into out[n_rows][head_dim] (+ lse_out, optional):
  * the split-by-sequence combine of the multi-GPU path (new) */

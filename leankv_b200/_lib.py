@@ -78,6 +78,7 @@ SIGNATURES = {
     "tq_decode_attention_workspace_size": (C.c_size_t, [_v]),
     "tq_decode_attention_cuda": (_i32, [_v, _v]),
     "tq_decode_attention_static_cuda": (_i32, [_v, _v]),
+    "tq_decode_attention_paged_cuda": (_i32, [_v, _v, _v]),
     "tq_lse_combine_cuda": (_i32, [_i32, _i64, _i32, _v, _v, _v, _v, _v]),
     "tq_lse_merge_cuda": (_i32, [_i32, _i64, _i32, _v, _i64, _v, _i64, _v, _i32, _v, _v]),
     # outlier channels (mixed precision); config pointers are host struct pointers
@@ -97,6 +98,7 @@ SIGNATURES = {
     "tq_proto_decode_cuda": (_i32, [_v, _v, _i64, _i32, _i32, _v, _v, _i32, _v, _i32, _v, _v, _v]),
     # KV-cache append
     "tq_kv_append_cuda": (_i32, [_i32, _v, _i32, _v, _i32, _i32, _i32, _i64, _i64, _v, _i32, _i32, _v, _v]),
+    "tq_kv_append_paged_cuda": (_i32, [_i32, _v, _i32, _v, _i32, _i32, _i32, _v, _i64, _v, _i32, _i32, _v, _v]),
     # split-sequence merge over peer memory (exchange handles are opaque pointers)
     "tq_peer_exchange_create": (_i32, [_i32, _i32, _i64, _i32, C.c_uint32, _v, _v]),
     "tq_peer_exchange_connect": (_i32, [_v, _v]),

@@ -35,12 +35,29 @@ class AttnArgs(C.Structure):
     ]
 
 
+class KVPages(C.Structure):
+    """Mirror of tq_kv_pages (include/leankv_tq.h): a paged cache's page table."""
+    _fields_ = [("page_table", C.c_void_p), ("max_pages_per_seq", C.c_int64), ("num_pages", C.c_int64),
+                ("page_size", C.c_int)]
+
+
+def make_pages(page_table: torch.Tensor, num_pages: int, page_size: int) -> KVPages:
+    pg = KVPages()
+    pg.page_table = page_table.data_ptr()
+    pg.max_pages_per_seq = page_table.shape[1]
+    pg.num_pages = int(num_pages)
+    pg.page_size = int(page_size)
+    return pg
+
+
 def _bind():
     lib = L.load()
     lib.tq_decode_attention_workspace_size.restype = C.c_size_t
     lib.tq_decode_attention_workspace_size.argtypes = [C.POINTER(AttnArgs)]
     lib.tq_decode_attention_cuda.restype = C.c_int
     lib.tq_decode_attention_cuda.argtypes = [C.POINTER(AttnArgs), C.c_void_p]
+    lib.tq_decode_attention_paged_cuda.restype = C.c_int
+    lib.tq_decode_attention_paged_cuda.argtypes = [C.POINTER(AttnArgs), C.POINTER(KVPages), C.c_void_p]
     lib.tq_lse_combine_cuda.restype = C.c_int
     lib.tq_lse_combine_cuda.argtypes = [C.c_int, C.c_int64, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                         C.c_void_p, C.c_void_p]
@@ -90,32 +107,11 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     (default: the capacity).  out / lse_out: preallocated contiguous [B, Hq, D]
     and float32 [B, Hq] destinations (lse_out implies the lse is written).
     """
-    _need_cuda(q, k_cache, v_cache)
-    if q.dim() != 3 or not q.is_contiguous():
-        raise ValueError("q must be a contiguous [B, Hq, D] tensor")
-    if k_cache.dtype != torch.uint8 or v_cache.dtype != torch.uint8:
-        raise ValueError("caches must be uint8 block tensors")
-    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
-        raise ValueError("caches must be contiguous")
-    if kv_len is not None:
-        _need_cuda(kv_len)
-        if kv_len.dtype != torch.int32 or kv_len.numel() != q.shape[0]:
-            raise ValueError("kv_len must be int32 [batch]")
-        kv_len = kv_len.contiguous()
-    B, Hq, D = q.shape
-    if out is None:
-        out = torch.empty((B, Hq, D), dtype=out_dtype, device=q.device)
-    if lse_out is not None:
-        _need_cuda(lse_out)
-        if lse_out.dtype != torch.float32 or lse_out.numel() != B * Hq or not lse_out.is_contiguous():
-            raise ValueError("lse_out must be a contiguous float32 [B, Hq] tensor")
-        lse = lse_out
-    else:
-        lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device) if return_lse else None
-    k_type = 4 if k_cache.shape[-1] == 18 else 3
-    v_type = 4 if v_cache.shape[-1] == 18 else 3
+    _check_caches(q, k_cache, v_cache)
+    kv_len = _check_len(kv_len, q.shape[0])
+    out, lse = _outputs(q, out_dtype, out, lse_out, return_lse)
     a = make_args(q, k_cache, v_cache, kv_len, max_kv_len or 0, sm_scale or 0.0, rotate_q, v_rotated, out, lse,
-                  k_type, v_type)
+                  _btype(k_cache), _btype(v_cache))
     lib = _bind()
     need = lib.tq_decode_attention_workspace_size(C.byref(a))
     if need == 0:
@@ -125,6 +121,76 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     L.check(lib.tq_decode_attention_cuda(C.byref(a), _stream(q)))
     return (out, lse) if return_lse else out
+
+
+def decode_attention_paged(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, page_table: torch.Tensor,
+                           kv_len: torch.Tensor, max_kv_len: int | None = None, sm_scale: float | None = None,
+                           rotate_q: bool = True, v_rotated: bool = True, out_dtype: torch.dtype = torch.float32,
+                           return_lse: bool = False, out: torch.Tensor | None = None,
+                           lse_out: torch.Tensor | None = None):
+    """decode_attention over paged caches (tq_decode_attention_paged_cuda).
+
+    k_pool / v_pool: uint8 [num_pages, n_kv_heads, page_size, head_dim/32, bytes];
+    page_table: int32 CUDA [B, max_pages_per_seq], row b listing the pool pages of
+    sequence b's tokens in order; kv_len: int32 CUDA [B].  Bit-identical to
+    decode_attention on the same tokens stored contiguously.
+    """
+    _check_caches(q, k_pool, v_pool)
+    kv_len = _check_len(kv_len, q.shape[0])
+    _need_cuda(page_table)
+    if page_table.dtype != torch.int32 or page_table.dim() != 2 or page_table.shape[0] != q.shape[0] \
+            or not page_table.is_contiguous():
+        raise ValueError("page_table must be a contiguous int32 [batch, max_pages_per_seq] tensor")
+    if k_pool.shape[:3] != v_pool.shape[:3]:
+        raise ValueError("K and V pools must have the same pages, heads and page size")
+    num_pages, _, page_size = k_pool.shape[:3]
+    out, lse = _outputs(q, out_dtype, out, lse_out, return_lse)
+    a = make_args(q, k_pool, v_pool, kv_len, max_kv_len or 0, sm_scale or 0.0, rotate_q, v_rotated, out, lse,
+                  _btype(k_pool), _btype(v_pool))
+    a.kv_capacity = page_table.shape[1] * page_size
+    pg = make_pages(page_table, num_pages, page_size)
+    lib = _bind()
+    need = lib.tq_decode_attention_workspace_size(C.byref(a))
+    if need:
+        ws = _workspace(q.device, need)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    L.check(lib.tq_decode_attention_paged_cuda(C.byref(a), C.byref(pg), _stream(q)))
+    return (out, lse) if return_lse else out
+
+
+def _btype(cache: torch.Tensor) -> int:
+    return 4 if cache.shape[-1] == 18 else 3
+
+
+def _check_caches(q, k_cache, v_cache) -> None:
+    _need_cuda(q, k_cache, v_cache)
+    if q.dim() != 3 or not q.is_contiguous():
+        raise ValueError("q must be a contiguous [B, Hq, D] tensor")
+    if k_cache.dtype != torch.uint8 or v_cache.dtype != torch.uint8:
+        raise ValueError("caches must be uint8 block tensors")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("caches must be contiguous")
+
+
+def _check_len(kv_len, batch):
+    if kv_len is None:
+        return None
+    _need_cuda(kv_len)
+    if kv_len.dtype != torch.int32 or kv_len.numel() != batch:
+        raise ValueError("kv_len must be int32 [batch]")
+    return kv_len.contiguous()
+
+
+def _outputs(q, out_dtype, out, lse_out, return_lse):
+    B, Hq, D = q.shape
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=out_dtype, device=q.device)
+    if lse_out is not None:
+        _need_cuda(lse_out)
+        if lse_out.dtype != torch.float32 or lse_out.numel() != B * Hq or not lse_out.is_contiguous():
+            raise ValueError("lse_out must be a contiguous float32 [B, Hq] tensor")
+        return out, lse_out
+    return out, (torch.empty((B, Hq), dtype=torch.float32, device=q.device) if return_lse else None)
 
 
 def last_status(device: torch.device | str | int | None = None) -> int:

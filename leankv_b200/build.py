@@ -9,6 +9,7 @@ with the source tree; nothing is installed into site-packages.
 from __future__ import annotations
 
 import argparse
+import concurrent.futures
 import glob
 import os
 import shutil
@@ -56,9 +57,9 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     os.makedirs(OUT_DIR, exist_ok=True)
     objdir = os.path.join(OUT_DIR, "obj")
     os.makedirs(objdir, exist_ok=True)
-    objs = []
     nv = nvcc()
-    for src in sources():
+
+    def compile_one(src: str) -> str:
         obj = os.path.join(objdir, os.path.basename(src) + ".o")
         cmd = [nv, *ARCH, *NVCC_FLAGS, *(extra or []), "-I", INCLUDE, "-I", CSRC, "-c", src, "-o", obj]
         if verbose:
@@ -69,7 +70,12 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
             raise RuntimeError(f"nvcc failed on {os.path.basename(src)}")
         if verbose and (r.stdout or r.stderr):
             sys.stderr.write(r.stdout + r.stderr)
-        objs.append(obj)
+        return obj
+
+    # translation units compile independently; the largest (the attention kernels) sets the time
+    srcs = sorted(sources(), key=os.path.getsize, reverse=True)
+    with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, min(len(srcs), os.cpu_count() or 1))) as ex:
+        objs = list(ex.map(compile_one, srcs))
     tmp = LIB + ".tmp"
     cmd = [nv, *ARCH, "-shared", "-o", tmp, *objs, "-lcuda"]
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -223,6 +223,11 @@ struct AttnKernelArgs {
     int B, Hq, Hkv, grp, slots;
     int q_dtype, out_dtype, rotate_q, v_rotated;
     PeerOut peer;               // world 0: write out / lse; else store rows into every rank's slot
+    const int32_t* pages;       // paged caches: [B][max_pages] pool pages (kernel template PG)
+    int64_t max_pages, num_pages;
+    int page_shift;             // log2 tokens per page, >= 4 (a 16-token tile never crosses a page)
+    uint32_t page_mask;         // (1 << page_shift) - 1
+    uint32_t page_kbytes, page_vbytes;   // bytes of one K / V pool page: (Hkv << page_shift) rows
 };
 
 template <int RES>
@@ -364,7 +369,8 @@ __device__ __forceinline__ void pair_sync(int ring) {
 // PK (GQA group of at most 4 query heads): the score mma's 8 columns hold the group's q~ hi parts
 // in columns 0-3 and its lo parts in columns 4-7, so one mma per chunk forms both products and one
 // shuffle per score adds them; larger groups run a second mma per chunk with the lo parts.
-template <int D, int KT, int RES, bool PK>
+// PG: paged caches; the issuing lane looks up each tile's pool page two tiles ahead of its copy.
+template <int D, int KT, int RES, bool PK, bool PG>
 __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const AttnKernelArgs a) {
     using Cfg = AttnCfg<D, KT>;
     constexpr int WARPS = Cfg::WARPS, THREADS = Cfg::THREADS;
@@ -387,6 +393,8 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
     // head_dim 256: the lo parts of q~'s B fragments, [half][chunk][lane], one copy per half of the
     // dimensions (every warp of a half holds the same ones), read per chunk instead of held in registers
     uint2* s_qfl = reinterpret_cast<uint2*>(s_abort + 4);
+    // paged caches: the pool pages of the next tile of each stage of each ring, [ring][stage]
+    int32_t* const s_pgs_all = reinterpret_cast<int32_t*>(s_qfl + (SPLIT == 2 ? 2 * NCH * 32 : 0));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ring = warp / SPLIT, half = warp % SPLIT;   // tile stream, half of the dimensions
@@ -469,8 +477,8 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         const int ntiles_seg = t1 > t0 ? (int)((t1 - t0 + ATT_TILE - 1) / ATT_TILE) : 0;
         const int ntiles = ntiles_seg > ring ? (ntiles_seg - ring + RINGS - 1) / RINGS : 0;
 
-        const uint8_t* kbase = a.k + (size_t)pair * a.cap * KB;
-        const uint8_t* vbase = a.v + (size_t)pair * a.cap * VB;
+        const uint8_t* kbase = a.k + (PG ? 0 : (size_t)pair * a.cap * KB);
+        const uint8_t* vbase = a.v + (PG ? 0 : (size_t)pair * a.cap * VB);
 
         float o[NMT][4];
 #pragma unroll
@@ -483,15 +491,58 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         const int64_t tok_first = t0 + (int64_t)ring * ATT_TILE;      // first token of tile 0
         // tokens of the last tile that exist in memory (capacity), for the copy size
         const int64_t t_last = tok_first + (int64_t)(ntiles > 0 ? ntiles - 1 : 0) * RINGS * ATT_TILE;
-        const uint32_t last_nt = (uint32_t)(a.cap - t_last < ATT_TILE ? a.cap - t_last : ATT_TILE);
+        const uint32_t last_nt = PG ? (uint32_t)ATT_TILE   // pages hold whole tiles
+                                    : (uint32_t)(a.cap - t_last < ATT_TILE ? a.cap - t_last : ATT_TILE);
         // tokens of the last tile below the valid length (tiles before it are full)
         const int last_valid = (int)(t1 - t_last < ATT_TILE ? t1 - t_last : ATT_TILE);
         int issued = 0;
+        // paged: slot S of this ring's page slots holds the pool page of the next tile copied into
+        // stage S.  The issuing lane fetches it with an asynchronous 4-byte copy (cp.async) when the
+        // stage's previous tile is issued, four tiles ahead, one commit group per tile, and waits
+        // for the group only when it issues the tile; a page id outside the pool is reported
+        // (TQ_ERROR_INVALID_VALUE) and read as page 0.  (32-bit token offsets: the host keeps paged
+        // capacities below 2^31 tokens.)
+        const bool issuer = lane == 0 && half == 0;
+        const int64_t pseq = PG ? pair / a.Hkv : 0;
+        const uint32_t prow = PG ? (uint32_t)(pseq * a.max_pages) : 0u;                 // page-table row
+        const uint32_t hrow = PG ? (uint32_t)(pair - pseq * a.Hkv) << a.page_shift : 0u;   // head's first row
+        const uint32_t tok0 = (uint32_t)tok_first;
+        const uint32_t s_pgs = smem_u32(s_pgs_all + ring * ATT_STAGES);
+        // the page id of the tile starting at token `tok` (tile j) -> slot, then a commit; every lane
+        // runs it (no divergent branch in the tile loop), the copy is predicated on the issuing lane
+        auto page_fetch = [&](uint32_t tok, int j, int slot) {
+            const int32_t* src = a.pages + (prow + (tok >> a.page_shift));
+            asm volatile("{\n\t.reg .pred p;\n\t"
+                         "setp.ne.u32 p, %2, 0;\n\t"
+                         "@p cp.async.ca.shared.global [%0], [%1], 4;\n\t"
+                         "cp.async.commit_group;\n\t}"
+                         ::"r"(s_pgs + 4u * slot), "l"(src), "r"((uint32_t)(issuer && j < ntiles)) : "memory");
+        };
+        if constexpr (PG) {
+#pragma unroll
+            for (int j = 0; j < ATT_STAGES; ++j) page_fetch(tok0 + (uint32_t)j * (RINGS * ATT_TILE), j, j);
+        }
         auto issue_next = [&](auto stage_c) {
             constexpr int S = decltype(stage_c)::value;
             const bool last = issued == ntiles - 1;
             const uint32_t nt = last ? last_nt : (uint32_t)ATT_TILE;
-            bool go = lane == 0 && half == 0 && issued < ntiles;
+            if constexpr (PG) {   // tile `issued` goes into stage S = issued mod 4 (every lane runs this)
+                const uint32_t tok = tok0 + (uint32_t)issued * (RINGS * ATT_TILE);
+                // groups of tiles issued + 1 .. issued + 3 may still be in flight
+                asm volatile("cp.async.wait_group 3;" ::: "memory");
+                uint32_t pg;
+                asm volatile("ld.shared.u32 %0, [%1];" : "=r"(pg) : "r"(s_pgs + 4u * S) : "memory");
+                const bool bad = pg >= (uint32_t)a.num_pages;
+                if (bad && issuer && issued < ntiles) atomicExch(a.err, (int)TQ_ERROR_INVALID_VALUE);
+                pg = bad ? 0u : pg;
+                // this tile's first token row inside its page: head * P + token in page
+                const uint32_t r = hrow + (tok & a.page_mask);
+                ksrc = a.k + ((uint64_t)pg * a.page_kbytes + (uint64_t)(r * (uint32_t)KB));
+                vsrc = a.v + ((uint64_t)pg * a.page_vbytes + (uint64_t)(r * (uint32_t)VB));
+                // after the slot's value is in use
+                page_fetch(tok + ATT_STAGES * RINGS * ATT_TILE, issued + ATT_STAGES, S);
+            }
+            bool go = issuer && issued < ntiles;
             if (SPLIT == 2 && go && issued >= ATT_STAGES) {
                 // the partner warp must be done with tile issued - ATT_STAGES in this stage; a
                 // release that never comes leaves the stage unfilled and the full-barrier wait
@@ -501,8 +552,10 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
             }
             bulk_issue(go, stage0 + S * STAGE, ksrc, nt * KB, stage0 + S * STAGE + KTILE, vsrc, nt * VB,
                        bar0 + 8 * S);
-            ksrc += (size_t)RINGS * ATT_TILE * KB;
-            vsrc += (size_t)RINGS * ATT_TILE * VB;
+            if constexpr (!PG) {
+                ksrc += (size_t)RINGS * ATT_TILE * KB;
+                vsrc += (size_t)RINGS * ATT_TILE * VB;
+            }
             ++issued;
         };
         // Tiles are processed in pairs: tiles 2p and 2p + 1 sit in stages 2p mod 4 and
@@ -844,6 +897,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
             }
 #pragma unroll
             for (int s2 = 0; s2 < ATT_STAGES; ++s2) mbar_wait(bar0 + 8 * s2, (phase_bits >> s2) & 1u);
+            if (PG && issuer) asm volatile("cp.async.wait_all;" ::: "memory");
         }
         if (SPLIT == 2 && !timed_out && lane == 0 && half == 0) {
             // take the releases of the last tiles of the segment, which no refill waited for, so
@@ -1018,6 +1072,7 @@ static size_t decode_smem_bytes() {
     s += (size_t)Cfg::EBARS * 8;
     s += 16;                                                        // s_abort
     if (Cfg::SPLIT == 2) s += (size_t)2 * Cfg::NCH * 32 * 8;        // s_qfl
+    s += (size_t)Cfg::RINGS * ATT_STAGES * 4;                       // page slots (paged caches)
     return s;
 }
 
@@ -1064,7 +1119,7 @@ static int reserved_smem() {
     return cached[dev];
 }
 
-template <int D, int KT, int RES, bool PK>
+template <int D, int KT, int RES, bool PK, bool PG>
 static cudaError_t launch_decode_kernel(const AttnKernelArgs& a, int grid, cudaStream_t st) {
     const size_t smem = decode_smem_bytes<D, KT>();
     // the shared-memory opt-in is set once per device, so that later calls (for example
@@ -1074,22 +1129,22 @@ static cudaError_t launch_decode_kernel(const AttnKernelArgs& a, int grid, cudaS
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(attn_decode_kernel<D, KT, RES, PK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(attn_decode_kernel<D, KT, RES, PK, PG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    attn_decode_kernel<D, KT, RES, PK><<<grid, AttnCfg<D, KT>::THREADS, smem, st>>>(a);
+    attn_decode_kernel<D, KT, RES, PK, PG><<<grid, AttnCfg<D, KT>::THREADS, smem, st>>>(a);
     return cudaGetLastError();
 }
 
-template <int D, int RES>
+template <int D, int RES, bool PG>
 static cudaError_t launch_decode_kt(const AttnKernelArgs& a, int k_type, int grid, cudaStream_t st) {
     if (a.grp <= 4)
-        return k_type == 4 ? launch_decode_kernel<D, 4, RES, true>(a, grid, st)
-                           : launch_decode_kernel<D, 3, RES, true>(a, grid, st);
-    return k_type == 4 ? launch_decode_kernel<D, 4, RES, false>(a, grid, st)
-                       : launch_decode_kernel<D, 3, RES, false>(a, grid, st);
+        return k_type == 4 ? launch_decode_kernel<D, 4, RES, true, PG>(a, grid, st)
+                           : launch_decode_kernel<D, 3, RES, true, PG>(a, grid, st);
+    return k_type == 4 ? launch_decode_kernel<D, 4, RES, false, PG>(a, grid, st)
+                       : launch_decode_kernel<D, 3, RES, false, PG>(a, grid, st);
 }
 
 template <int D>
@@ -1124,10 +1179,22 @@ static cudaError_t run_decode(const AttnRun& r, const AttnPlan& p, uint8_t* ws, 
     a.rotate_q = r.rotate_q;
     a.v_rotated = r.v_rotated;
     a.peer = r.peer;
-    const int res = reserved_smem();
-    if (res == 0) return launch_decode_kt<D, 0>(a, r.k_type, p.grid, st);
-    if (res == 1024) return launch_decode_kt<D, 1024>(a, r.k_type, p.grid, st);
-    return cudaErrorNotSupported;
+    a.pages = r.pages;
+    a.max_pages = r.max_pages;
+    a.num_pages = r.num_pages;
+    a.page_shift = r.page_shift;
+    a.page_mask = (1u << r.page_shift) - 1u;
+    {
+        const uint32_t rows = (uint32_t)r.Hkv << r.page_shift;
+        const uint32_t kbb = r.k_type == 4 ? TQ4_BYTES : TQ3_BYTES;
+        a.page_kbytes = rows * (uint32_t)(D / 32) * kbb;
+        a.page_vbytes = rows * (uint32_t)(D / 32) * TQ4_BYTES;
+    }
+    // the codebook table sits at the start of the shared window, an instruction immediate: B200
+    // reserves 1 KB of every CTA's shared memory below it
+    if (reserved_smem() != 1024) return cudaErrorNotSupported;
+    return r.pages ? launch_decode_kt<D, 1024, true>(a, r.k_type, p.grid, st)
+                   : launch_decode_kt<D, 1024, false>(a, r.k_type, p.grid, st);
 }
 
 cudaError_t launch_decode_attention(const AttnRun& r, const AttnPlan& p, void* workspace, cudaStream_t st) {

@@ -42,6 +42,12 @@ struct AttnRun {
     int out_dtype = 0;
     float* lse = nullptr;
     PeerOut peer;
+    // paged caches (pages != null): k / v are page pools [num_pages][Hkv][1 << page_shift][blocks],
+    // pages[b * max_pages + i] the pool page of tokens [i << page_shift, (i + 1) << page_shift) of
+    // sequence b; cap = max_pages << page_shift
+    const int32_t* pages = nullptr;
+    int64_t max_pages = 0, num_pages = 0;
+    int page_shift = 0;
 };
 
 AttnPlan attn_plan(int B, int Hkv, int D, int64_t cap, int64_t max_len);

@@ -219,11 +219,48 @@ extern "C" tq_status tq_quantize_cuda(tq_type type, const void* x, tq_dtype x_dt
                        "quantize kernel launch");
 }
 
+tq_status tq::pages_check(const tq_kv_pages* pg, int batch, int* shift) {
+    if (!pg) return set_error(TQ_ERROR_INVALID_VALUE, "null page description");
+    const int l2 = log2_pow2(pg->page_size);
+    if (l2 < 4 || l2 > 16) return set_error(TQ_ERROR_INVALID_VALUE, "page_size=%d (a power of two, 16 .. 65536)", pg->page_size);
+    if (pg->max_pages_per_seq <= 0 || pg->max_pages_per_seq > (int64_t(1) << 40))
+        return set_error(TQ_ERROR_INVALID_VALUE, "max_pages_per_seq=%lld", (long long)pg->max_pages_per_seq);
+    if (pg->num_pages <= 0 || pg->num_pages > INT32_MAX)
+        return set_error(TQ_ERROR_INVALID_VALUE, "num_pages=%lld (1 .. 2^31 - 1)", (long long)pg->num_pages);
+    if (batch > 0 && !pg->page_table) return set_error(TQ_ERROR_INVALID_VALUE, "null page table");
+    if (((uintptr_t)pg->page_table) & 3) return set_error(TQ_ERROR_MISALIGNED, "page table not 4-byte aligned");
+    *shift = l2;
+    return TQ_SUCCESS;
+}
+
+static tq_status kv_append(tq_type type, const void* src, tq_dtype src_dtype, void* cache, int batch, int n_kv_heads,
+                           int head_dim, int64_t capacity, const tq_kv_pages* pages, int page_shift, int64_t n_new,
+                           const int32_t* pos, int rotate, int opt_passes, int32_t* overflow, void* stream);
+
 extern "C" tq_status tq_kv_append_cuda(tq_type type, const void* src, tq_dtype src_dtype, void* cache, int batch,
                                        int n_kv_heads, int head_dim, int64_t capacity, int64_t n_new,
                                        const int32_t* pos, int rotate, int opt_passes, int32_t* overflow,
                                        void* stream) {
     g_err[0] = 0;
+    return kv_append(type, src, src_dtype, cache, batch, n_kv_heads, head_dim, capacity, nullptr, 0, n_new, pos, rotate,
+                     opt_passes, overflow, stream);
+}
+
+extern "C" tq_status tq_kv_append_paged_cuda(tq_type type, const void* src, tq_dtype src_dtype, void* pool, int batch,
+                                             int n_kv_heads, int head_dim, const tq_kv_pages* pages, int64_t n_new,
+                                             const int32_t* pos, int rotate, int opt_passes, int32_t* overflow,
+                                             void* stream) {
+    g_err[0] = 0;
+    int shift = 0;
+    const tq_status s = pages_check(pages, batch, &shift);
+    if (s) return s;
+    return kv_append(type, src, src_dtype, pool, batch, n_kv_heads, head_dim, pages->max_pages_per_seq << shift, pages,
+                     shift, n_new, pos, rotate, opt_passes, overflow, stream);
+}
+
+static tq_status kv_append(tq_type type, const void* src, tq_dtype src_dtype, void* cache, int batch, int n_kv_heads,
+                           int head_dim, int64_t capacity, const tq_kv_pages* pages, int page_shift, int64_t n_new,
+                           const int32_t* pos, int rotate, int opt_passes, int32_t* overflow, void* stream) {
     if (!type_ok(type)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown block type %d", (int)type);
     if (!dtype_ok(src_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown input dtype %d", (int)src_dtype);
     if (batch < 0 || n_kv_heads <= 0 || capacity < 0 || n_new < 0)
@@ -244,6 +281,12 @@ extern "C" tq_status tq_kv_append_cuda(tq_type type, const void* src, tq_dtype s
     map.nblk = head_dim / QK;
     map.pos = pos;
     map.overflow = overflow;
+    if (pages) {
+        map.pages = pages->page_table;
+        map.max_pages = pages->max_pages_per_seq;
+        map.num_pages = pages->num_pages;
+        map.page_shift = page_shift;
+    }
     return cuda_status(launch_quantize((int)type, (int)src_dtype, src, cache, rows * (head_dim / QK),
                                        rotate ? l2 : -1, rotate ? fwht_norm(head_dim) : 1.0f, opt_passes,
                                        (cudaStream_t)stream, map),

@@ -61,6 +61,33 @@ extern "C" tq_status tq_decode_attention_cuda(const tq_decode_attention_args* a,
     return cuda_status(launch_decode_attention(r, p, a->workspace, (cudaStream_t)stream), "decode attention launch");
 }
 
+extern "C" tq_status tq_decode_attention_paged_cuda(const tq_decode_attention_args* a, const tq_kv_pages* pg,
+                                                    void* stream) {
+    AttnRun r;
+    AttnPlan p;
+    tq_status s = attn_check(a, &r, &p);
+    if (s) return s;
+    int shift = 0;
+    if ((s = pages_check(pg, a->batch, &shift))) return s;
+    if (a->kv_capacity != (pg->max_pages_per_seq << shift))
+        return set_error(TQ_ERROR_INVALID_VALUE, "kv_capacity must equal max_pages_per_seq * page_size");
+    // the kernel addresses tokens and page-table entries in 32 bits
+    const int64_t page_bytes = ((int64_t)a->n_kv_heads << shift) * (a->head_dim / 32) * 18;   // the larger pool
+    if (a->kv_capacity >= (int64_t(1) << 31) || (int64_t)a->batch * pg->max_pages_per_seq >= (int64_t(1) << 32) ||
+        page_bytes >= (int64_t(1) << 32))
+        return set_error(TQ_ERROR_UNSUPPORTED, "paged cache too large: capacity, page table and page bytes must fit 32 bits");
+    if (r.B == 0) return TQ_SUCCESS;
+    r.pages = pg->page_table;
+    r.max_pages = pg->max_pages_per_seq;
+    r.num_pages = pg->num_pages;
+    r.page_shift = shift;
+    const size_t need = attn_workspace_bytes(r.B, r.Hkv, r.D, p);
+    if (!a->workspace || a->workspace_bytes < need)
+        return set_error(TQ_ERROR_INVALID_VALUE, "workspace of %zu bytes needed", need);
+    if (((uintptr_t)a->workspace) & 255) return set_error(TQ_ERROR_MISALIGNED, "workspace must be 256-byte aligned");
+    return cuda_status(launch_decode_attention(r, p, a->workspace, (cudaStream_t)stream), "paged decode attention launch");
+}
+
 extern "C" tq_status tq_lse_merge_cuda(int n_parts, int64_t n_rows, int head_dim, const float* o,
                                        int64_t o_part_stride, const float* lse, int64_t lse_part_stride, void* out,
                                        tq_dtype out_dtype, float* lse_out, void* stream) {

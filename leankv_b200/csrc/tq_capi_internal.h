@@ -21,5 +21,7 @@ bool dtype_ok(int dt);
 bool type_ok(int t);
 // checks a decode-attention argument block and fills the kernel's run description and work plan
 tq_status attn_check(const tq_decode_attention_args* a, AttnRun* r, AttnPlan* p);
+// checks a paged-cache description for `batch` sequences; *shift = log2(page_size)
+tq_status pages_check(const tq_kv_pages* pg, int batch, int* shift);
 
 }  // namespace tq

@@ -296,13 +296,24 @@ __device__ __forceinline__ void map_rows(int64_t* __restrict__ s_dst, int64_t b0
         }
         const int64_t slot = (map.pos ? (int64_t)map.pos[seq] : 0) + t;
         int64_t off = -1;
-        if (slot >= 0 && slot < map.cap) off = (sh * map.cap + slot) * row_bytes;
-        else if (map.overflow) atomicAdd(map.overflow, 1);
+        int64_t run_end = map.cap;   // the slots [slot, run_end) are consecutive in memory
+        if (slot >= 0 && slot < map.cap) {
+            if (map.pages) {
+                const int32_t pg = map.pages[seq * map.max_pages + (slot >> map.page_shift)];
+                const int64_t in_page = slot & ((int64_t(1) << map.page_shift) - 1);
+                if ((uint64_t)(int64_t)pg < (uint64_t)map.num_pages)
+                    off = ((((int64_t)pg * map.hkv + (sh - seq * map.hkv)) << map.page_shift) + in_page) * row_bytes;
+                run_end = slot - in_page + (int64_t(1) << map.page_shift);
+            } else {
+                off = (sh * map.cap + slot) * row_bytes;
+            }
+        }
+        if (off < 0 && map.overflow) atomicAdd(map.overflow, 1);
         s_dst[threadIdx.x] = off;
         if (threadIdx.x == 0) {
             // the whole tile lands in consecutive slots of one (sequence, head) when its last
-            // row belongs to the same (sequence, head) and still fits
-            s_dst[CODEC_THREADS] = (off >= 0 && sh1 == sh && slot + (nr - 1) < map.cap) ? 1 : 0;
+            // row belongs to the same (sequence, head) and still fits (in the same page)
+            s_dst[CODEC_THREADS] = (off >= 0 && sh1 == sh && slot + (nr - 1) < run_end) ? 1 : 0;
         }
     }
 }

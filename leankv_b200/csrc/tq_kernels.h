@@ -19,6 +19,11 @@ struct RowMap {
     int nblk = 1;
     const int32_t* pos = nullptr;
     int* overflow = nullptr;
+    // paged cache (pages != null): slot s of (sequence q, head h) is token s & (2^page_shift - 1)
+    // of pool page pages[q * max_pages + (s >> page_shift)], pool [num_pages][hkv][2^page_shift][nblk]
+    const int32_t* pages = nullptr;
+    int64_t max_pages = 0, num_pages = 0;
+    int page_shift = 0;
 };
 
 // [FWHT over heads of 2^log2_hd elements when log2_hd >= 0] + quantize nblocks blocks.

@@ -143,6 +143,48 @@ def kv_append(src: torch.Tensor, cache: torch.Tensor, pos: torch.Tensor | None =
     return cache
 
 
+def kv_append_paged(src: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor, pos: torch.Tensor | None = None,
+                    qtype=None, rotate: bool = True, opt_passes: int = 0,
+                    overflow: torch.Tensor | None = None) -> torch.Tensor:
+    """kv_append into a paged cache (tq_kv_append_paged_cuda).
+
+    pool uint8 [num_pages, n_kv_heads, page_size, head_dim/32, block_bytes];
+    page_table int32 CUDA [batch, max_pages_per_seq]: token slot s of sequence b
+    lives in pool page page_table[b, s // page_size] at row s % page_size.  Rows
+    whose slot is past max_pages_per_seq * page_size, or whose page id is outside
+    the pool, are skipped and counted into overflow.  Returns pool.
+    """
+    from .attention import make_pages
+    _need_cuda(src, pool, page_table)
+    if src.dim() != 4 or not src.is_contiguous() or src.dtype not in _DTYPES:
+        raise ValueError("src must be a contiguous f32/f16/bf16 [batch, n_kv_heads, n_new, head_dim] tensor")
+    if pool.dim() != 5 or pool.dtype != torch.uint8 or not pool.is_contiguous():
+        raise ValueError("pool must be a contiguous uint8 [num_pages, n_kv_heads, page_size, head_dim/32, bytes] tensor")
+    B, H, n_new, D = src.shape
+    if qtype is None:
+        qtype = TQ4_0 if pool.shape[-1] == BLOCK_BYTES[TQ4_0] else TQ3_0
+    q = _qtype(qtype)
+    if pool.shape[1] != H or pool.shape[3] * QK != D or pool.shape[4] != BLOCK_BYTES[q]:
+        raise ValueError(f"pool shape {tuple(pool.shape)} does not match src {tuple(src.shape)} / type {q}")
+    if page_table.dtype != torch.int32 or page_table.dim() != 2 or page_table.shape[0] != B \
+            or not page_table.is_contiguous():
+        raise ValueError("page_table must be a contiguous int32 [batch, max_pages_per_seq] tensor")
+    if pos is not None:
+        _need_cuda(pos)
+        if pos.dtype != torch.int32 or pos.numel() != B or not pos.is_contiguous():
+            raise ValueError("pos must be a contiguous int32 [batch] tensor")
+    if overflow is not None:
+        _need_cuda(overflow)
+        if overflow.dtype != torch.int32:
+            raise ValueError("overflow must be an int32 tensor")
+    pg = make_pages(page_table, pool.shape[0], pool.shape[2])
+    L.check(L.load().tq_kv_append_paged_cuda(q, src.data_ptr(), _DTYPES[src.dtype], pool.data_ptr(), B, H, D,
+                                             C.byref(pg), n_new, pos.data_ptr() if pos is not None else None,
+                                             int(rotate), int(opt_passes),
+                                             overflow.data_ptr() if overflow is not None else None, _stream(src)))
+    return pool
+
+
 def requantize(blocks: torch.Tensor, src_qtype, dst_qtype) -> torch.Tensor:
     """Blocks of src_qtype -> blocks of dst_qtype (dequantize + quantize per block, one kernel;
     requantize_tq4_to_tq3 / tq3_to_tq2 / tq4_to_tq2 of src/ggml-tq.c:329-357)."""

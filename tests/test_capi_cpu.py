@@ -149,6 +149,59 @@ def ctypes_sizeof_matches_c(tmp=None):
             and off_sc == A.AttnArgs.sm_scale.offset)
 
 
+def test_paged_argument_errors():
+    """The paged attention and append entry points check the page description before any
+    device work (runs without a GPU)."""
+    from leankv_b200 import attention as A
+    lib = A._bind()
+    a = A.AttnArgs()
+    a.batch, a.n_q_heads, a.n_kv_heads, a.head_dim = 2, 16, 2, 128
+    a.k_type = a.v_type = 4
+    a.q = a.out = 16
+    a.k_cache = a.v_cache = 32
+    table = (C.c_int32 * 8)()
+    pg = A.KVPages()
+    pg.page_table = C.addressof(table)
+    pg.max_pages_per_seq, pg.num_pages, pg.page_size = 4, 8, 16
+    a.kv_capacity = 64
+    assert lib.tq_decode_attention_paged_cuda(C.byref(a), None, None) == 1            # no page description
+    assert lib.tq_decode_attention_paged_cuda(C.byref(a), C.byref(pg), None) == 1     # no workspace
+    for field, bad in (("page_size", 24), ("page_size", 8), ("num_pages", 0), ("max_pages_per_seq", 0)):
+        saved = getattr(pg, field)
+        setattr(pg, field, bad)
+        assert lib.tq_decode_attention_paged_cuda(C.byref(a), C.byref(pg), None) == 1, field
+        setattr(pg, field, saved)
+    a.kv_capacity = 62                                                                 # != 4 pages x 16
+    assert lib.tq_decode_attention_paged_cuda(C.byref(a), C.byref(pg), None) == 1
+    a.kv_capacity = 64
+    pg.page_table = None
+    assert lib.tq_decode_attention_paged_cuda(C.byref(a), C.byref(pg), None) == 1      # null table
+    a.batch = 0
+    assert lib.tq_decode_attention_paged_cuda(C.byref(a), C.byref(pg), None) == 0      # nothing to do
+    lib2 = L.load()
+    pg.page_table = C.addressof(table)
+    assert lib2.tq_kv_append_paged_cuda(4, None, 0, None, 0, 2, 128, None, 1, None, 1, 0, None, None) == 1
+    assert lib2.tq_kv_append_paged_cuda(4, None, 0, None, 0, 2, 128, C.byref(pg), 1, None, 1, 0, None, None) == 0
+    pg.page_size = 48
+    assert lib2.tq_kv_append_paged_cuda(4, None, 0, None, 0, 2, 128, C.byref(pg), 1, None, 1, 0, None, None) == 1
+    assert pages_sizeof_matches_c()
+
+
+def pages_sizeof_matches_c():
+    """sizeof / offsets of tq_kv_pages in C equal the ctypes mirror."""
+    import tempfile
+    from leankv_b200 import attention as A
+    with tempfile.TemporaryDirectory() as td:
+        src = os.path.join(td, "p.c")
+        open(src, "w").write('#include "leankv_tq.h"\n#include <stdio.h>\n#include <stddef.h>\n'
+                             'int main(void){printf("%zu %zu %zu\\n", sizeof(tq_kv_pages),'
+                             ' offsetof(tq_kv_pages, num_pages), offsetof(tq_kv_pages, page_size)); return 0;}\n')
+        exe = os.path.join(td, "p")
+        subprocess.run(["gcc", "-I", L.HEADER_DIR, src, "-o", exe], check=True)
+        sz, off_n, off_p = map(int, subprocess.run([exe], capture_output=True, text=True).stdout.split())
+    return sz == C.sizeof(A.KVPages) and off_n == A.KVPages.num_pages.offset and off_p == A.KVPages.page_size.offset
+
+
 @pytest.mark.parametrize("args", [(0, 0, 8, 128), (65, 0, 8, 128), (2, 2, 8, 128), (2, -1, 8, 128),
                                   (2, 0, 0, 128), (2, 0, 8, 0)])
 def test_peer_exchange_argument_errors(args):

@@ -218,7 +218,7 @@ struct AttnKernelArgs {
     int64_t cap;                // token capacity per (sequence, KV head)
     int64_t lnom;               // nominal tokens per pair (multiple of 16, >= every kv_len used)
     int64_t chunk;              // tokens per CTA (multiple of 256)
-    float qscale;               // sm_scale * log2(e) [* 1/sqrt(D) of the query FWHT]
+    float qscale;               // sm_scale * log2(e) [* 1/sqrt(D) of the query FWHT] / alpha of the K codebook
     float onorm;                // 1/sqrt(D) of the output FWHT
     int B, Hq, Hkv, grp, slots;
     int q_dtype, out_dtype, rotate_q, v_rotated;
@@ -618,22 +618,23 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         uint32_t bad_scale = 0;   // max |d| bits over the block scales seen
 
         // block-scale extraction of one tile into scratch xs: K -> f32 [row][blk], V -> f16 bits
-        // [blk][row]; tokens past `valid` (stale or never-written stage bytes) get scale 0
-        auto extract = [&](uint32_t st, uint32_t xs, int valid) {
+        // [blk][row]; tokens past `valid` (stale or never-written stage bytes) get scale 0, which
+        // only the last tile of a segment needs (FULL: all 16 tokens valid)
+        auto extract = [&](uint32_t st, uint32_t xs, int valid, auto full_c) {
+            constexpr bool FULL = decltype(full_c)::value;
             static_for<0, 2 * NXH>([&](auto r_c) {
                 constexpr int r = decltype(r_c)::value;
                 constexpr bool IS_V = r >= NXH;
                 constexpr int rr = IS_V ? r - NXH : r;
-                const bool xv = xt0 + rr * TSTEP < valid;
                 const uint32_t src = IS_V ? xvs + rr * TSTEP * VB : xks + rr * TSTEP * KB;
                 uint16_t h;
                 asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(st + src));
-                h = xv ? h : (uint16_t)0;
+                if constexpr (!FULL) h = xt0 + rr * TSTEP < valid ? h : (uint16_t)0;
                 // |d| >= 2^15 (|bits| >= 0x7800): exponent 31 decodes as a finite value in the reference but
                 // as inf/nan in IEEE fp16, and P * d could overflow fp16: reported once per segment
                 bad_scale = max(bad_scale, (uint32_t)(h & 0x7FFFu));
-                if (!IS_V) {
-                    const float f = __half2float(__ushort_as_half(h)) * (1.0f / (KT == 4 ? TQ4_ALPHA : TQ3_ALPHA));
+                if (!IS_V) {   // (the K codebook's 1/alpha is folded into the query scale)
+                    const float f = __half2float(__ushort_as_half(h));
                     asm volatile("st.shared.f32 [%0], %1;" ::"r"(xs + xkd + rr * ROWSTEP * NBLK * 4), "f"(f));
                 } else {
                     constexpr int VDELTA = (((rr * ROWSTEP) & 7) >> 1) * NBLK * 8 + ((rr * ROWSTEP) >> 3) * 4;
@@ -748,14 +749,13 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 constexpr int blk = decltype(blk_c)::value;
                 const uint32_t w0 = ld16<blk * TQ4_BYTES>(vr), w1 = ld16<blk * TQ4_BYTES + VO1>(vr);
                 const uint32_t w2 = ld16<blk * TQ4_BYTES + VO8>(vr), w3 = ld16<blk * TQ4_BYTES + VO9>(vr);
-                // bytes [A0 B0 A1 B1] of the two tokens of a k pair; the codebook index of an element
-                // pair is (A nibble | B nibble << 4), built with one bit-select per word
-                const uint32_t ra = prmt(w0, w1, 0x5140u), rb = prmt(w2, w3, 0x5140u);
-                const uint32_t ra4 = ra >> 4, rb4 = rb >> 4, ra8 = ra >> 8, rb8 = rb >> 8;
-                const uint32_t xa = (ra & 0x0F0F0F0Fu) | (ra4 & 0xF0F0F0F0u);
-                const uint32_t ya = (ra4 & 0x0F0F0F0Fu) | (ra8 & 0xF0F0F0F0u);
-                const uint32_t xb = (rb & 0x0F0F0F0Fu) | (rb4 & 0xF0F0F0F0u);
-                const uint32_t yb = (rb4 & 0x0F0F0F0Fu) | (rb8 & 0xF0F0F0F0u);
+                // tokens A, B (k 2t, 2t+1) and C, D (k 2t+8, 2t+9), code bytes 0 and 1 each: the words
+                // [A0 A1 C0 C1] and [B0 B1 D0 D1]; the codebook index of an element pair is (first
+                // token's nibble | second token's nibble << 4), one bit-select per word gives four:
+                // nlo = low nibbles (elements j, j+1 of the bytes), nhi = high nibbles (j+16, j+17)
+                const uint32_t wac = prmt(w0, w2, 0x5410u), wbd = prmt(w1, w3, 0x5410u);
+                const uint32_t nlo = (wac & 0x0F0F0F0Fu) | ((wbd << 4) & 0xF0F0F0F0u);
+                const uint32_t nhi = ((wac >> 4) & 0x0F0F0F0Fu) | (wbd & 0xF0F0F0F0u);
                 // TQ4 K: one 128-bit load per block pair; TQ3 K (more live offsets) one 64-bit load per block
                 if constexpr (KT == 3) {
                     const uint2 d2 = ld64u<blk * 8>(sdv);
@@ -768,15 +768,15 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 const uint32_t b0 = h2_mul(pb01, hi ? dvw.z : dvw.x);
                 const uint32_t b1 = h2_mul(pb23, hi ? dvw.w : dvw.y);
                 uint32_t af[4];
-                af[0] = lut_ld<RES>(xa, lane4, LUT_SEL0);
-                af[1] = lut_ld<RES>(ya, lane4, LUT_SEL0);
-                af[2] = lut_ld<RES>(xb, lane4, LUT_SEL0);
-                af[3] = lut_ld<RES>(yb, lane4, LUT_SEL0);
+                af[0] = lut_ld<RES>(nlo, lane4, LUT_SEL0);   // element 2g of tokens A, B
+                af[1] = lut_ld<RES>(nhi, lane4, LUT_SEL0);   // element 2g + 16
+                af[2] = lut_ld<RES>(nlo, lane4, LUT_SEL2);   // element 2g of tokens C, D
+                af[3] = lut_ld<RES>(nhi, lane4, LUT_SEL2);
                 mma16816(o[2 * blk], af, b0, b1);
-                af[0] = lut_ld<RES>(xa, lane4, LUT_SEL2);
-                af[1] = lut_ld<RES>(ya, lane4, LUT_SEL2);
-                af[2] = lut_ld<RES>(xb, lane4, LUT_SEL2);
-                af[3] = lut_ld<RES>(yb, lane4, LUT_SEL2);
+                af[0] = lut_ld<RES>(nlo, lane4, LUT_SEL1);   // element 2g + 1
+                af[1] = lut_ld<RES>(nhi, lane4, LUT_SEL1);   // element 2g + 17
+                af[2] = lut_ld<RES>(nlo, lane4, LUT_SEL3);
+                af[3] = lut_ld<RES>(nhi, lane4, LUT_SEL3);
                 mma16816(o[2 * blk + 1], af, b0, b1);
             });
         };
@@ -806,8 +806,13 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 const int valid_a = ia == ntiles - 1 ? last_valid : ATT_TILE;
                 const int valid_b = !has_b ? 0 : (ia + 1 == ntiles - 1 ? last_valid : ATT_TILE);
                 const uint32_t sta = stage0 + SA * STAGE, stb = stage0 + SB * STAGE;
-                extract(sta, scr, valid_a);
-                extract(stb, scr + SCR, valid_b);
+                if (valid_a == ATT_TILE && valid_b == ATT_TILE) {
+                    extract(sta, scr, valid_a, std::true_type{});
+                    extract(stb, scr + SCR, valid_b, std::true_type{});
+                } else {
+                    extract(sta, scr, valid_a, std::false_type{});
+                    extract(stb, scr + SCR, valid_b, std::false_type{});
+                }
                 __syncwarp();
                 float sa[4], sb[4];
                 scores(sta, scr, valid_a, sa);
@@ -1167,7 +1172,9 @@ static cudaError_t run_decode(const AttnRun& r, const AttnPlan& p, uint8_t* ws, 
     a.lnom = p.lnom;
     a.chunk = p.chunk;
     // q~ = FWHT(q) / sqrt(D) * sm_scale * log2(e): the FWHT normalisation folds into the scale
-    a.qscale = r.sm_scale * LOG2E * (r.rotate_q ? fwht_norm(D) : 1.0f);
+    // K codebook tables hold alpha * level (alpha chosen for the fp16 rounding of the levels): 1/alpha
+    // joins the query scale
+    a.qscale = r.sm_scale * LOG2E * (r.rotate_q ? fwht_norm(D) : 1.0f) / (r.k_type == 4 ? TQ4_ALPHA : TQ3_ALPHA);
     a.onorm = fwht_norm(D);
     a.B = r.B;
     a.Hq = r.Hq;

@@ -409,9 +409,12 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         const int k = i >> 5, l = i & 31;
         *reinterpret_cast<uint32_t*>(smem + (k << 8) + (l << 2)) =
             pack_h2(TQ4_ALPHA * tq4_level(k & 15), TQ4_ALPHA * tq4_level(k >> 4));
-        if (KT == 3 && k < 64)
+        // TQ3 pairs in the upper halves: rows 0..63 at head_dim 256 (rows 64..192 carry the pair
+        // score exchange there), every row at head_dim 128, row k holding pair k mod 64 so that a
+        // byte whose low 6 bits are a pair index addresses it directly
+        if (KT == 3 && (SPLIT == 1 || k < 64))
             *reinterpret_cast<uint32_t*>(smem + (k << 8) + 128 + (l << 2)) =
-                pack_h2(TQ3_ALPHA * tq3_level(k & 7), TQ3_ALPHA * tq3_level(k >> 3));
+                pack_h2(TQ3_ALPHA * tq3_level(k & 7), TQ3_ALPHA * tq3_level((k >> 3) & 7));
     }
     if (lane == 0 && half == 0)
         for (int s = 0; s < ATT_STAGES; ++s) {
@@ -713,16 +716,30 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     const uint32_t sh = (blk & 1) ? k3_sh_o : k3_sh_e;
                     const uint32_t wg = __funnelshift_r(ld32<IMM>(kr), ld32<IMM + 4>(kr), sh);
                     const uint32_t wh = __funnelshift_r(ld32<IMM + KROW8>(kr), ld32<IMM + KROW8 + 4>(kr), sh);
-                    af[0] = lut_ld_addr<RES>(tq3_lut_addr<0>(wg, lane4x));
-                    af[1] = lut_ld_addr<RES>(tq3_lut_addr<0>(wh, lane4x));
-                    af[2] = lut_ld_addr<RES>(tq3_lut_addr<1>(wg, lane4x));
-                    af[3] = lut_ld_addr<RES>(tq3_lut_addr<1>(wh, lane4x));
+                    // head_dim 128 (table in all 256 rows): pair i read from a byte of a shifted word,
+                    // pair 0 = byte 0 of w, 1 = byte 1 of w << 2, 2 = byte 1 of w >> 4, 3 = byte 2 of w >> 2
+                    auto t3 = [&](auto i_c, uint32_t w) -> uint32_t {
+                        constexpr int I = decltype(i_c)::value;
+                        if constexpr (SPLIT == 2) return lut_ld_addr<RES>(tq3_lut_addr<I>(w, lane4x));
+                        else if constexpr (I == 0) return lut_ld<RES>(w, lane4x, LUT_SEL0);
+                        else if constexpr (I == 1) return lut_ld<RES>(w << 2, lane4x, LUT_SEL1);
+                        else if constexpr (I == 2) return lut_ld<RES>(w >> 4, lane4x, LUT_SEL1);
+                        else return lut_ld<RES>(w >> 2, lane4x, LUT_SEL2);
+                    };
+                    using I0 = std::integral_constant<int, 0>;
+                    using I1 = std::integral_constant<int, 1>;
+                    using I2 = std::integral_constant<int, 2>;
+                    using I3 = std::integral_constant<int, 3>;
+                    af[0] = t3(I0{}, wg);
+                    af[1] = t3(I0{}, wh);
+                    af[2] = t3(I1{}, wg);
+                    af[3] = t3(I1{}, wh);
                     mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
                     lo_mma(acc, af, 2 * blk);
-                    af[0] = lut_ld_addr<RES>(tq3_lut_addr<2>(wg, lane4x));
-                    af[1] = lut_ld_addr<RES>(tq3_lut_addr<2>(wh, lane4x));
-                    af[2] = lut_ld_addr<RES>(tq3_lut_addr<3>(wg, lane4x));
-                    af[3] = lut_ld_addr<RES>(tq3_lut_addr<3>(wh, lane4x));
+                    af[0] = t3(I2{}, wg);
+                    af[1] = t3(I2{}, wh);
+                    af[2] = t3(I3{}, wg);
+                    af[3] = t3(I3{}, wh);
                     mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
                     lo_mma(acc, af, 2 * blk + 1);
                 }

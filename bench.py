@@ -716,7 +716,10 @@ def run_ours(args, ws, rank, local):
             "data": "synthetic (seeded)",
             "config": {**wl.config,
                        "parallelism": getattr(wl, "parallelism", f"token-row shards x{ws}, no collective"),
-                       "l2": getattr(wl, "l2_note", "flushed (256 MiB write) between timed steps")},
+                       "l2": getattr(wl, "l2_note", "flushed (256 MiB write) between timed steps"),
+                       # a peer transport whose setup failed on some rank: every rank ran NCCL instead
+                       **({"transport_fallback": wl.att.fallback}
+                          if getattr(getattr(wl, "att", None), "fallback", None) else {})},
             "us_per_step": round(ms_max * 1e3, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,

@@ -75,12 +75,30 @@ def local_lengths(kv_len: torch.Tensor, start: int, stop: int) -> torch.Tensor:
     return (kv_len.to(torch.int64) - start).clamp_(0, stop - start).to(torch.int32)
 
 
+class PeerSetupError(RuntimeError):
+    """The peer exchange could not be set up on every rank; raised on all ranks together."""
+
+
+def _all_ranks_ok(ok: bool, group) -> bool:
+    """Collective: True when `ok` holds on every rank of `group`."""
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return ok
+    dev = "cuda" if dist.get_backend(group) == "nccl" else "cpu"
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    return bool(flag.item())
+
+
 class PeerExchange:
     """Exchange buffers of one rank for tq_peer_exchange_merge (CUDA IPC over NVLink).
 
     Created collectively: every rank of `group` allocates its buffer, the IPC
     handles are all-gathered over the process group (host objects), and every
-    rank maps the others'.  `merge(part, out, lse_out)` then runs one step on the
+    rank maps the others'.  Setup is all or nothing: every rank takes the same
+    collective steps whatever fails locally, the ranks agree on the outcome, and
+    if any rank failed (no CUDA device, two ranks on one GPU, an allocation or a
+    mapping refused) every rank unmaps, waits for the others, frees, and raises
+    PeerSetupError.  `merge(part, out, lse_out)` then runs one step on the
     current stream; every rank must call it the same number of times, in order.
     `wait_ms` bounds each step's wait for the other ranks (0: 2000 ms).  A wait
     that runs out leaves `out` unmerged and the exchange unusable; `status()`
@@ -93,29 +111,52 @@ class PeerExchange:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.n_rows, self.head_dim = n_rows, head_dim
-        dev = torch.cuda.current_device()
+        lib = L.load()
+        self._ex = C.c_void_p()
+        err = None
+        uuid = None
+        try:
+            dev = torch.cuda.current_device()
+            uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        except Exception as e:          # no usable CUDA device on this rank
+            err = f"rank {self.rank}: no CUDA device ({e})"
         if self.world > 1:
             # the kernel of one rank waits for the kernels of the others: one GPU per rank
             ids = [None] * self.world
-            dist.all_gather_object(ids, (str(torch.cuda.get_device_properties(dev).uuid), dev), group=group)
-            if len({i[0] for i in ids}) != self.world:
-                raise ValueError("the peer exchange needs a distinct GPU for every rank")
-        lib = L.load()
-        self._ex = C.c_void_p()
-        handle = C.create_string_buffer(L.TQ_PEER_HANDLE_BYTES)
-        L.check(lib.tq_peer_exchange_create(self.world, self.rank, n_rows, head_dim, int(wait_ms), C.byref(self._ex),
-                                            handle))
-        try:
-            handles = [None] * self.world
-            if self.world > 1:
-                dist.all_gather_object(handles, handle.raw, group=group)
+            dist.all_gather_object(ids, uuid, group=group)
+            if err is None and (None in ids or len(set(ids)) != self.world):
+                err = "the peer exchange needs a distinct GPU for every rank"
+        raw = b""
+        if err is None:
+            handle = C.create_string_buffer(L.TQ_PEER_HANDLE_BYTES)
+            st = lib.tq_peer_exchange_create(self.world, self.rank, n_rows, head_dim, int(wait_ms),
+                                             C.byref(self._ex), handle)
+            if st:
+                err = f"rank {self.rank}: create: {lib.tq_last_error_string().decode(errors='replace')}"
+                self._ex = C.c_void_p()
             else:
-                handles[0] = handle.raw
-            L.check(lib.tq_peer_exchange_connect(self._ex, b"".join(handles)))
-        except BaseException:
-            lib.tq_peer_exchange_destroy(self._ex)   # unmaps what was mapped, frees this rank's buffer
-            self._ex = C.c_void_p()
-            raise
+                raw = handle.raw
+        handles = [raw]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, raw, group=group)
+        if err is None:
+            if any(len(h) != L.TQ_PEER_HANDLE_BYTES for h in handles):
+                err = "another rank could not create its exchange buffer"
+            else:
+                st = lib.tq_peer_exchange_connect(self._ex, b"".join(handles))
+                if st:
+                    err = f"rank {self.rank}: connect: {lib.tq_last_error_string().decode(errors='replace')}"
+        if not _all_ranks_ok(err is None, group):
+            # undo in the order of close(): unmap, wait until no rank maps a peer's buffer, free
+            if self._ex:
+                lib.tq_peer_exchange_disconnect(self._ex)
+            if self.world > 1:
+                dist.barrier(group=group)
+            if self._ex:
+                lib.tq_peer_exchange_destroy(self._ex)
+                self._ex = C.c_void_p()
+            raise PeerSetupError(err or "another rank could not set up the peer exchange")
 
     def merge(self, part: torch.Tensor, out: torch.Tensor, lse_out: torch.Tensor | None = None) -> torch.Tensor:
         n, D = self.n_rows, self.head_dim
@@ -204,6 +245,7 @@ class SplitSequenceAttention:
         if transport == "peer" and attend is not None:
             raise ValueError("the fused peer transport runs the CUDA attention itself; use 'peer_merge' with attend")
         self.transport = transport
+        self.fallback = None   # why a peer transport was replaced by NCCL, if it was
         self.wait_ms = wait_ms
         self._peers: dict = {}
         self.group = group
@@ -238,28 +280,41 @@ class SplitSequenceAttention:
         if out is None:
             out = torch.empty((B, Hq, D), dtype=out_dtype, device=q.device)
         if self.transport == "peer":
-            key = (n, D, str(q.device))
-            ex = self._peers.get(key)
-            if ex is None:
-                ex = self._peers[key] = PeerExchange(n, D, self.group, self.wait_ms)
-            return ex.attention(q, k_shard, v_shard, out, kv_len_local, max_kv_len, **kw)
+            ex = self._peer(n, D, q.device)
+            if ex is not None:
+                return ex.attention(q, k_shard, v_shard, out, kv_len_local, max_kv_len, **kw)
         send, recv = self._buffers(n, D, q.device)
         o_local = send[: n * D].view(B, Hq, D)
         lse_local = send[n * D:].view(B, Hq)
         self._attend(q, k_shard, v_shard, kv_len_local, max_kv_len, o_local, lse_local, **kw)
         if self.transport == "peer_merge":
-            key = (n, D, str(q.device))
-            ex = self._peers.get(key)
-            if ex is None:
-                ex = self._peers[key] = PeerExchange(n, D, self.group, self.wait_ms)
-            ex.merge(send, out.view(n, D))
-            return out
+            ex = self._peer(n, D, q.device)
+            if ex is not None:
+                ex.merge(send, out.view(n, D))
+                return out
         if self.world == 1:
             self._merge(send, 1, n, D, out.view(n, D))
             return out
+        if recv is None:   # a peer transport whose setup failed on some rank: all ranks take NCCL
+            recv = torch.empty(self.world * send.numel(), dtype=torch.float32, device=send.device)
+            self._bufs[(n, D, str(q.device))] = (send, recv)
         dist.all_gather_into_tensor(recv, send, group=self.group)
         self._merge(recv, self.world, n, D, out.view(n, D))
         return out
+
+    def _peer(self, n: int, D: int, device):
+        """The exchange for this shape, set up on first use; None after a failed setup, when
+        every rank has switched to the NCCL transport (and `fallback` holds the reason)."""
+        key = (n, D, str(device))
+        ex = self._peers.get(key)
+        if ex is None:
+            try:
+                ex = self._peers[key] = PeerExchange(n, D, self.group, self.wait_ms)
+            except PeerSetupError as e:    # raised on every rank together
+                self.fallback = f"{self.transport} setup failed ({e}); NCCL all_gather + merge instead"
+                self.transport = "nccl"
+                return None
+        return ex
 
     def status(self) -> None:
         """Peer transport: synchronize and raise if a step's wait ran out."""

@@ -55,7 +55,7 @@ def _cpu_merge(parts, n_parts, n_rows, head_dim, out):
     return out
 
 
-def _rank_main(rank, world, port, result_dir):
+def _rank_main(rank, world, port, result_dir, transport="nccl"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -63,10 +63,14 @@ def _rank_main(rank, world, port, result_dir):
         q, kc, vc = _problem()
         s0, s1 = token_shard(T, rank, world)
         lens = local_lengths(torch.tensor(LENS, dtype=torch.int32), s0, s1)
-        att = SplitSequenceAttention(attend=_cpu_attend, merge=_cpu_merge)
+        att = SplitSequenceAttention(attend=_cpu_attend, merge=_cpu_merge, transport=transport)
         assert att.world == world and att.rank == rank
         out = att(torch.from_numpy(q), torch.from_numpy(np.ascontiguousarray(kc[:, :, s0:s1])),
                   torch.from_numpy(np.ascontiguousarray(vc[:, :, s0:s1])), lens, s1 - s0)
+        if transport != "nccl":
+            # CPU ranks cannot set up the peer exchange: every rank agreed and took NCCL
+            assert att.transport == "nccl" and "setup failed" in att.fallback, att.fallback
+        att.close()
         np.save(os.path.join(result_dir, f"out{rank}.npy"), out.numpy())
     finally:
         dist.destroy_process_group()
@@ -104,3 +108,17 @@ def test_local_lengths_clamp():
     kv = torch.tensor([0, 5, 100, 1000], dtype=torch.int32)
     assert local_lengths(kv, 64, 128).tolist() == [0, 0, 36, 64]
     assert local_lengths(kv, 0, 64).tolist() == [0, 5, 64, 64]
+
+
+def test_peer_setup_failure_falls_back_on_every_rank(orc, tmp_path):
+    """A peer exchange that cannot be set up on some rank fails on all ranks together (one
+    agreement after the same collective steps), and the split attention continues over the
+    NCCL path: no rank hangs in a collective the others skipped."""
+    world = 2
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), "peer_merge"), nprocs=world,
+                       start_method="spawn")
+    q, kc, vc = _problem()
+    ref, _ = orc.decode_attention(q, kc, 3, vc, 4, HKV, kv_len=np.array(LENS))
+    for r in range(world):
+        out = np.load(tmp_path / f"out{r}.npy")
+        np.testing.assert_allclose(out, ref, rtol=1e-5, atol=1e-5 * np.abs(ref).max())

@@ -1,4 +1,5 @@
-"""LeanKVCache with storage="tq_blocks": quantize-on-write appends and the fused decode attention
+"""LeanKVCache with storage="tq_blocks" and "tq_pages": quantize-on-write appends and the fused
+decode attention
 over the packed cache, against the prototype's flow (dequantize the whole cache, then attend) on
 the same blocks, over a prefill and many single-token decode steps (the capacity grows on the way).
 
@@ -82,3 +83,27 @@ def test_blocks_cache_appends_equal_one_shot_quantize():
     assert torch.equal(kc, ops.quantize(full_k, 3, fwht_head_dim=D))
     assert torch.equal(vc, ops.quantize(full_v, 4, fwht_head_dim=D))
 
+
+
+@pytest.mark.parametrize("D,k_bits,page_size", [(128, 3, 16), (256, 4, 64)])
+def test_pages_cache_equals_blocks_cache(D, k_bits, page_size):
+    """storage="tq_pages" (fixed page pools) and storage="tq_blocks" (doubling buffers) hold the
+    same blocks and run the same split-KV plan: equal attention outputs after every update."""
+    B, Hkv, grp, layers, prefill, steps = 3, 2, 4, 2, 300, 12
+    g = torch.Generator(device=DEV).manual_seed(D * k_bits + page_size)
+    blocks = LeanKVCache(layers, D, Hkv, k_bits=k_bits, storage="tq_blocks", device="cuda")
+    pages = LeanKVCache(layers, D, Hkv, k_bits=k_bits, storage="tq_pages", device="cuda",
+                        num_pages=B * (-(-(prefill + steps) // page_size)), page_size=page_size)
+    for step in range(steps + 1):
+        n = prefill if step == 0 else 1
+        for layer in range(layers):
+            k, v = kv_rows(B, Hkv, n, D, g), kv_rows(B, Hkv, n, D, g)
+            blocks.update(k, v, layer)
+            kp, vp = pages.update(k, v, layer)
+            assert kp.shape[:3] == (pages._blocks[layer].num_pages, Hkv, page_size)
+            q = torch.randn(B, Hkv * grp, 1, D, device=DEV, generator=g).to(torch.bfloat16)
+            assert torch.equal(pages.attention(q, layer), blocks.attention(q, layer)), (step, layer)
+    assert pages.get_seq_length() == blocks.get_seq_length() == prefill + steps
+    with pytest.raises(MemoryError):   # the pools hold exactly prefill + steps tokens per sequence
+        for _ in range(page_size):
+            pages.update(kv_rows(B, Hkv, 1, D, g), kv_rows(B, Hkv, 1, D, g), 0)

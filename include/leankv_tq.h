@@ -57,6 +57,23 @@ typedef struct {
 } block_tq4_0;           /* 18 bytes */
 #endif
 
+/* TQ2_1: the static mixed-precision block of the LeanKV llama.cpp fork
+ * (docs/RESULTS.md:1451-1466, docs/CUDA-RESULTS.md:54-62): 128 elements in 44
+ * bytes, elements 0..31 as one TQ3_0 block and 32..63, 64..95, 96..127 as three
+ * TQ2_0 blocks, each with its own scale.  Byte for byte it is a block_tq3_0
+ * followed by three block_tq2_0 of the reference's encoders. */
+#define QK_TQ2_1 128
+typedef struct {
+    uint16_t d_out;      /* TQ3_0 sub-block: elements 0..31 */
+    uint8_t  qs_out[12];
+    uint16_t d_n0;       /* TQ2_0 sub-blocks: elements 32..63, 64..95, 96..127 */
+    uint8_t  qs_n0[8];
+    uint16_t d_n1;
+    uint8_t  qs_n1[8];
+    uint16_t d_n2;
+    uint8_t  qs_n2[8];
+} block_tq2_1;           /* 44 bytes */
+
 /* ── 1. drop-in entry points (src/ggml-tq.h) ─────────────────────────────── */
 
 /* replaces quantize_row_tq3_0_ref, src/ggml-tq.c:215-247 */
@@ -146,6 +163,12 @@ tq_status tq_quantize_randomized_cuda(tq_type type, const void *x, tq_dtype x_dt
 /* Requantize k elements from src_type blocks to dst_type blocks in one pass (each block is
  * dequantized to float32 and quantized again, as requantize_tq4_to_tq3 and friends do). */
 tq_status tq_requantize_cuda(tq_type src_type, const void *src, tq_type dst_type, void *dst, int64_t k, void *stream);
+/* TQ2_1 (the fork's mixed-precision type; block_tq2_1 above): k elements, a multiple of 128,
+ * of f32 / f16 / bf16 x into k / 128 blocks (no rotation: rotate the rows first when the cache
+ * holds rotated rows), and back to float32.  Codes and scales equal quantize_row_tq3_0_ref on
+ * elements 0..31 and quantize_row_tq2_0_ref on the other three 32-element runs of each block. */
+tq_status tq_quantize_tq2_1_cuda(const void *x, tq_dtype x_dtype, void *y, int64_t k, void *stream);
+tq_status tq_dequantize_tq2_1_cuda(const void *x, float *y, int64_t k, void *stream);
 
 /*
  * Quantize-on-write into a KV cache: [FWHT] + quantize n_new new head rows per

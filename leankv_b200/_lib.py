@@ -93,6 +93,9 @@ SIGNATURES = {
     "tq_outlier_identify_cuda": (_i32, [_v, _v, _i32, _i32, _f32, _i32, _i32, _v]),
     "tq_mixed_quantize_cuda": (_i32, [_v, _v, _i32, _i64, _v, _v, _v]),
     "tq_mixed_dequantize_cuda": (_i32, [_v, _v, _v, _i64, _v, _v]),
+    # TQ2_1 blocks (the fork's static mixed-precision type)
+    "tq_quantize_tq2_1_cuda": (_i32, [_v, _i32, _v, _i64, _v]),
+    "tq_dequantize_tq2_1_cuda": (_i32, [_v, _v, _i64, _v]),
     # prototype vector codec (levels / boundaries are host float arrays)
     "tq_proto_encode_cuda": (_i32, [_v, _i32, _v, _i64, _i32, _i32, _v, _i32, _i32, _v, _v, _v, _v, _v, _v, _v]),
     "tq_proto_decode_cuda": (_i32, [_v, _v, _i64, _i32, _i32, _v, _v, _i32, _v, _i32, _v, _v, _v]),

@@ -1288,6 +1288,61 @@ cudaError_t launch_mixed_dequantize(const void* obuf, const void* nbuf, int64_t 
     return cudaGetLastError();
 }
 
+// ── TQ2_1: one TQ3_0 sub-block and three TQ2_0 sub-blocks per 128 elements ───
+// One thread per 32-element sub-block s of block b: sub-block 0 is encoded as TQ3_0 at byte 0
+// of the block, sub-blocks 1..3 as TQ2_0 at bytes 14, 24, 34 (all even: the encoder's
+// 2-byte alignment holds).  The two tiers' nearest-level tables sit in shared memory.
+__device__ __forceinline__ int tq21_off(int s) { return s == 0 ? 0 : TQ3_BYTES + (s - 1) * TQ2_BYTES; }
+
+template <typename IN>
+__global__ void __launch_bounds__(MIX_THREADS)
+tq21_quantize_kernel(const IN* __restrict__ x, int64_t nblocks, uint8_t* __restrict__ y) {
+    __shared__ __align__(16) uint2 s_near[2][NEAR_ROWS * NEAR_REP];
+    near_table_init<3>(s_near[0]);
+    near_table_init<2>(s_near[1]);
+    __syncthreads();
+    const uint32_t lane_off = 8u * (threadIdx.x & (NEAR_REP - 1));
+    const int64_t total = nblocks * 4;
+    for (int64_t gs = (int64_t)blockIdx.x * MIX_THREADS + threadIdx.x; gs < total; gs += (int64_t)gridDim.x * MIX_THREADS) {
+        const int64_t b = gs >> 2;
+        const int s = (int)(gs & 3);
+        float vals[QK];
+#pragma unroll
+        for (int i = 0; i < QK; ++i) vals[i] = ld_f<IN>(x + gs * QK + i);
+        const uint32_t tb = (uint32_t)__cvta_generic_to_shared(s_near[s == 0 ? 0 : 1]) + lane_off;
+        encode_block_rt(s == 0 ? 3 : 2, vals, tb, y + b * TQ21_BYTES + tq21_off(s));
+    }
+}
+
+__global__ void __launch_bounds__(MIX_THREADS)
+tq21_dequantize_kernel(const uint8_t* __restrict__ x, int64_t nblocks, float* __restrict__ y) {
+    const int64_t total = nblocks * 4;
+    for (int64_t gs = (int64_t)blockIdx.x * MIX_THREADS + threadIdx.x; gs < total; gs += (int64_t)gridDim.x * MIX_THREADS) {
+        const int s = (int)(gs & 3);
+        float vals[QK];
+        decode_block_rt(s == 0 ? 3 : 2, x + (gs >> 2) * TQ21_BYTES + tq21_off(s), vals);
+#pragma unroll
+        for (int i = 0; i < QK; i += 4)
+            *reinterpret_cast<float4*>(y + gs * QK + i) = make_float4(vals[i], vals[i + 1], vals[i + 2], vals[i + 3]);
+    }
+}
+
+cudaError_t launch_tq21_quantize(int in_dtype, const void* x, int64_t nblocks, void* y, cudaStream_t st) {
+    const int grid = mix_grid(nblocks * 4, MIX_THREADS);
+    switch (in_dtype) {
+        case DT_F32: tq21_quantize_kernel<float><<<grid, MIX_THREADS, 0, st>>>((const float*)x, nblocks, (uint8_t*)y); break;
+        case DT_F16: tq21_quantize_kernel<__half><<<grid, MIX_THREADS, 0, st>>>((const __half*)x, nblocks, (uint8_t*)y); break;
+        default: tq21_quantize_kernel<__nv_bfloat16><<<grid, MIX_THREADS, 0, st>>>((const __nv_bfloat16*)x, nblocks, (uint8_t*)y); break;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tq21_dequantize(const void* x, int64_t nblocks, float* y, cudaStream_t st) {
+    const int grid = mix_grid(nblocks * 4, MIX_THREADS);
+    tq21_dequantize_kernel<<<grid, MIX_THREADS, 0, st>>>((const uint8_t*)x, nblocks, y);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_gather(const float* x, const MixedPlan& plan, int64_t n_vec, float* y, cudaStream_t st) {
     gather_kernel<<<mix_grid(n_vec * plan.head_dim, 256), 256, 0, st>>>(x, plan, n_vec, y);
     return cudaGetLastError();

@@ -106,6 +106,29 @@ extern "C" tq_status tq_mixed_dequantize_cuda(const tq_outlier_config* config, c
                        "mixed dequantize launch");
 }
 
+// ── TQ2_1 (the fork's static mixed-precision block) ─────────────────────────
+
+extern "C" tq_status tq_quantize_tq2_1_cuda(const void* x, tq_dtype x_dtype, void* y, int64_t k, void* stream) {
+    clear_error();
+    if (!dtype_ok(x_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "unknown input dtype %d", (int)x_dtype);
+    if (k < 0 || k % 128) return set_error(TQ_ERROR_INVALID_VALUE, "k=%lld is not a multiple of 128", (long long)k);
+    if (k == 0) return TQ_SUCCESS;
+    if (!x || !y) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    if (((uintptr_t)x) % dtype_bytes(x_dtype)) return set_error(TQ_ERROR_MISALIGNED, "x not aligned to its element size");
+    if (((uintptr_t)y) & 1) return set_error(TQ_ERROR_MISALIGNED, "blocks must be 2-byte aligned (fp16 scales)");
+    return cuda_status(launch_tq21_quantize((int)x_dtype, x, k / 128, y, (cudaStream_t)stream), "TQ2_1 quantize launch");
+}
+
+extern "C" tq_status tq_dequantize_tq2_1_cuda(const void* x, float* y, int64_t k, void* stream) {
+    clear_error();
+    if (k < 0 || k % 128) return set_error(TQ_ERROR_INVALID_VALUE, "k=%lld is not a multiple of 128", (long long)k);
+    if (k == 0) return TQ_SUCCESS;
+    if (!x || !y) return set_error(TQ_ERROR_INVALID_VALUE, "null pointer");
+    if ((((uintptr_t)x) & 1) || (((uintptr_t)y) & 15))
+        return set_error(TQ_ERROR_MISALIGNED, "blocks must be 2-byte and y 16-byte aligned");
+    return cuda_status(launch_tq21_dequantize(x, k / 128, y, (cudaStream_t)stream), "TQ2_1 dequantize launch");
+}
+
 // ── drop-in names (src/ggml-tq-outlier.h), host pointers, one head vector per call ─
 
 [[noreturn]] static void die(const char* fn, const char* why) {

@@ -23,6 +23,10 @@ cudaError_t launch_mixed_quantize(int in_dtype, const void* x, int64_t n_vec, co
                                   void* nbuf, cudaStream_t st);
 cudaError_t launch_mixed_dequantize(const void* obuf, const void* nbuf, int64_t n_vec, const MixedPlan& plan, float* y,
                                     cudaStream_t st);
+// TQ2_1 blocks (44 bytes per 128 elements: a TQ3_0 block, then three TQ2_0 blocks)
+constexpr int TQ21_BYTES = 44;
+cudaError_t launch_tq21_quantize(int in_dtype, const void* x, int64_t nblocks, void* y, cudaStream_t st);
+cudaError_t launch_tq21_dequantize(const void* x, int64_t nblocks, float* y, cudaStream_t st);
 // y[v][i] = x[v][plan.perm[i]] (plan.perm may hold an inverse permutation)
 cudaError_t launch_gather(const float* x, const MixedPlan& plan, int64_t n_vec, float* y, cudaStream_t st);
 

@@ -185,6 +185,32 @@ def kv_append_paged(src: torch.Tensor, pool: torch.Tensor, page_table: torch.Ten
     return pool
 
 
+TQ2_1_BYTES = 44   # block_tq2_1: a TQ3_0 block and three TQ2_0 blocks per 128 elements
+
+
+def quantize_tq2_1(x: torch.Tensor) -> torch.Tensor:
+    """TQ2_1 blocks (the fork's static mixed-precision type, tq_quantize_tq2_1_cuda) of a contiguous
+    f32/f16/bf16 tensor whose last dim is a multiple of 128: uint8 (..., last / 128, 44).  No
+    rotation is applied (rotate first with hadamard_ when the rows should be rotated)."""
+    _need_cuda(x)
+    if x.dtype not in _DTYPES or not x.is_contiguous() or x.dim() == 0 or x.shape[-1] % 128:
+        raise ValueError("x must be a contiguous f32/f16/bf16 tensor whose last dim is a multiple of 128")
+    out = torch.empty((*x.shape[:-1], x.shape[-1] // 128, TQ2_1_BYTES), dtype=torch.uint8, device=x.device)
+    L.check(L.load().tq_quantize_tq2_1_cuda(x.data_ptr(), _DTYPES[x.dtype], out.data_ptr(), x.numel(), _stream(x)))
+    return out
+
+
+def dequantize_tq2_1(blocks: torch.Tensor) -> torch.Tensor:
+    """float32 (..., n_blocks * 128) from uint8 TQ2_1 blocks (..., n_blocks, 44)."""
+    _need_cuda(blocks)
+    if blocks.dtype != torch.uint8 or not blocks.is_contiguous() or blocks.dim() < 2 \
+            or blocks.shape[-1] != TQ2_1_BYTES:
+        raise ValueError("blocks must be a contiguous uint8 (..., n_blocks, 44) tensor")
+    out = torch.empty((*blocks.shape[:-2], blocks.shape[-2] * 128), dtype=torch.float32, device=blocks.device)
+    L.check(L.load().tq_dequantize_tq2_1_cuda(blocks.data_ptr(), out.data_ptr(), out.numel(), _stream(blocks)))
+    return out
+
+
 def requantize(blocks: torch.Tensor, src_qtype, dst_qtype) -> torch.Tensor:
     """Blocks of src_qtype -> blocks of dst_qtype (dequantize + quantize per block, one kernel;
     requantize_tq4_to_tq3 / tq3_to_tq2 / tq4_to_tq2 of src/ggml-tq.c:329-357)."""

@@ -69,6 +69,25 @@ def test_argument_errors(call, status):
     assert lib.tq_last_error_string()  # a message is set
 
 
+def test_tq21_argument_errors_and_layout(tmp_path):
+    """TQ2_1 entry points check k and pointers before any device work; block_tq2_1 is 44 bytes
+    with the TQ3_0 sub-block first (runs without a GPU)."""
+    lib = L.load()
+    assert lib.tq_quantize_tq2_1_cuda(16, 0, 16, 96, None) == 1          # k not a multiple of 128
+    assert lib.tq_quantize_tq2_1_cuda(16, 7, 16, 128, None) == 1         # bad dtype
+    assert lib.tq_quantize_tq2_1_cuda(None, 0, None, 128, None) == 1     # null pointers
+    assert lib.tq_quantize_tq2_1_cuda(None, 0, None, 0, None) == 0       # nothing to do
+    assert lib.tq_dequantize_tq2_1_cuda(16, 16, 130, None) == 1
+    assert lib.tq_dequantize_tq2_1_cuda(17, 16, 128, None) == 3          # blocks not 2-byte aligned
+    src = tmp_path / "b.c"
+    src.write_text('#include "leankv_tq.h"\n#include <stddef.h>\n'
+                   'int main(void){ return sizeof(block_tq2_1) != 44 || offsetof(block_tq2_1, d_n0) != 14 ||'
+                   ' offsetof(block_tq2_1, d_n2) != 34; }\n')
+    exe = tmp_path / "b"
+    subprocess.run(["gcc", "-I", L.HEADER_DIR, str(src), "-o", str(exe)], check=True)
+    assert subprocess.run([str(exe)]).returncode == 0
+
+
 def test_zero_length_is_a_noop():
     lib = L.load()
     assert lib.tq_quantize_cuda(4, None, 0, None, 0, 0, 0, None) == 0

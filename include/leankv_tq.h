@@ -274,8 +274,8 @@ tq_status tq_proto_decode_cuda(const uint8_t *indices, const float *scales, int6
  * q / out: [batch][n_q_heads][head_dim].  lse (optional): [batch][n_q_heads],
  * natural log of sum_t exp(s_t); -inf and a zero output for kv_len == 0.
  * Requirements: head_dim 128 or 256; n_q_heads / n_kv_heads in 1 .. 8;
- * kv_capacity even; cache pointers 16-byte aligned.  Block types: K TQ4_0 or
- * TQ3_0, V TQ4_0.  Work memory: tq_decode_attention_workspace_size() bytes of
+ * kv_capacity even; cache pointers 16-byte aligned.  Block types: K TQ4_0,
+ * TQ3_0 or TQ2_0 (the last tier of a TQ4 -> TQ3 -> TQ2 cache), V TQ4_0.  Work memory: tq_decode_attention_workspace_size() bytes of
  * device memory; its first int32 receives the kernel-side status (TQ_SUCCESS,
  * TQ_ERROR_TIMEOUT for a bulk copy that never completed, TQ_ERROR_UNSUPPORTED
  * for a block scale of magnitude >= 2^15) once the stream has run the call.

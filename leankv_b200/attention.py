@@ -1,7 +1,7 @@
 """Fused decode attention over packed TurboQuant K/V caches (torch front end).
 
 Cache tensors are uint8 with shape [batch, n_kv_heads, capacity, head_dim/32, bytes]
-of TQ4_0 (18-byte) or, for K, TQ3_0 (14-byte) blocks (src/ggml-tq.h:131-141);
+of TQ4_0 (18-byte) or, for K, TQ3_0 (14-byte) or TQ2_0 (10-byte) blocks (src/ggml-tq.h:125-141);
 head_dim is 128 or 256 and capacity even.  K and V hold Hadamard-rotated rows
 (quantize with fwht_head_dim=head_dim); the query is rotated inside, and the
 output rotated back, so the result is attention in the original space.
@@ -159,7 +159,7 @@ def decode_attention_paged(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
 
 
 def _btype(cache: torch.Tensor) -> int:
-    return 4 if cache.shape[-1] == 18 else 3
+    return {18: 4, 14: 3, 10: 2}.get(int(cache.shape[-1]), 0)   # 0: rejected by the argument check
 
 
 def _check_caches(q, k_cache, v_cache) -> None:

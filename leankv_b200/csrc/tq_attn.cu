@@ -144,6 +144,7 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 // relative error of at most 6.05e-5 (TQ4) and 9.75e-6 (TQ3).
 constexpr float TQ4_ALPHA = 1.5976254940032959f;
 constexpr float TQ3_ALPHA = 1.7372877597808838f;
+constexpr float TQ2_ALPHA = 1.4960941076278687f;   // TQ2 levels: worst fp16 rounding 2.7e-7 relative
 
 // hi + lo fp16 parts of two floats: hi = fp16(a), lo = fp16(a - hi)
 __device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_t& lo) {
@@ -328,7 +329,7 @@ struct AttnCfg {
     // stage-release barriers: the second warp of a pair frees a stage before the first refills it
     static constexpr int EBARS = SPLIT == 2 ? RINGS * ATT_STAGES : 0;
     static constexpr int THREADS = WARPS * 32;
-    static constexpr int KBB = KT == 4 ? TQ4_BYTES : TQ3_BYTES;   // K bytes per block
+    static constexpr int KBB = KT == 4 ? TQ4_BYTES : KT == 3 ? TQ3_BYTES : TQ2_BYTES;   // K bytes per block
     static constexpr int KB = KBB * NBLK;                          // K bytes per token
     static constexpr int VB = TQ4_BYTES * NBLK;                    // V bytes per token
     static constexpr int KTILE = ATT_TILE * KB, VTILE = ATT_TILE * VB;
@@ -379,7 +380,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
     constexpr int KBB = Cfg::KBB, KB = Cfg::KB, VB = Cfg::VB;
     constexpr int KTILE = Cfg::KTILE, STAGE = Cfg::STAGE;
     constexpr int NCH = Cfg::NCH, NMT = Cfg::NMT, SCR = Cfg::SCR;
-    static_assert(KT == 3 || KT == 4, "TQ3_0 or TQ4_0 K");
+    static_assert(KT == 2 || KT == 3 || KT == 4, "TQ2_0, TQ3_0 or TQ4_0 K");
     static_assert(D == 128 || D == 256, "head_dim 128 or 256");
 
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -415,6 +416,10 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
         if (KT == 3 && (SPLIT == 1 || k < 64))
             *reinterpret_cast<uint32_t*>(smem + (k << 8) + 128 + (l << 2)) =
                 pack_h2(TQ3_ALPHA * tq3_level(k & 7), TQ3_ALPHA * tq3_level((k >> 3) & 7));
+        // TQ2 pairs (two consecutive elements, codes c0 | c1 << 2: a nibble) in rows 0..15
+        if (KT == 2 && k < 16)
+            *reinterpret_cast<uint32_t*>(smem + (k << 8) + 128 + (l << 2)) =
+                pack_h2(TQ2_ALPHA * tq2_level(k & 3), TQ2_ALPHA * tq2_level(k >> 2));
     }
     if (lane == 0 && half == 0)
         for (int s = 0; s < ATT_STAGES; ++s) {
@@ -710,6 +715,25 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                     af[3] = lut_ld<RES>(w1, lane4, LUT_SEL1);
                     mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
                     lo_mma(acc, af, 2 * blk + 1);
+                } else if constexpr (KT == 2) {
+                    // TQ2 K: code bytes 2t, 2t+1 of the block hold elements 8t .. 8t+7, a nibble per
+                    // element pair; the low nibbles become the bytes of nl, the high ones those of nh
+                    const uint32_t kr = st + k_off;
+                    const uint32_t w0 = ld16<blk * TQ2_BYTES>(kr), w1 = ld16<blk * TQ2_BYTES + KROW8>(kr);
+                    const uint32_t nl0 = w0 & 0x0F0Fu, nh0 = (w0 >> 4) & 0x0F0Fu;
+                    const uint32_t nl1 = w1 & 0x0F0Fu, nh1 = (w1 >> 4) & 0x0F0Fu;
+                    af[0] = lut_ld<RES>(nl0, lane4x, LUT_SEL0);   // elements 8t, 8t+1 of row g
+                    af[1] = lut_ld<RES>(nl1, lane4x, LUT_SEL0);   // of row g + 8
+                    af[2] = lut_ld<RES>(nh0, lane4x, LUT_SEL0);   // elements 8t+2, 8t+3
+                    af[3] = lut_ld<RES>(nh1, lane4x, LUT_SEL0);
+                    mma16816_zc(acc, af, qf[2 * blk][0], qf[2 * blk][1]);
+                    lo_mma(acc, af, 2 * blk);
+                    af[0] = lut_ld<RES>(nl0, lane4x, LUT_SEL1);   // elements 8t+4, 8t+5
+                    af[1] = lut_ld<RES>(nl1, lane4x, LUT_SEL1);
+                    af[2] = lut_ld<RES>(nh0, lane4x, LUT_SEL1);   // elements 8t+6, 8t+7
+                    af[3] = lut_ld<RES>(nh1, lane4x, LUT_SEL1);
+                    mma16816(acc, af, qf[2 * blk + 1][0], qf[2 * blk + 1][1]);
+                    lo_mma(acc, af, 2 * blk + 1);
                 } else {
                     constexpr int IMM = blk * TQ3_BYTES - 2 * (blk & 1);
                     const uint32_t kr = st + ((blk & 1) ? k3_off_o : k3_off_e);
@@ -773,7 +797,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 const uint32_t wac = prmt(w0, w2, 0x5410u), wbd = prmt(w1, w3, 0x5410u);
                 const uint32_t nlo = (wac & 0x0F0F0F0Fu) | ((wbd << 4) & 0xF0F0F0F0u);
                 const uint32_t nhi = ((wac >> 4) & 0x0F0F0F0Fu) | (wbd & 0xF0F0F0F0u);
-                // TQ4 K: one 128-bit load per block pair; TQ3 K (more live offsets) one 64-bit load per block
+                // TQ4 / TQ2 K: one 128-bit load per block pair; TQ3 K (more live offsets) one 64-bit load per block
                 if constexpr (KT == 3) {
                     const uint2 d2 = ld64u<blk * 8>(sdv);
                     dvw.x = d2.x;
@@ -781,7 +805,7 @@ __global__ void __launch_bounds__(att_warps(D) * 32, 1) attn_decode_kernel(const
                 } else if constexpr ((blk & 1) == 0) {
                     dvw = ld128u<blk * 8>(sdv);
                 }
-                const bool hi = KT == 4 && (blk & 1);
+                const bool hi = KT != 3 && (blk & 1);
                 const uint32_t b0 = h2_mul(pb01, hi ? dvw.z : dvw.x);
                 const uint32_t b1 = h2_mul(pb23, hi ? dvw.w : dvw.y);
                 uint32_t af[4];
@@ -1163,10 +1187,12 @@ static cudaError_t launch_decode_kernel(const AttnKernelArgs& a, int grid, cudaS
 template <int D, int RES, bool PG>
 static cudaError_t launch_decode_kt(const AttnKernelArgs& a, int k_type, int grid, cudaStream_t st) {
     if (a.grp <= 4)
-        return k_type == 4 ? launch_decode_kernel<D, 4, RES, true, PG>(a, grid, st)
-                           : launch_decode_kernel<D, 3, RES, true, PG>(a, grid, st);
-    return k_type == 4 ? launch_decode_kernel<D, 4, RES, false, PG>(a, grid, st)
-                       : launch_decode_kernel<D, 3, RES, false, PG>(a, grid, st);
+        return k_type == 4   ? launch_decode_kernel<D, 4, RES, true, PG>(a, grid, st)
+               : k_type == 3 ? launch_decode_kernel<D, 3, RES, true, PG>(a, grid, st)
+                             : launch_decode_kernel<D, 2, RES, true, PG>(a, grid, st);
+    return k_type == 4   ? launch_decode_kernel<D, 4, RES, false, PG>(a, grid, st)
+           : k_type == 3 ? launch_decode_kernel<D, 3, RES, false, PG>(a, grid, st)
+                         : launch_decode_kernel<D, 2, RES, false, PG>(a, grid, st);
 }
 
 template <int D>
@@ -1191,7 +1217,8 @@ static cudaError_t run_decode(const AttnRun& r, const AttnPlan& p, uint8_t* ws, 
     // q~ = FWHT(q) / sqrt(D) * sm_scale * log2(e): the FWHT normalisation folds into the scale
     // K codebook tables hold alpha * level (alpha chosen for the fp16 rounding of the levels): 1/alpha
     // joins the query scale
-    a.qscale = r.sm_scale * LOG2E * (r.rotate_q ? fwht_norm(D) : 1.0f) / (r.k_type == 4 ? TQ4_ALPHA : TQ3_ALPHA);
+    a.qscale = r.sm_scale * LOG2E * (r.rotate_q ? fwht_norm(D) : 1.0f) /
+               (r.k_type == 4 ? TQ4_ALPHA : r.k_type == 3 ? TQ3_ALPHA : TQ2_ALPHA);
     a.onorm = fwht_norm(D);
     a.B = r.B;
     a.Hq = r.Hq;
@@ -1210,7 +1237,7 @@ static cudaError_t run_decode(const AttnRun& r, const AttnPlan& p, uint8_t* ws, 
     a.page_mask = (1u << r.page_shift) - 1u;
     {
         const uint32_t rows = (uint32_t)r.Hkv << r.page_shift;
-        const uint32_t kbb = r.k_type == 4 ? TQ4_BYTES : TQ3_BYTES;
+        const uint32_t kbb = r.k_type == 4 ? TQ4_BYTES : r.k_type == 3 ? TQ3_BYTES : TQ2_BYTES;
         a.page_kbytes = rows * (uint32_t)(D / 32) * kbb;
         a.page_vbytes = rows * (uint32_t)(D / 32) * TQ4_BYTES;
     }
@@ -1222,7 +1249,7 @@ static cudaError_t run_decode(const AttnRun& r, const AttnPlan& p, uint8_t* ws, 
 }
 
 cudaError_t launch_decode_attention(const AttnRun& r, const AttnPlan& p, void* workspace, cudaStream_t st) {
-    if (r.v_type != 4 || (r.k_type != 3 && r.k_type != 4)) return cudaErrorInvalidValue;
+    if (r.v_type != 4 || r.k_type < 2 || r.k_type > 4) return cudaErrorInvalidValue;
     if (r.D == 128) return run_decode<128>(r, p, (uint8_t*)workspace, st);
     if (r.D == 256) return run_decode<256>(r, p, (uint8_t*)workspace, st);
     return cudaErrorInvalidValue;

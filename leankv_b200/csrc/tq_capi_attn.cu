@@ -18,8 +18,9 @@ tq_status tq::attn_check(const tq_decode_attention_args* a, AttnRun* r, AttnPlan
     if (grp > 8) return set_error(TQ_ERROR_UNSUPPORTED, "GQA group size %d (supported: 1 .. 8)", grp);
     if (a->head_dim != 128 && a->head_dim != 256)
         return set_error(TQ_ERROR_UNSUPPORTED, "head_dim %d (supported: 128, 256)", a->head_dim);
-    if ((a->k_type != TQ_TYPE_TQ4_0 && a->k_type != TQ_TYPE_TQ3_0) || a->v_type != TQ_TYPE_TQ4_0)
-        return set_error(TQ_ERROR_UNSUPPORTED, "block types K=%d V=%d (supported: K TQ4_0 or TQ3_0, V TQ4_0)",
+    if ((a->k_type != TQ_TYPE_TQ4_0 && a->k_type != TQ_TYPE_TQ3_0 && a->k_type != TQ_TYPE_TQ2_0) ||
+        a->v_type != TQ_TYPE_TQ4_0)
+        return set_error(TQ_ERROR_UNSUPPORTED, "block types K=%d V=%d (supported: K TQ4_0, TQ3_0 or TQ2_0, V TQ4_0)",
                          (int)a->k_type, (int)a->v_type);
     if (!dtype_ok(a->q_dtype) || !dtype_ok(a->out_dtype)) return set_error(TQ_ERROR_INVALID_VALUE, "bad dtype");
     if (a->kv_capacity < 0 || (a->kv_capacity & 1)) return set_error(TQ_ERROR_INVALID_VALUE, "kv_capacity must be even");

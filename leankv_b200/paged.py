@@ -127,8 +127,8 @@ class PagedKVCache:
         import torch
         if head_dim not in (128, 256):
             raise ValueError("head_dim must be 128 or 256 (fused decode attention)")
-        if k_bits not in (3, 4):
-            raise ValueError("keys are TQ3_0 or TQ4_0")
+        if k_bits not in (2, 3, 4):
+            raise ValueError("keys are TQ2_0, TQ3_0 or TQ4_0")
         if k_opt_passes and k_bits != 3:
             raise ValueError("optimal rounding applies to TQ3_0 keys")
         max_pages_per_seq = max_pages_per_seq or num_pages
@@ -136,7 +136,7 @@ class PagedKVCache:
         self.n_layers, self.n_kv_heads, self.head_dim = n_layers, n_kv_heads, head_dim
         self.k_bits, self.k_opt_passes = k_bits, k_opt_passes
         self.device = torch.device(device)
-        kb = 14 if k_bits == 3 else 18
+        kb = {2: 10, 3: 14, 4: 18}[k_bits]
         shape = (num_pages, n_kv_heads, page_size, head_dim // 32)
         self.k = [torch.zeros(shape + (kb,), dtype=torch.uint8, device=self.device) for _ in range(n_layers)]
         self.v = [torch.zeros(shape + (18,), dtype=torch.uint8, device=self.device) for _ in range(n_layers)]

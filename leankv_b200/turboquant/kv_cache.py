@@ -103,7 +103,7 @@ class _BlockStore:
         if self.len + n > self.cap:
             cap = max(2 * self.cap, self.len + n, 16)
             cap += cap & 1
-            kb = 18 if self.k_type == 4 else 14
+            kb = {2: 10, 3: 14, 4: 18}[self.k_type]
             knew = torch.empty(B, H, cap, D // 32, kb, dtype=torch.uint8, device=k.device)
             vnew = torch.empty(B, H, cap, D // 32, 18, dtype=torch.uint8, device=k.device)
             if self.len:
@@ -173,8 +173,8 @@ class LeanKVCache:
         if storage in ("tq_blocks", "tq_pages"):
             if head_dim not in (128, 256):
                 raise ValueError(f"{storage} storage needs head_dim 128 or 256 (fused decode attention)")
-            if k_bits not in (3, 4) or v_bits != 4:
-                raise ValueError(f"{storage} storage holds TQ3_0 or TQ4_0 keys and TQ4_0 values")
+            if k_bits not in (2, 3, 4) or v_bits != 4:
+                raise ValueError(f"{storage} storage holds TQ2_0, TQ3_0 or TQ4_0 keys and TQ4_0 values")
             if k_opt_passes and k_bits != 3:
                 raise ValueError("optimal rounding applies to TQ3_0 keys")
             if not str(device).startswith("cuda"):
@@ -300,7 +300,7 @@ class LeanKVCache:
 
     def memory_summary(self) -> dict:
         if self.storage in ("tq_blocks", "tq_pages"):
-            k_bits = (18 if self.k_bits == 4 else 14) * 8 / 32
+            k_bits = {2: 10, 3: 14, 4: 18}[self.k_bits] * 8 / 32
             v_bits = 18 * 8 / 32
         else:
             k_bits = self.k_quantizer.memory_bits_per_element()

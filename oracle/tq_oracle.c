@@ -25,6 +25,7 @@ const float ORC_TQ3_BOUNDS[7] = {
     -0.8122602f, -0.4879221f, -0.2326114f, +0.0000000f,
     +0.2326114f, +0.4879221f, +0.8122602f,
 };
+const float ORC_TQ2_LEVELS[4] = {-1.0000000f, -0.2997714f, +0.2997714f, +1.0000000f};
 const float ORC_TQ4_LEVELS[16] = {
     -1.0000000f, -0.7573038f, -0.5923403f, -0.4599576f,
     -0.3450764f, -0.2405254f, -0.1421261f, -0.0470277f,
@@ -180,6 +181,19 @@ void orc_tq3_dequantize(const uint8_t *blocks, float *y, int64_t k) {
     }
 }
 
+/* ── TQ2_0 decode: src/ggml-tq.c:191-207 ───────────────────────────────
+ * Byte i of the codes holds elements 4i .. 4i+3, two bits each from the low end
+ * (the unpack of src/ggml-tq.c:70-77); y = level * d. */
+void orc_tq2_dequantize(const uint8_t *blocks, float *y, int64_t k) {
+    const int64_t nb = k / ORC_QK;
+    for (int64_t i = 0; i < nb; ++i) {
+        const uint8_t *src = blocks + ORC_TQ2_BYTES * i;
+        const float d = orc_float_from_half(get_half(src));
+        for (int b = 0; b < 8; ++b)
+            for (int e = 0; e < 4; ++e) y[ORC_QK * i + 4 * b + e] = ORC_TQ2_LEVELS[(src[2 + b] >> (2 * e)) & 3] * d;
+    }
+}
+
 /* ── TQ4_0: src/ggml-tq.c:273-321 ───────────────────────────────────── */
 
 void orc_tq4_quantize(const float *x, uint8_t *blocks, int64_t k) {
@@ -318,6 +332,7 @@ void orc_tq3_quantize_opt2_row(const void *x, void *blocks, int64_t k) {
 
 static void dequant_row(const uint8_t *blocks, int type, float *y, int D) {
     if (type == 3) orc_tq3_dequantize(blocks, y, D);
+    else if (type == 2) orc_tq2_dequantize(blocks, y, D);
     else orc_tq4_dequantize(blocks, y, D);
 }
 
@@ -349,7 +364,7 @@ typedef struct {
 static void attn_pair(const attn_job *J, int b, int g) {
     const int D = J->D, grp = J->Hq / J->Hkv;
     const int64_t n = J->kv_len ? J->kv_len[b] : J->T;
-    const int kbytes = (J->k_type == 3 ? ORC_TQ3_BYTES : ORC_TQ4_BYTES) * (D / ORC_QK);
+    const int kbytes = (J->k_type == 3 ? ORC_TQ3_BYTES : J->k_type == 2 ? ORC_TQ2_BYTES : ORC_TQ4_BYTES) * (D / ORC_QK);
     const int vbytes = (J->v_type == 3 ? ORC_TQ3_BYTES : ORC_TQ4_BYTES) * (D / ORC_QK);
     const uint8_t *kbase = J->k + ((int64_t)b * J->Hkv + g) * J->T * kbytes;
     const uint8_t *vbase = J->v + ((int64_t)b * J->Hkv + g) * J->T * vbytes;

@@ -33,16 +33,22 @@ extern "C" {
 #define ORC_QK 32
 #define ORC_TQ4_BYTES 18
 #define ORC_TQ3_BYTES 14
+#define ORC_TQ2_BYTES 10
 
 /* codebooks restated from src/ggml-tq.h:98-121 (float32, ±1 outer levels) */
 extern const float ORC_TQ3_LEVELS[8];
 extern const float ORC_TQ3_BOUNDS[7];
 extern const float ORC_TQ4_LEVELS[16];
 extern const float ORC_TQ4_BOUNDS[15];
+/* TQ2 levels, src/ggml-tq.h:89-91 */
+extern const float ORC_TQ2_LEVELS[4];
 
 /* fp16 codec of the standalone build: src/ggml-tq.h:39-64 */
 uint16_t orc_half_from_float(float f);
 float    orc_float_from_half(uint16_t h);
+
+/* TQ2_0 decode: dequantize_row_tq2_0, src/ggml-tq.c:191-207 (2-bit unpack :70-77) */
+void orc_tq2_dequantize(const uint8_t *blocks, float *y, int64_t k);
 
 /* Walsh-Hadamard transform: src/ggml-tq.c:361-381 and :398-404 */
 void orc_fwht(float *x, int d);

@@ -225,6 +225,38 @@ def test_attention_head_dim_256(orc, kt, T, lens):
     print(f"D256 K TQ{kt} T {T}: rel err {rel:.3g}")
 
 
+@pytest.mark.parametrize("D,grp", [(128, 1), (128, 3), (128, 4), (128, 8), (256, 4), (256, 8)])
+def test_attention_tq2_k_vs_oracle(orc, D, grp):
+    """TQ2_0 K / TQ4_0 V caches (keys in the last tier of a TQ4 -> TQ3 -> TQ2 cache), ragged
+    lengths, both query rotations at head_dim 256."""
+    B, Hkv, T = 2, 2, 700
+    kc = make_cache(B, Hkv, T, D, 140 + grp + D, qtype=2)
+    vc = make_cache(B, Hkv, T, D, 150 + grp + D)
+    q = torch.randn(B, Hkv * grp, D, generator=torch.Generator().manual_seed(160 + grp + D)).to(torch.float16)
+    lens = torch.tensor([T, 251], dtype=torch.int32)
+    for rotate in ((True, False) if D == 256 else (True,)):
+        out, lse = attention.decode_attention(q.to(DEV), kc, vc, kv_len=lens.to(DEV), return_lse=True,
+                                              rotate_q=rotate)
+        ref, lref = orc.decode_attention(q.float().numpy(), kc.cpu().numpy(), 2, vc.cpu().numpy(), 4, Hkv,
+                                         kv_len=lens.numpy(), rotate_q=rotate, nthreads=8)
+        rel = check(out.cpu().numpy(), ref, lse.cpu().numpy(), lref)
+        print(f"TQ2 K D {D} grp {grp} rotate {rotate}: rel err {rel:.3g}")
+
+
+def test_attention_tq2_k_tiered_cache_equals_requantized(orc):
+    """A key cache moved down the tiers on the GPU (TQ4 -> TQ2 with the requantize kernel) is
+    attended directly: equal to the oracle over the same TQ2 blocks."""
+    from leankv_b200 import ops
+    B, Hkv, T, D, grp = 2, 2, 512, 128, 4
+    k4 = make_cache(B, Hkv, T, D, 170, qtype=4)
+    kc = ops.requantize(k4, 4, 2).view(B, Hkv, T, D // 32, 10)
+    vc = make_cache(B, Hkv, T, D, 171)
+    q = torch.randn(B, Hkv * grp, D, generator=torch.Generator().manual_seed(172)).to(torch.float16)
+    out = attention.decode_attention(q.to(DEV), kc, vc)
+    ref, _ = orc.decode_attention(q.float().numpy(), kc.cpu().numpy(), 2, vc.cpu().numpy(), 4, Hkv, nthreads=8)
+    check(out.cpu().numpy(), ref)
+
+
 @pytest.mark.parametrize("grp", [1, 2, 3, 8])
 @pytest.mark.parametrize("kt", [4, 3])
 def test_attention_head_dim_256_grp(orc, kt, grp):

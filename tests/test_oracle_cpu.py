@@ -179,3 +179,16 @@ def test_lse_combine_oracle(orc):
     w = np.exp(lse - lse.max(0))
     np.testing.assert_allclose(out, (w[..., None] * o).sum(0) / w.sum(0)[..., None], rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(lo, lse.max(0) + np.log(w.sum(0)), rtol=1e-6)
+
+
+def test_tq2_dequantize_restatement_equals_reference(orc):
+    """The restated TQ2_0 decoder (the decode attention's TQ2 keys) equals the reference
+    dequantize_row_tq2_0 on random block bytes, every scale bit pattern included."""
+    rng = np.random.default_rng(22)
+    blocks = rng.integers(0, 256, size=(20000, 10), dtype=np.uint8)
+    blocks[:, :2] = rng.integers(0, 256, size=(20000, 2), dtype=np.uint8)
+    y = orc.dequantize(2, blocks)
+    ref = orc.ref_dequantize(2, blocks)
+    assert np.array_equal(np.isnan(y), np.isnan(ref))
+    fin = ~np.isnan(ref)
+    assert np.array_equal(y[fin], ref[fin])
